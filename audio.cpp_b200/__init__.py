@@ -1,0 +1,212 @@
+"""Python host layer over libb200diff.so (the sm_100a diffusion hot-path library).
+
+Mirrors the reference's entry points for this path:
+  * ``VibeVoiceDiffusionHead``   ~ VibeVoiceDiffusionHeadWeightsRuntime + sample_vibevoice_speech_latents
+    (include/engine/models/vibevoice/diffusion_head.h:58-97, diffusion_sampler.h:23-26)
+  * ``vv_schedule``              ~ VibeVoiceDPMSolverScheduler timesteps / step coefficients
+Everything runs through the C ABI declared in include/b200diff.h.  There is no
+CPU fallback: if the library or a B200 is missing the calls raise.
+
+This directory name contains a dot, so load it by path, e.g.
+``importlib.util.spec_from_file_location("audiocpp_b200", ".../audio.cpp_b200/__init__.py")``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Dict, Iterable, Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libb200diff.so")
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_BF16 = 0, 1, 8, 30
+EPI_F32, EPI_CT, EPI_SWIGLU, EPI_RESID = 0, 1, 2, 3
+
+STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "ENONFINITE", -6: "ETIMEOUT",
+          -7: "ENODEV"}
+
+EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
+            "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
+            "b2d_gemm"]
+
+
+class B2DError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__("%s (%s)" % (message, STATUS.get(status, status)))
+        self.status = status
+
+
+class TensorView(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("ggml_type", C.c_int32), ("ndim", C.c_int32), ("dims", C.c_int64 * 4),
+                ("data", C.c_void_p), ("nbytes", C.c_size_t)]
+
+
+class HeadConfig(C.Structure):
+    _fields_ = [("hidden_size", C.c_int64), ("latent_size", C.c_int64), ("head_layers", C.c_int64),
+                ("head_ffn_ratio", C.c_float), ("rms_norm_eps", C.c_float), ("ddpm_num_steps", C.c_int64)]
+
+
+class VvStep(C.Structure):
+    _fields_ = [("timestep", C.c_int64), ("sigma", C.c_float), ("sigma_next", C.c_float), ("alpha_s", C.c_float),
+                ("sigma_s", C.c_float), ("sample_coeff", C.c_float), ("d0_coeff", C.c_float),
+                ("inv_r0", C.c_float), ("order", C.c_int32)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads the in-tree library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("libb200diff.so is not built; run python audio.cpp_b200/build.py")
+        L = C.CDLL(LIB_PATH)
+        P, I64, F, I32 = C.c_void_p, C.c_int64, C.c_float, C.c_int32
+        L.b2d_create.argtypes = [C.c_int, C.POINTER(P)]
+        L.b2d_destroy.argtypes = [P]
+        L.b2d_destroy.restype = None
+        L.b2d_last_error.argtypes = [P]
+        L.b2d_last_error.restype = C.c_char_p
+        L.b2d_version.restype = C.c_char_p
+        L.b2d_sync.argtypes = [P, P]
+        L.b2d_vv_schedule.argtypes = [I64, I64, C.POINTER(VvStep)]
+        L.b2d_vv_head_load.argtypes = [P, C.POINTER(HeadConfig), C.POINTER(TensorView), I32]
+        L.b2d_vv_predict.argtypes = [P, P, I64, I64, F, P, I64, P, P]
+        L.b2d_vv_sample.argtypes = [P, P, P, P, I64, I64, F, P, P]
+        L.b2d_vv_sample_device.argtypes = [P, P, P, P, I64, I64, F, P, P]
+        L.b2d_q8_0_dequantize.argtypes = [P, P, I64, I64, P, P]
+        L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
+        _lib = L
+    return _lib
+
+
+def version() -> str:
+    return lib().b2d_version().decode()
+
+
+def vv_schedule(ddpm_num_steps: int, steps: int) -> Sequence[VvStep]:
+    """VibeVoiceDPMSolverScheduler(ddpm_num_steps).set_timesteps(steps) tables + step coefficients (host only)."""
+    out = (VvStep * steps)()
+    st = lib().b2d_vv_schedule(ddpm_num_steps, steps, out)
+    if st != 0:
+        raise B2DError(st, "VibeVoice scheduler requires positive timestep counts")
+    return list(out)
+
+
+def _ptr(a) -> int:
+    """Host numpy array or torch tensor (host or device) -> raw address."""
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class Context:
+    """One device context (b2d_ctx).  Not thread-safe; one per GPU."""
+
+    def __init__(self, device: int = 0):
+        self._h = C.c_void_p()
+        st = lib().b2d_create(device, C.byref(self._h))
+        if st != 0:
+            raise B2DError(st, "b2d_create(%d) failed: no usable sm_100 device" % device)
+        self.device = device
+
+    def close(self) -> None:
+        if self._h:
+            lib().b2d_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, status: int) -> None:
+        if status != 0:
+            raise B2DError(status, lib().b2d_last_error(self._h).decode())
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    def sync(self, stream: int = 0) -> None:
+        self.check(lib().b2d_sync(self._h, C.c_void_p(stream)))
+
+    # ---------------------------------------------------------- kernel entries
+    def q8_0_dequantize(self, q8_dev: int, rows: int, k: int, out_dev: int, stream: int = 0) -> None:
+        self.check(lib().b2d_q8_0_dequantize(self._h, C.c_void_p(q8_dev), rows, k, C.c_void_p(out_dev),
+                                             C.c_void_p(stream)))
+
+    def gemm(self, a_dev: int, b_dev: int, m: int, n: int, k: int, *, bf16: bool = False, epilogue: int = EPI_F32,
+             bn: int = 256, bias: int = 0, out: int = 0, ldo: int = 0, resid: int = 0, ldr: int = 0, gate: int = 0,
+             ldg: int = 0, stream: int = 0) -> None:
+        self.check(lib().b2d_gemm(self._h, int(bf16), C.c_void_p(a_dev), C.c_void_p(b_dev), m, n, k, epilogue, bn,
+                                  C.c_void_p(bias or None), C.c_void_p(out or None), ldo, C.c_void_p(resid or None),
+                                  ldr, C.c_void_p(gate or None), ldg, C.c_void_p(stream)))
+
+
+WeightSpec = Tuple[str, int, Tuple[int, ...], np.ndarray]  # (name, ggml type, dims, raw payload)
+
+
+class VibeVoiceDiffusionHead:
+    """VibeVoiceDiffusionHeadWeightsRuntime on a B200 context.
+
+    ``weights`` is an iterable of (name, ggml_type, dims, payload) with the GGUF
+    tensor names ``model.prediction_head.*`` and raw stored bytes.
+    """
+
+    def __init__(self, ctx: Context, hidden_size: int, head_layers: int = 4, head_ffn_ratio: float = 3.0,
+                 latent_size: int = 64, rms_norm_eps: float = 1e-5, ddpm_num_steps: int = 1000,
+                 weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.hidden_size, self.latent_size = hidden_size, latent_size
+        self.ddpm_num_steps = ddpm_num_steps
+        cfg = HeadConfig(hidden_size, latent_size, head_layers, head_ffn_ratio, rms_norm_eps, ddpm_num_steps)
+        specs = list(weights)
+        views = (TensorView * len(specs))()
+        keep = []
+        for i, (name, gtype, dims, payload) in enumerate(specs):
+            payload = np.ascontiguousarray(payload)
+            keep.append(payload)
+            nb = name.encode()
+            keep.append(nb)
+            views[i].name = nb
+            views[i].ggml_type = gtype
+            views[i].ndim = len(dims)
+            for j, d in enumerate(dims):
+                views[i].dims[j] = d
+            views[i].data = payload.ctypes.data
+            views[i].nbytes = payload.nbytes
+        ctx.check(lib().b2d_vv_head_load(ctx.handle, C.byref(cfg), views, len(specs)))
+
+    def predict(self, noisy: np.ndarray, timestep: float, condition: np.ndarray) -> np.ndarray:
+        noisy = np.ascontiguousarray(noisy, np.float32)
+        condition = np.ascontiguousarray(condition, np.float32)
+        frames = noisy.shape[0]
+        out = np.empty((frames, self.latent_size), np.float32)
+        self.ctx.check(lib().b2d_vv_predict(self.ctx.handle, _ptr(noisy), frames, noisy.shape[1], float(timestep),
+                                            _ptr(condition), condition.shape[1], _ptr(out), None))
+        return out
+
+    def sample(self, positive_condition, negative_condition, initial_speech, steps: int, cfg: float,
+               out=None, stream: int = 0):
+        """Host buffers (numpy or pinned torch CPU tensors) -> latents [B, latent] (sync)."""
+        batch = positive_condition.shape[0]
+        if out is None:
+            out = np.empty((batch, self.latent_size), np.float32)
+        self.ctx.check(lib().b2d_vv_sample(self.ctx.handle, _ptr(positive_condition), _ptr(negative_condition),
+                                           _ptr(initial_speech), batch, steps, float(cfg), _ptr(out),
+                                           C.c_void_p(stream)))
+        return out
+
+    def sample_device(self, positive_condition, negative_condition, initial_speech, steps: int, cfg: float, out,
+                      stream: int = 0):
+        """Device tensors (torch CUDA) -> out (device), asynchronous on `stream`."""
+        batch = positive_condition.shape[0]
+        self.ctx.check(lib().b2d_vv_sample_device(self.ctx.handle, _ptr(positive_condition),
+                                                  _ptr(negative_condition), _ptr(initial_speech), batch, steps,
+                                                  float(cfg), _ptr(out), C.c_void_p(stream)))
+        return out

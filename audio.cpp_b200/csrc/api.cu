@@ -1,0 +1,760 @@
+// C ABI implementation (include/b200diff.h): device context, weight upload,
+// the VibeVoice diffusion-head runtime and its graph-captured sampling loop,
+// plus kernel-level entry points used by the parity tests.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/b200diff.h"
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+using namespace b2d;
+
+namespace {
+
+// ------------------------------------------------------------ error plumbing
+struct Fail {
+    b2d_status code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(b2d_status code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    throw Fail{code, buf};
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) fail(B2D_ECUDA, "%s failed: %s", #call, cudaGetErrorString(e_));    \
+    } while (0)
+
+// ----------------------------------------------------------- device buffers
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    explicit DevBuf(size_t n) { alloc(n); }
+    void alloc(size_t n) {
+        release();
+        if (n == 0) return;
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            cudaGetLastError();
+            fail(B2D_ENOMEM, "device allocation of %zu bytes failed: %s", n, cudaGetErrorString(e));
+        }
+        bytes = n;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    ~DevBuf() { release(); }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) {
+        o.p = nullptr;
+        o.bytes = 0;
+    }
+    template <typename T>
+    T* as() const { return static_cast<T*>(p); }
+};
+
+// ---------------------------------------------------------- TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) fail(B2D_ECUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2-D K-major operand [rows, k] of 16-bit elements, boxes of 64 (K) x box_rows, 128B swizzle.
+CUtensorMap make_tmap(const void* base, bool bf16, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    if (reinterpret_cast<uintptr_t>(base) % 16) fail(B2D_EINVAL, "GEMM operand is not 16-byte aligned");
+    if (k % 64) fail(B2D_EINVAL, "GEMM K (%llu) must be a multiple of 64", (unsigned long long)k);
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {k, rows};
+    const cuuint64_t strides[1] = {k * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(B2D_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return m;
+}
+
+// ------------------------------------------------------------ GEMM launcher
+template <int BN, int EPI, typename CT>
+void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K, const EpiParams& ep,
+                   int num_sms, cudaStream_t st) {
+    using S = GemmShape<BN>;
+    static bool configured = false;  // per instantiation; attribute is per device-function
+    if (!configured) {
+        CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(S::SMEM_BYTES)));
+        configured = true;
+    }
+    const int64_t tiles = ((M + 127) / 128) * (N / BN);
+    if (tiles == 0) return;
+    const int grid = int(tiles < num_sms ? tiles : num_sms);
+    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, int(M), int(N), int(K), ep);
+    CK(cudaGetLastError());
+}
+
+template <typename CT>
+void launch_gemm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K,
+                 const EpiParams& ep, int num_sms, cudaStream_t st) {
+    if (N % bn) fail(B2D_EINVAL, "GEMM N (%lld) must be a multiple of the tile width %d", (long long)N, bn);
+#define B2D_G(BNv, EPIv)                                                  \
+    if (bn == BNv && epi == EPIv) {                                      \
+        launch_gemm_t<BNv, EPIv, CT>(ta, tb, M, N, K, ep, num_sms, st); \
+        return;                                                          \
+    }
+    B2D_G(256, EPI_F32) B2D_G(256, EPI_CT) B2D_G(256, EPI_SWIGLU) B2D_G(256, EPI_RESID)
+    B2D_G(128, EPI_F32) B2D_G(128, EPI_CT) B2D_G(128, EPI_RESID)
+    B2D_G(64, EPI_F32) B2D_G(64, EPI_CT) B2D_G(64, EPI_RESID)
+#undef B2D_G
+    fail(B2D_EINVAL, "unsupported GEMM tile %d / epilogue %d", bn, epi);
+}
+
+int grid_for(int64_t n, int threads, int num_sms) {
+    int64_t g = (n + threads - 1) / threads;
+    const int64_t cap = int64_t(num_sms) * 8;
+    if (g > cap) g = cap;
+    return int(g < 1 ? 1 : g);
+}
+
+// ------------------------------------------------------------------ weights
+struct HostTensor {
+    const b2d_tensor_view* v = nullptr;
+};
+
+const b2d_tensor_view* find_tensor(const b2d_tensor_view* ts, int n, const std::string& name) {
+    for (int i = 0; i < n; ++i)
+        if (ts[i].name && name == ts[i].name) return &ts[i];
+    return nullptr;
+}
+
+size_t type_row_bytes(int type, int64_t k) {
+    switch (type) {
+        case B2D_TYPE_F32: return size_t(k) * 4;
+        case B2D_TYPE_F16:
+        case B2D_TYPE_BF16: return size_t(k) * 2;
+        case B2D_TYPE_Q8_0: return size_t(k / 32) * 34;
+        default: return 0;
+    }
+}
+
+// Uploads a [rows, k] weight (any supported encoding) into `dst` (ct, leading dim k) with a row map.
+template <typename CT>
+void upload_weight(const b2d_tensor_view* t, int64_t rows, int64_t k, CT* dst, RowMap map, int num_sms,
+                   cudaStream_t st) {
+    int64_t elems = 1;
+    for (int i = 0; i < t->ndim; ++i) elems *= t->dims[i];
+    if (t->dims[0] != rows || elems != rows * k) fail(B2D_EINVAL, "tensor shape mismatch for %s", t->name);
+    if (t->ggml_type == B2D_TYPE_Q8_0 && k % 32) fail(B2D_EINVAL, "Q8_0 row not divisible by 32: %s", t->name);
+    const size_t need = type_row_bytes(t->ggml_type, k) * size_t(rows);
+    if (need == 0) fail(B2D_EINVAL, "unsupported tensor type %d for %s", t->ggml_type, t->name);
+    if (t->nbytes != need) fail(B2D_EINVAL, "tensor byte size mismatch for %s", t->name);
+    DevBuf staging(need);
+    CK(cudaMemcpyAsync(staging.p, t->data, need, cudaMemcpyHostToDevice, st));
+    const int grid = grid_for(rows * k, 256, num_sms);
+    switch (t->ggml_type) {
+        case B2D_TYPE_Q8_0:
+            dequant_q8_0_kernel<CT><<<grid_for(rows * k / 32, 256, num_sms), 256, 0, st>>>(staging.as<uint8_t>(), rows,
+                                                                                          k, dst, k, map);
+            break;
+        case B2D_TYPE_F16:
+            convert_rows_kernel<__half, CT><<<grid, 256, 0, st>>>(staging.as<__half>(), rows, k, dst, k, map);
+            break;
+        case B2D_TYPE_BF16:
+            convert_rows_kernel<__nv_bfloat16, CT><<<grid, 256, 0, st>>>(staging.as<__nv_bfloat16>(), rows, k, dst, k,
+                                                                         map);
+            break;
+        default:
+            convert_rows_kernel<float, CT><<<grid, 256, 0, st>>>(staging.as<float>(), rows, k, dst, k, map);
+            break;
+    }
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(st));
+}
+
+std::vector<float> host_f32(const b2d_tensor_view* t, int64_t n) {
+    if (!t) fail(B2D_EINVAL, "missing f32 tensor");
+    std::vector<float> v(static_cast<size_t>(n));
+    if (t->ggml_type == B2D_TYPE_F32 && t->nbytes == size_t(n) * 4) {
+        std::memcpy(v.data(), t->data, size_t(n) * 4);
+    } else if (t->ggml_type == B2D_TYPE_F16 && t->nbytes == size_t(n) * 2) {
+        const uint16_t* h = static_cast<const uint16_t*>(t->data);
+        for (int64_t i = 0; i < n; ++i) {
+            __half_raw r;
+            r.x = h[i];
+            v[size_t(i)] = __half2float(__half(r));
+        }
+    } else if (t->ggml_type == B2D_TYPE_BF16 && t->nbytes == size_t(n) * 2) {
+        const uint16_t* h = static_cast<const uint16_t*>(t->data);
+        for (int64_t i = 0; i < n; ++i) {
+            uint32_t u = uint32_t(h[i]) << 16;
+            std::memcpy(&v[size_t(i)], &u, 4);
+        }
+    } else {
+        fail(B2D_EINVAL, "tensor byte size mismatch for %s", t->name);
+    }
+    return v;
+}
+
+// ------------------------------------------------------------- VibeVoice head
+constexpr int kHeadLatent = 64;
+
+struct HeadWorkspace {
+    int64_t batch = 0;  // B; GEMM rows = 2B
+    DevBuf x, cp, sc, ada, h, ffn, v, noisy, cond, cond_ct, init, xstate, hist0, hist1, out, temb, h1, tsteps, coefs, ptstep;
+    CUtensorMap tm_noisy, tm_cond, tm_sc, tm_h, tm_ffn;
+    std::map<std::tuple<int64_t, uint32_t>, cudaGraphExec_t> graphs;  // (steps, cfg bits) -> graph
+    ~HeadWorkspace() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    }
+};
+
+struct HeadModel {
+    b2d_vv_head_config cfg{};
+    int64_t H = 0, F = 0, NADA = 0;
+    bool bf16 = false;
+    DevBuf w_in, w_cond, w_t1, w_t2, w_ada, w_final, norms;
+    std::vector<DevBuf> w_gu, w_down;
+    CUtensorMap tm_in, tm_cond, tm_ada, tm_final;
+    std::vector<CUtensorMap> tm_gu, tm_down;
+    std::unique_ptr<HeadWorkspace> ws;
+};
+
+}  // namespace
+
+struct b2d_ctx {
+    int device = 0;
+    int num_sms = 148;
+    std::string err;
+    DevBuf status;  // int device-side status word
+    cudaStream_t load_stream = nullptr;
+    std::unique_ptr<HeadModel> head;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+template <typename F>
+b2d_status guarded(b2d_ctx* ctx, F&& f) {
+    if (!ctx) return B2D_EINVAL;
+    try {
+        DeviceGuard g(ctx->device);
+        f();
+        ctx->err.clear();
+        return B2D_OK;
+    } catch (const Fail& e) {
+        ctx->err = e.msg;
+        return e.code;
+    } catch (const std::exception& e) {
+        ctx->err = e.what();
+        return B2D_EINVAL;
+    }
+}
+
+void check_status_word(b2d_ctx* ctx, cudaStream_t st) {
+    int s = 0;
+    CK(cudaMemcpyAsync(&s, ctx->status.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (s != 0) {
+        CK(cudaMemsetAsync(ctx->status.p, 0, sizeof(int), st));
+        CK(cudaStreamSynchronize(st));
+        if (s == kErrNonFinite) fail(B2D_ENONFINITE, "VibeVoice diffusion sampler produced non-finite latent");
+        fail(B2D_ETIMEOUT, "a device-side wait expired (code %d); the kernel unwound", s);
+    }
+}
+
+// ------------------------------------------------------------ head: load
+template <typename CT>
+void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
+    const int64_t H = m.H, F = m.F, L = m.cfg.head_layers;
+    const std::string P = "model.prediction_head.";
+    cudaStream_t st = ctx->load_stream;
+    auto need = [&](const std::string& name) {
+        const b2d_tensor_view* t = find_tensor(ts, n, P + name);
+        if (!t) fail(B2D_EINVAL, "missing tensor %s%s", P.c_str(), name.c_str());
+        return t;
+    };
+    auto plain = [](int64_t rows) { return RowMap{rows, 0, 0}; };
+    const size_t e = sizeof(CT);
+    m.w_in.alloc(size_t(H) * kHeadLatent * e);
+    upload_weight<CT>(need("noisy_images_proj.weight"), H, kHeadLatent, m.w_in.as<CT>(), plain(H), ctx->num_sms, st);
+    m.w_cond.alloc(size_t(H) * H * e);
+    upload_weight<CT>(need("cond_proj.weight"), H, H, m.w_cond.as<CT>(), plain(H), ctx->num_sms, st);
+    m.w_t1.alloc(size_t(H) * 256 * e);
+    upload_weight<CT>(need("t_embedder.mlp.0.weight"), H, 256, m.w_t1.as<CT>(), plain(H), ctx->num_sms, st);
+    m.w_t2.alloc(size_t(H) * H * e);
+    upload_weight<CT>(need("t_embedder.mlp.2.weight"), H, H, m.w_t2.as<CT>(), plain(H), ctx->num_sms, st);
+    // All adaLN projections in one [NADA, H] matrix: layer l at rows [3H l, 3H (l+1)), final at [3H L, 3H L + 2H).
+    m.w_ada.alloc(size_t(m.NADA) * H * e);
+    std::vector<float> norms(static_cast<size_t>(L * H));
+    m.w_gu.resize(size_t(L));
+    m.w_down.resize(size_t(L));
+    for (int64_t l = 0; l < L; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        upload_weight<CT>(need(p + "adaLN_modulation.1.weight"), 3 * H, H, m.w_ada.as<CT>(),
+                          RowMap{3 * H, 0, 3 * H * l}, ctx->num_sms, st);
+        // gate_proj / up_proj interleaved in 128-row blocks: [g0..g127 | u0..u127 | g128.. ] so one
+        // 256-column GEMM tile holds matching gate and up columns for the SwiGLU epilogue.
+        m.w_gu[size_t(l)].alloc(size_t(2 * F) * H * e);
+        upload_weight<CT>(need(p + "ffn.gate_proj.weight"), F, H, m.w_gu[size_t(l)].as<CT>(), RowMap{128, 256, 0},
+                          ctx->num_sms, st);
+        upload_weight<CT>(need(p + "ffn.up_proj.weight"), F, H, m.w_gu[size_t(l)].as<CT>(), RowMap{128, 256, 128},
+                          ctx->num_sms, st);
+        m.w_down[size_t(l)].alloc(size_t(H) * F * e);
+        upload_weight<CT>(need(p + "ffn.down_proj.weight"), H, F, m.w_down[size_t(l)].as<CT>(), plain(H),
+                          ctx->num_sms, st);
+        const auto nw = host_f32(need(p + "norm.weight"), H);
+        std::memcpy(norms.data() + l * H, nw.data(), size_t(H) * 4);
+    }
+    upload_weight<CT>(need("final_layer.adaLN_modulation.1.weight"), 2 * H, H, m.w_ada.as<CT>(),
+                      RowMap{2 * H, 0, 3 * H * L}, ctx->num_sms, st);
+    m.w_final.alloc(size_t(kHeadLatent) * H * e);
+    upload_weight<CT>(need("final_layer.linear.weight"), kHeadLatent, H, m.w_final.as<CT>(), plain(kHeadLatent),
+                      ctx->num_sms, st);
+    m.norms.alloc(norms.size() * 4);
+    CK(cudaMemcpy(m.norms.p, norms.data(), norms.size() * 4, cudaMemcpyHostToDevice));
+
+    const bool bf = m.bf16;
+    m.tm_in = make_tmap(m.w_in.p, bf, H, kHeadLatent, 256);
+    m.tm_cond = make_tmap(m.w_cond.p, bf, H, H, 256);
+    m.tm_ada = make_tmap(m.w_ada.p, bf, m.NADA, H, 256);
+    m.tm_final = make_tmap(m.w_final.p, bf, kHeadLatent, H, 64);
+    m.tm_gu.clear();
+    m.tm_down.clear();
+    for (int64_t l = 0; l < L; ++l) {
+        m.tm_gu.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 256));
+        m.tm_down.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 256));
+    }
+}
+
+// --------------------------------------------------------- head: workspace
+template <typename CT>
+HeadWorkspace& head_workspace(b2d_ctx* ctx, HeadModel& m, int64_t batch) {
+    if (m.ws && m.ws->batch == batch) return *m.ws;
+    m.ws.reset();
+    auto ws = std::make_unique<HeadWorkspace>();
+    ws->batch = batch;
+    const int64_t R = 2 * batch, H = m.H, F = m.F;
+    const size_t e = sizeof(CT);
+    ws->x.alloc(size_t(R) * H * 4);
+    ws->cp.alloc(size_t(R) * H * 4);
+    ws->sc.alloc(size_t(R) * H * e);
+    ws->ada.alloc(size_t(R) * m.NADA * 4);
+    ws->h.alloc(size_t(R) * H * e);
+    ws->ffn.alloc(size_t(R) * F * e);
+    ws->v.alloc(size_t(R) * kHeadLatent * 4);
+    ws->noisy.alloc(size_t(R) * kHeadLatent * e);
+    ws->cond.alloc(size_t(R) * H * 4);
+    ws->cond_ct.alloc(size_t(R) * H * e);
+    ws->init.alloc(size_t(R) * kHeadLatent * 4);
+    ws->xstate.alloc(size_t(batch) * kHeadLatent * 4);
+    ws->hist0.alloc(size_t(batch) * kHeadLatent * 4);
+    ws->hist1.alloc(size_t(batch) * kHeadLatent * 4);
+    ws->out.alloc(size_t(batch) * kHeadLatent * 4);
+    ws->temb.alloc(size_t(kMaxTembSteps) * H * 4);
+    ws->h1.alloc(size_t(kMaxTembSteps) * H * 4);
+    ws->tsteps.alloc(size_t(kMaxTembSteps) * 4);
+    ws->coefs.alloc(size_t(kMaxTembSteps) * sizeof(VvStepCoef));
+    ws->ptstep.alloc(256);
+    const bool bf = m.bf16;
+    ws->tm_noisy = make_tmap(ws->noisy.p, bf, R, kHeadLatent, 128);
+    ws->tm_cond = make_tmap(ws->cond_ct.p, bf, R, H, 128);
+    ws->tm_sc = make_tmap(ws->sc.p, bf, R, H, 128);
+    ws->tm_h = make_tmap(ws->h.p, bf, R, H, 128);
+    ws->tm_ffn = make_tmap(ws->ffn.p, bf, R, F, 128);
+    m.ws = std::move(ws);
+    return *m.ws;
+}
+
+// One evaluation of the head on ws.noisy / ws.cp (cond_proj already applied) with
+// the time embedding row temb_row -> ws.v.  diffusion_head.cpp:495-523.
+template <typename CT>
+void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, cudaStream_t st) {
+    const int64_t R = 2 * ws.batch, H = m.H, F = m.F, L = m.cfg.head_layers;
+    const int sms = ctx->num_sms;
+    int* status = ctx->status.as<int>();
+    EpiParams ep;
+    ep.status = status;
+    // x = noisy * W_in^T
+    ep.out = ws.x.p;
+    ep.ldo = H;
+    launch_gemm<CT>(256, EPI_F32, ws.tm_noisy, m.tm_in, R, H, kHeadLatent, ep, sms, st);
+    // sc = silu(cond_proj + t_emb)
+    silu_cond_kernel<CT><<<grid_for(R * H / 4, 256, sms), 256, 0, st>>>(
+        ws.cp.as<float>(), ws.temb.as<float>() + int64_t(temb_row) * H, R, int(H), ws.sc.as<CT>());
+    CK(cudaGetLastError());
+    // every adaLN modulation of every layer in one GEMM: ada = sc * W_ada^T  [R, NADA]
+    ep = EpiParams{};
+    ep.status = status;
+    ep.out = ws.ada.p;
+    ep.ldo = m.NADA;
+    launch_gemm<CT>(256, EPI_F32, ws.tm_sc, m.tm_ada, R, m.NADA, H, ep, sms, st);
+    const float* ada = ws.ada.as<float>();
+    for (int64_t l = 0; l < L; ++l) {
+        const float* shift = ada + 3 * H * l;
+        rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(ws.x.as<float>(), H, m.norms.as<float>() + l * H,
+                                                                  shift, shift + H, m.NADA, m.cfg.rms_norm_eps,
+                                                                  int(H), ws.h.as<CT>(), H);
+        CK(cudaGetLastError());
+        ep = EpiParams{};
+        ep.status = status;
+        ep.out = ws.ffn.p;
+        ep.ldo = F;
+        launch_gemm<CT>(256, EPI_SWIGLU, ws.tm_h, m.tm_gu[size_t(l)], R, 2 * F, H, ep, sms, st);
+        ep = EpiParams{};
+        ep.status = status;
+        ep.resid = ws.x.as<float>();
+        ep.ldr = H;
+        ep.gate = shift + 2 * H;
+        ep.ldg = m.NADA;
+        launch_gemm<CT>(256, EPI_RESID, ws.tm_ffn, m.tm_down[size_t(l)], R, H, F, ep, sms, st);
+    }
+    const float* fshift = ada + 3 * H * L;
+    rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(ws.x.as<float>(), H, nullptr, fshift, fshift + H,
+                                                              m.NADA, m.cfg.rms_norm_eps, int(H), ws.h.as<CT>(), H);
+    CK(cudaGetLastError());
+    ep = EpiParams{};
+    ep.status = status;
+    ep.out = ws.v.p;
+    ep.ldo = kHeadLatent;
+    launch_gemm<CT>(64, EPI_F32, ws.tm_h, m.tm_final, R, kHeadLatent, H, ep, sms, st);
+}
+
+// cond_ct = ct(cond); cp = cond * W_cond^T (step-invariant, hoisted out of the loop)
+template <typename CT>
+void head_cond_proj(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, cudaStream_t st) {
+    const int64_t R = 2 * ws.batch, H = m.H;
+    f32_to_ct_kernel<CT><<<grid_for(R * H, 256, ctx->num_sms), 256, 0, st>>>(ws.cond.as<float>(), R * H,
+                                                                              ws.cond_ct.as<CT>());
+    CK(cudaGetLastError());
+    EpiParams ep;
+    ep.status = ctx->status.as<int>();
+    ep.out = ws.cp.p;
+    ep.ldo = H;
+    launch_gemm<CT>(256, EPI_F32, ws.tm_cond, m.tm_cond, R, H, H, ep, ctx->num_sms, st);
+}
+
+template <typename CT>
+void head_temb(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, const float* tsteps, int S, cudaStream_t st) {
+    const int H = int(m.H);
+    const int blocks = (H + 7) / 8;
+    temb_stage1_kernel<CT><<<blocks, 256, 0, st>>>(tsteps, S, m.w_t1.as<CT>(), H, ws.h1.as<float>());
+    CK(cudaGetLastError());
+    temb_stage2_kernel<CT><<<blocks, 256, 0, st>>>(ws.h1.as<float>(), S, m.w_t2.as<CT>(), H, ws.temb.as<float>());
+    CK(cudaGetLastError());
+}
+
+// The full sampling loop on workspace buffers (ws.cond, ws.init filled; coefs/tsteps uploaded).
+template <typename CT>
+void head_sample_body(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int S, float cfg, cudaStream_t st) {
+    const int64_t n_half = ws.batch * kHeadLatent;
+    const int sms = ctx->num_sms;
+    head_cond_proj<CT>(ctx, m, ws, st);
+    head_temb<CT>(ctx, m, ws, ws.tsteps.as<float>(), S, st);
+    vv_init_kernel<CT><<<grid_for(n_half, 256, sms), 256, 0, st>>>(ws.init.as<float>(), ws.xstate.as<float>(),
+                                                                     ws.noisy.as<CT>(), n_half);
+    CK(cudaGetLastError());
+    for (int s = 0; s < S; ++s) {
+        head_forward<CT>(ctx, m, ws, s, st);
+        float* hp = (s & 1) ? ws.hist0.as<float>() : ws.hist1.as<float>();
+        float* hc = (s & 1) ? ws.hist1.as<float>() : ws.hist0.as<float>();
+        vv_cfg_dpm_kernel<CT><<<grid_for(n_half, 256, sms), 256, 0, st>>>(
+            ws.v.as<float>(), ws.xstate.as<float>(), hp, hc, ws.noisy.as<CT>(), ws.out.as<float>(), n_half,
+            ws.coefs.as<VvStepCoef>(), s, cfg, ctx->status.as<int>());
+        CK(cudaGetLastError());
+    }
+}
+
+template <typename CT>
+void head_sample(b2d_ctx* ctx, const float* pos, const float* neg, const float* init, int64_t batch, int64_t steps,
+                 float cfg, float* out, cudaStream_t st, bool host) {
+    HeadModel& m = *ctx->head;
+    if (steps > kMaxTembSteps) fail(B2D_EINVAL, "at most %d inference steps per call are supported", kMaxTembSteps);
+    HeadWorkspace& ws = head_workspace<CT>(ctx, m, batch);
+    const int64_t H = m.H;
+    const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    const size_t half = size_t(batch) * H * 4;
+    CK(cudaMemcpyAsync(ws.cond.p, pos, half, kind, st));
+    CK(cudaMemcpyAsync(ws.cond.as<char>() + half, neg, half, kind, st));
+    CK(cudaMemcpyAsync(ws.init.p, init, size_t(2 * batch) * kHeadLatent * 4, kind, st));
+
+    std::vector<b2d_vv_step> sched(static_cast<size_t>(steps));
+    if (b2d_vv_schedule(m.cfg.ddpm_num_steps, steps, sched.data()) != B2D_OK)
+        fail(B2D_EINVAL, "VibeVoice scheduler requires positive timestep counts");
+    uint32_t cfg_bits;
+    std::memcpy(&cfg_bits, &cfg, 4);
+    const auto key = std::make_tuple(steps, cfg_bits);
+    auto it = ws.graphs.find(key);
+    if (it == ws.graphs.end()) {
+        // Step tables are constant for a given (ddpm steps, steps): upload once, then capture.
+        std::vector<VvStepCoef> coefs(static_cast<size_t>(steps));
+        std::vector<float> ts(static_cast<size_t>(steps));
+        for (int64_t i = 0; i < steps; ++i) {
+            const b2d_vv_step& s = sched[size_t(i)];
+            coefs[size_t(i)] = VvStepCoef{s.alpha_s, s.sigma_s, s.sample_coeff, s.d0_coeff, s.inv_r0, s.order,
+                                          i == steps - 1 ? 1 : 0, 0};
+            ts[size_t(i)] = float(s.timestep);
+        }
+        CK(cudaMemcpyAsync(ws.coefs.p, coefs.data(), coefs.size() * sizeof(VvStepCoef), cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(ws.tsteps.p, ts.data(), ts.size() * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaStreamSynchronize(st));
+        cudaStream_t cap;
+        CK(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+        try {
+            head_sample_body<CT>(ctx, m, ws, int(steps), cfg, cap);
+        } catch (...) {
+            cudaStreamEndCapture(cap, &g);
+            if (g) cudaGraphDestroy(g);
+            cudaStreamDestroy(cap);
+            throw;
+        }
+        CK(cudaStreamEndCapture(cap, &g));
+        cudaGraphExec_t exec = nullptr;
+        CK(cudaGraphInstantiate(&exec, g, 0));
+        cudaGraphDestroy(g);
+        cudaStreamDestroy(cap);
+        // The tables in ws.coefs/ws.tsteps belong to the most recently captured key; keep one
+        // schedule resident by dropping graphs of other step counts.
+        for (auto& kv : ws.graphs) cudaGraphExecDestroy(kv.second);
+        ws.graphs.clear();
+        it = ws.graphs.emplace(key, exec).first;
+    }
+    CK(cudaGraphLaunch(it->second, st));
+    CK(cudaMemcpyAsync(out, ws.out.p, size_t(batch) * kHeadLatent * 4,
+                       host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+    if (host) check_status_word(ctx, st);
+}
+
+template <typename CT>
+void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timestep, const float* cond, float* out,
+                  cudaStream_t st) {
+    HeadModel& m = *ctx->head;
+    // predict() evaluates `frames` rows; the workspace holds 2*batch rows, so use ceil(frames/2).
+    const int64_t batch = (frames + 1) / 2;
+    HeadWorkspace& ws = head_workspace<CT>(ctx, m, batch);
+    const int64_t R = 2 * batch, H = m.H;
+    CK(cudaMemsetAsync(ws.cond.p, 0, size_t(R) * H * 4, st));
+    CK(cudaMemcpyAsync(ws.cond.p, cond, size_t(frames) * H * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemsetAsync(ws.init.p, 0, size_t(R) * kHeadLatent * 4, st));
+    CK(cudaMemcpyAsync(ws.init.p, noisy, size_t(frames) * kHeadLatent * 4, cudaMemcpyHostToDevice, st));
+    f32_to_ct_kernel<CT><<<grid_for(R * kHeadLatent, 256, ctx->num_sms), 256, 0, st>>>(
+        ws.init.as<float>(), R * kHeadLatent, ws.noisy.as<CT>());
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(ws.ptstep.p, &timestep, 4, cudaMemcpyHostToDevice, st));
+    head_cond_proj<CT>(ctx, m, ws, st);
+    head_temb<CT>(ctx, m, ws, ws.ptstep.as<float>(), 1, st);
+    head_forward<CT>(ctx, m, ws, 0, st);
+    CK(cudaMemcpyAsync(out, ws.v.p, size_t(frames) * kHeadLatent * 4, cudaMemcpyDeviceToHost, st));
+    check_status_word(ctx, st);
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+const char* b2d_version(void) { return "b200diff 0.1 (sm_100a)"; }
+
+b2d_status b2d_create(int device, b2d_ctx** out) {
+    if (!out) return B2D_EINVAL;
+    *out = nullptr;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+        cudaGetLastError();
+        return B2D_ENODEV;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return B2D_ENODEV;
+    auto ctx = std::make_unique<b2d_ctx>();
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    b2d_status s = guarded(ctx.get(), [&] {
+        ctx->status.alloc(256);
+        CK(cudaMemset(ctx->status.p, 0, 256));
+        CK(cudaStreamCreateWithFlags(&ctx->load_stream, cudaStreamNonBlocking));
+        encode_fn();
+    });
+    if (s != B2D_OK) return s;
+    *out = ctx.release();
+    return B2D_OK;
+}
+
+void b2d_destroy(b2d_ctx* ctx) {
+    if (!ctx) return;
+    {
+        DeviceGuard g(ctx->device);
+        cudaDeviceSynchronize();
+        ctx->head.reset();
+        ctx->status.release();
+        if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
+    }
+    delete ctx;
+}
+
+const char* b2d_last_error(const b2d_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+b2d_status b2d_sync(b2d_ctx* ctx, void* stream) {
+    return guarded(ctx, [&] { check_status_word(ctx, static_cast<cudaStream_t>(stream)); });
+}
+
+b2d_status b2d_vv_head_load(b2d_ctx* ctx, const b2d_vv_head_config* config, const b2d_tensor_view* tensors,
+                            int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "VibeVoice diffusion head requires model weights");
+        const b2d_vv_head_config& c = *config;
+        if (c.hidden_size <= 0 || c.latent_size <= 0 || c.head_layers <= 0)
+            fail(B2D_EINVAL, "VibeVoice diffusion head dimensions must be positive");
+        if (!(c.head_ffn_ratio > 0.0F)) fail(B2D_EINVAL, "VibeVoice diffusion head FFN ratio must be positive");
+        if (!(c.rms_norm_eps > 0.0F)) fail(B2D_EINVAL, "VibeVoice diffusion head RMS epsilon must be positive");
+        if (c.latent_size != kHeadLatent) fail(B2D_EINVAL, "latent_size must be 64 on this path");
+        auto m = std::make_unique<HeadModel>();
+        m->cfg = c;
+        m->H = c.hidden_size;
+        m->F = int64_t(double(c.hidden_size) * double(c.head_ffn_ratio));
+        if (m->F <= 0) fail(B2D_EINVAL, "VibeVoice diffusion head FFN dimension is invalid");
+        if (m->H % 256 || m->F % 128)
+            fail(B2D_EINVAL, "hidden_size must be a multiple of 256 and the FFN width a multiple of 128");
+        m->NADA = 3 * m->H * c.head_layers + 2 * m->H;
+        // fp16 operands for F16 / Q8_0 / F32 weights; bf16 when the weights are BF16.
+        const b2d_tensor_view* probe = find_tensor(tensors, n_tensors, "model.prediction_head.cond_proj.weight");
+        m->bf16 = probe && probe->ggml_type == B2D_TYPE_BF16;
+        ctx->head.reset();
+        if (m->bf16)
+            head_load_t<__nv_bfloat16>(ctx, *m, tensors, n_tensors);
+        else
+            head_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->head = std::move(m);
+    });
+}
+
+b2d_status b2d_vv_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, int64_t latent_size, float timestep,
+                          const float* condition, int64_t condition_hidden_size, float* out, void* stream) {
+    return guarded(ctx, [&] {
+        if (!ctx->head) fail(B2D_ESTATE, "VibeVoice diffusion head weights are not loaded");
+        const HeadModel& m = *ctx->head;
+        if (frames <= 0 || latent_size != m.cfg.latent_size || condition_hidden_size != m.H)
+            fail(B2D_EINVAL, "VibeVoice diffusion head received invalid input shape");
+        if (!noisy || !condition || !out) fail(B2D_EINVAL, "VibeVoice diffusion head received invalid input shape");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (m.bf16)
+            head_predict<__nv_bfloat16>(ctx, noisy, frames, timestep, condition, out, st);
+        else
+            head_predict<__half>(ctx, noisy, frames, timestep, condition, out, st);
+    });
+}
+
+static b2d_status vv_sample_common(b2d_ctx* ctx, const float* pos, const float* neg, const float* init, int64_t batch,
+                                   int64_t steps, float cfg, float* out, void* stream, bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->head) fail(B2D_ESTATE, "VibeVoice diffusion head weights are not loaded");
+        if (batch <= 0) fail(B2D_EINVAL, "VibeVoice diffusion sampler requires positive dimensions");
+        if (steps <= 0) fail(B2D_EINVAL, "VibeVoice diffusion sampler requires positive inference steps");
+        if (!pos) fail(B2D_EINVAL, "VibeVoice diffusion sampler payload size mismatch for positive_condition");
+        if (!neg) fail(B2D_EINVAL, "VibeVoice diffusion sampler payload size mismatch for negative_condition");
+        if (!init) fail(B2D_EINVAL, "VibeVoice diffusion sampler payload size mismatch for initial_speech");
+        if (!out) fail(B2D_EINVAL, "output buffer is null");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (ctx->head->bf16)
+            head_sample<__nv_bfloat16>(ctx, pos, neg, init, batch, steps, cfg, out, st, host);
+        else
+            head_sample<__half>(ctx, pos, neg, init, batch, steps, cfg, out, st, host);
+    });
+}
+
+b2d_status b2d_vv_sample(b2d_ctx* ctx, const float* positive_condition, const float* negative_condition,
+                         const float* initial_speech, int64_t batch, int64_t steps, float cfg, float* out_latents,
+                         void* stream) {
+    return vv_sample_common(ctx, positive_condition, negative_condition, initial_speech, batch, steps, cfg,
+                            out_latents, stream, true);
+}
+
+b2d_status b2d_vv_sample_device(b2d_ctx* ctx, const float* positive_condition, const float* negative_condition,
+                                const float* initial_speech, int64_t batch, int64_t steps, float cfg,
+                                float* out_latents, void* stream) {
+    return vv_sample_common(ctx, positive_condition, negative_condition, initial_speech, batch, steps, cfg,
+                            out_latents, stream, false);
+}
+
+b2d_status b2d_q8_0_dequantize(b2d_ctx* ctx, const void* q8_dev, int64_t rows, int64_t k, float* out_dev,
+                               void* stream) {
+    return guarded(ctx, [&] {
+        if (!q8_dev || !out_dev || rows <= 0 || k <= 0 || k % 32) fail(B2D_EINVAL, "invalid Q8_0 shape");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        dequant_q8_0_kernel<float><<<grid_for(rows * k / 32, 256, ctx->num_sms), 256, 0, st>>>(
+            static_cast<const uint8_t*>(q8_dev), rows, k, out_dev, k, RowMap{rows, 0, 0});
+        CK(cudaGetLastError());
+    });
+}
+
+b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
+                    int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
+                    float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream) {
+    return guarded(ctx, [&] {
+        if (m <= 0 || n <= 0 || k <= 0) fail(B2D_EINVAL, "GEMM dimensions must be positive");
+        if (epilogue == EPI_SWIGLU && bn != 256) fail(B2D_EINVAL, "SwiGLU epilogue needs 256-column tiles");
+        if (epilogue == EPI_RESID ? !resid_dev : !out_dev) fail(B2D_EINVAL, "GEMM output is null");
+        const CUtensorMap ta = make_tmap(a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128);
+        const CUtensorMap tb = make_tmap(b_dev, bf16 != 0, uint64_t(n), uint64_t(k), uint32_t(bn));
+        EpiParams ep;
+        ep.out = out_dev;
+        ep.ldo = ldo;
+        ep.bias = bias_dev;
+        ep.resid = resid_dev;
+        ep.ldr = ldr;
+        ep.gate = gate_dev;
+        ep.ldg = ldg;
+        ep.status = ctx->status.as<int>();
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (bf16)
+            launch_gemm<__nv_bfloat16>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+        else
+            launch_gemm<__half>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+    });
+}
+
+}  // extern "C"

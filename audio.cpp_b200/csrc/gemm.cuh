@@ -1,0 +1,279 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a:  C = A * B^T
+//   A: activations [M, K], K contiguous (fp16 or bf16)
+//   B: weights     [N, K], K contiguous (the ggml [out, in] layout), same type as A
+// with fp32 accumulation in TMEM and a fused epilogue.  This is the dense
+// contraction behind every ggml_mul_mat(W, X) on the diffusion hot path
+// (LinearModule::build, src/framework/modules/linear_module.cpp:73-108).
+//
+// CTA = 6 warps: warp 0 issues TMA loads (128B-swizzled K-major tiles) into a
+// STAGES-deep shared-memory ring; warp 1 owns TMEM and issues tcgen05.mma
+// (M=128, N=BN, K=16 per instruction) from one lane; warps 2-5 drain the
+// double-buffered TMEM accumulator (2 x BN fp32 columns) and run the epilogue
+// while the next tile's MMAs proceed.  One CTA per SM, grid = min(tiles, SMs),
+// tiles walk M fastest so CTAs running together share a weight slice in L2.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <type_traits>
+
+#include "ptx.cuh"
+
+namespace b2d {
+
+enum EpiKind : int {
+    EPI_F32 = 0,     // out_f32[r, n] = acc + bias[n]
+    EPI_CT = 1,      // out_ct[r, n]  = ct(acc + bias[n])
+    EPI_SWIGLU = 2,  // BN=256 tile = [128 "activated" | 128 "linear"] cols -> out_ct[r, n0/2 + j] = silu(a+ba) * (l+bl)
+    EPI_RESID = 3,   // resid[r, n] += gate[r, n] * (acc + bias[n])   (gate == nullptr -> 1)
+};
+
+struct EpiParams {
+    void* out = nullptr;
+    int64_t ldo = 0;
+    const float* bias = nullptr;
+    float* resid = nullptr;
+    int64_t ldr = 0;
+    const float* gate = nullptr;
+    int64_t ldg = 0;
+    int* status = nullptr;
+};
+
+template <typename CT>
+struct CtTraits;
+template <>
+struct CtTraits<__half> {
+    static constexpr uint32_t kFmt = 0;
+    __device__ static __forceinline__ uint32_t pack2(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+template <>
+struct CtTraits<__nv_bfloat16> {
+    static constexpr uint32_t kFmt = 1;
+    __device__ static __forceinline__ uint32_t pack2(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN>
+struct GemmShape {
+    static constexpr int BM = 128;
+    static constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+    static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr uint32_t A_BYTES = BM * BK * 2;
+    static constexpr uint32_t B_BYTES = BN * BK * 2;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+};
+
+template <int BN, int EPI, typename CT>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                   int K, EpiParams ep) {
+    using S = GemmShape<BN>;
+    constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert(EPI != EPI_SWIGLU || BN == 256, "SwiGLU tiles pair 128 + 128 columns");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_tiles = (M + BM - 1) / BM;
+    const int num_tiles = m_tiles * (N / BN);
+    const int k_blocks = K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int m0 = (tile % m_tiles) * BM;
+                const int n0 = (tile / m_tiles) * BN;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
+                    uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
+                    tma_load_2d(sa + S::A_BYTES, &tmB, &full[stage], kb * BK, n0);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(CtTraits<CT>::kFmt, BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, ep.status, kErrTimeoutMma)) goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, ep.status, kErrTimeoutMma)) goto done;
+                    tc_fence_after();
+                    uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
+                    const uint64_t adesc = smem_desc_sw128(sa);
+                    const uint64_t bdesc = smem_desc_sw128(sa + S::A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        // +32 bytes along K inside the 128-byte swizzle row == +2 in the >>4 address field
+                        mma_f16_ss(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc,
+                                   (kb | k) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                mma_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+        }
+    } else {
+        const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
+        const int row_in_tile = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int m0 = (tile % m_tiles) * BM;
+            const int n0 = (tile / m_tiles) * BN;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.status, kErrTimeoutEpilogue)) goto done;
+            tc_fence_after();
+            const int row = m0 + row_in_tile;
+            const bool live = row < M;
+            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+            if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    float a[32], l[32];
+                    __syncwarp();
+                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), a);
+                    tmem_ld_32x32b_x32(tbase + uint32_t(128 + c * 32), l);
+                    tmem_ld_wait();
+                    if (live) {
+                        if (ep.bias) {
+                            const float* ba = ep.bias + n0 + c * 32;
+                            const float* bl = ep.bias + n0 + 128 + c * 32;
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                a[j] += __ldg(ba + j);
+                                l[j] += __ldg(bl + j);
+                            }
+                        }
+                        uint32_t packed[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            packed[j] = CtTraits<CT>::pack2(silu_f(a[2 * j]) * l[2 * j],
+                                                            silu_f(a[2 * j + 1]) * l[2 * j + 1]);
+                        CT* dst = reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + n0 / 2 + c * 32;
+                        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    float v[32];
+                    __syncwarp();
+                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+                    tmem_ld_wait();
+                    if (!live) continue;
+                    const int n = n0 + c * 32;
+                    if (ep.bias) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + n + j);
+                    }
+                    if constexpr (EPI == EPI_F32) {
+                        float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.out) + int64_t(row) * ep.ldo + n);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else if constexpr (EPI == EPI_CT) {
+                        uint32_t packed[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) packed[j] = CtTraits<CT>::pack2(v[2 * j], v[2 * j + 1]);
+                        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + n);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+                    } else {  // EPI_RESID
+                        float4* r4 = reinterpret_cast<float4*>(ep.resid + int64_t(row) * ep.ldr + n);
+                        const float4* g4 =
+                            ep.gate ? reinterpret_cast<const float4*>(ep.gate + int64_t(row) * ep.ldg + n) : nullptr;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            float4 r = r4[j];
+                            const float4 g = g4 ? g4[j] : make_float4(1.f, 1.f, 1.f, 1.f);
+                            r.x += g.x * v[4 * j];
+                            r.y += g.y * v[4 * j + 1];
+                            r.z += g.z * v[4 * j + 2];
+                            r.w += g.w * v[4 * j + 3];
+                            r4[j] = r;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, S::TMEM_COLS);
+    }
+}
+
+}  // namespace b2d

@@ -1,0 +1,260 @@
+// Memory-bound kernels of the diffusion hot path: weight dequantisation,
+// fused RMSNorm + adaLN modulate, SiLU conditioning, the timestep-embedding
+// MLP, and the fused CFG + DPM-Solver++ update.  All use 128-bit accesses
+// along rows and warp-shuffle reductions; grids are sized to fill the SMs.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "gemm.cuh"
+
+namespace b2d {
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(float v) { return v; }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ------------------------------------------------------------------ weights
+// Source encodings (ggml type ids): 0 = F32, 1 = F16, 8 = Q8_0, 30 = BF16.
+// Row r of the source lands in destination row
+//   dst_row(r) = (r / blk) * blk_stride + (r % blk) + row_offset
+// which expresses plain copies (blk = rows) and the block interleaving used to
+// pair SwiGLU halves inside one GEMM tile.
+struct RowMap {
+    int64_t blk;
+    int64_t blk_stride;
+    int64_t row_offset;
+    __device__ __forceinline__ int64_t operator()(int64_t r) const { return (r / blk) * blk_stride + (r % blk) + row_offset; }
+};
+
+// Q8_0 block = fp16 scale d + 32 int8 quants (external/ggml/src/ggml-common.h:241-246).
+// value = q * fp32(d) exactly as dequantize_row_q8_0 (ggml-quants.c:491-505), then one
+// rounding to the GEMM operand type.
+template <typename OutT>
+__global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t k, OutT* __restrict__ dst,
+                                    int64_t ldd, RowMap map) {
+    const int64_t nblk_row = k / 32;
+    const int64_t total = rows * nblk_row;
+    for (int64_t b = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; b < total; b += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = b / nblk_row, kb = b % nblk_row;
+        const uint8_t* blk = src + b * 34;
+        const uint16_t dbits = uint16_t(blk[0]) | (uint16_t(blk[1]) << 8);
+        const float d = __half2float(__ushort_as_half(dbits));
+        OutT* o = dst + map(r) * ldd + kb * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = from_f32<OutT>(float(int8_t(blk[2 + j])) * d);
+    }
+}
+
+template <typename InT, typename OutT>
+__global__ void convert_rows_kernel(const InT* __restrict__ src, int64_t rows, int64_t k, OutT* __restrict__ dst,
+                                    int64_t ldd, RowMap map) {
+    const int64_t total = rows * k;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = i / k, c = i % k;
+        dst[map(r) * ldd + c] = from_f32<OutT>(to_f32(src[i]));
+    }
+}
+
+__global__ void bf16_bits_to_f32_kernel(const uint16_t* __restrict__ src, int64_t n, float* __restrict__ dst) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        dst[i] = __uint_as_float(uint32_t(src[i]) << 16);
+}
+
+// ------------------------------------------------- RMSNorm + adaLN modulate
+// h = ct( (x / sqrt(mean(x^2) + eps)) * w * (1 + scale) + shift )   per row
+// (RMSNormModule + modulate: src/models/vibevoice/diffusion_head.cpp:130-139,183-220)
+// One CTA per row; x, shift, scale are fp32 rows read with float4.
+template <typename CT, int THREADS>
+__global__ void __launch_bounds__(THREADS) rms_modulate_kernel(const float* __restrict__ x, int64_t ldx,
+                                                               const float* __restrict__ w, const float* __restrict__ shift,
+                                                               const float* __restrict__ scale, int64_t ldm, float eps,
+                                                               int H, CT* __restrict__ out, int64_t ldo) {
+    const int64_t row = blockIdx.x;
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * ldx);
+    const int n4 = H / 4;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n4; i += THREADS) {
+        const float4 v = x4[i];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    __shared__ float red[THREADS / 32];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < THREADS / 32 ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(red[0] / float(H) + eps);
+    const float4* s4 = reinterpret_cast<const float4*>(shift + row * ldm);
+    const float4* c4 = reinterpret_cast<const float4*>(scale + row * ldm);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (int i = threadIdx.x; i < n4; i += THREADS) {
+        float4 v = x4[i];
+        const float4 sh = s4[i], sc = c4[i];
+        const float4 ww = w ? w4[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float a = v.x * inv * ww.x * (1.f + sc.x) + sh.x;
+        const float b = v.y * inv * ww.y * (1.f + sc.y) + sh.y;
+        const float c = v.z * inv * ww.z * (1.f + sc.z) + sh.z;
+        const float d = v.w * inv * ww.w * (1.f + sc.w) + sh.w;
+        uint2 p = make_uint2(CtTraits<CT>::pack2(a, b), CtTraits<CT>::pack2(c, d));
+        reinterpret_cast<uint2*>(out + row * ldo)[i] = p;
+    }
+}
+
+// sc[r, :] = ct(silu(cp[r, :] + temb[:]))   (SiluModule on c = cond_proj + t_emb)
+template <typename CT>
+__global__ void silu_cond_kernel(const float* __restrict__ cp, const float* __restrict__ temb, int64_t rows, int H,
+                                 CT* __restrict__ out) {
+    const int64_t n4 = rows * H / 4;
+    const int h4 = H / 4;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        const float4 c = reinterpret_cast<const float4*>(cp)[i];
+        const float4 t = reinterpret_cast<const float4*>(temb)[i % h4];
+        const float a = c.x + t.x, b = c.y + t.y, d = c.z + t.z, e = c.w + t.w;
+        reinterpret_cast<uint2*>(out)[i] =
+            make_uint2(CtTraits<CT>::pack2(silu_f(a), silu_f(b)), CtTraits<CT>::pack2(silu_f(d), silu_f(e)));
+    }
+}
+
+// ------------------------------------------------ timestep embedding MLP
+// Stage 1: h1[s, n] = silu( sum_k W1[n, k] * feat_s[k] ), feat_s = [cos(t_s f) | sin(t_s f)], f_i = exp(-ln(1e4) i/128)
+// (make_timestep_freqs + build_timestep_embedding, diffusion_head.cpp:59-66,141-163)
+// Stage 2: temb[s, n] = sum_k W2[n, k] * h1[s, k].
+// One warp per output column n, all steps at once (weights read once).
+constexpr int kMaxTembSteps = 32;
+
+template <typename CT>
+__global__ void temb_stage1_kernel(const float* __restrict__ tsteps, int S, const CT* __restrict__ W1, int H,
+                                   float* __restrict__ h1) {
+    __shared__ float feat[kMaxTembSteps][256];
+    for (int i = threadIdx.x; i < S * 128; i += blockDim.x) {
+        const int s = i / 128, j = i % 128;
+        const float f = expf(-logf(10000.0f) * float(j) / 128.0f);
+        const float a = tsteps[s] * f;
+        feat[s][j] = cosf(a);
+        feat[s][128 + j] = sinf(a);
+    }
+    __syncthreads();
+    const int warps = blockDim.x / 32;
+    const int lane = threadIdx.x & 31;
+    for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < H; n += gridDim.x * warps) {
+        float wv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = to_f32(W1[int64_t(n) * 256 + lane * 8 + j]);
+        for (int s = 0; s < S; ++s) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc += wv[j] * feat[s][lane * 8 + j];
+            acc = warp_sum(acc);
+            if (lane == 0) h1[int64_t(s) * H + n] = silu_f(acc);
+        }
+    }
+}
+
+template <typename CT>
+__global__ void temb_stage2_kernel(const float* __restrict__ h1, int S, const CT* __restrict__ W2, int H,
+                                   float* __restrict__ temb) {
+    const int warps = blockDim.x / 32;
+    const int lane = threadIdx.x & 31;
+    for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < H; n += gridDim.x * warps) {
+        float acc[kMaxTembSteps];
+        for (int s = 0; s < S; ++s) acc[s] = 0.f;
+        for (int k = lane; k < H; k += 32) {
+            const float w = to_f32(W2[int64_t(n) * H + k]);
+            for (int s = 0; s < S; ++s) acc[s] += w * h1[int64_t(s) * H + k];
+        }
+        for (int s = 0; s < S; ++s) {
+            const float v = warp_sum(acc[s]);
+            if (lane == 0) temb[int64_t(s) * H + n] = v;
+        }
+    }
+}
+
+// --------------------------------------------- CFG + DPM-Solver++(2M) step
+// Per-step scalars, computed on the host in fp32 exactly as
+// VibeVoiceDPMSolverScheduler::step (src/models/vibevoice/scheduler.cpp:165-274).
+struct VvStepCoef {
+    float alpha_s;       // convert_model_output: x0 = alpha_s * x - sigma_s * eps
+    float sigma_s;
+    float sample_coeff;  // sigma_t / sigma_s0
+    float d0_coeff;      // -alpha_t * (exp(-h) - 1)
+    float inv_r0;        // 1 / r0 (second order only)
+    int order;           // 1 or 2
+    int last;            // 1 on the final step (write latents out)
+    int pad;
+};
+
+// v: head output [2B, 64] (cond rows then uncond rows).  x: sampler state [B, 64].
+// hist_prev / hist_cur: converted outputs of the previous / this step [B, 64].
+// noisy: next head input [2B, 64] in ct, both halves = x (duplicate_positive_half).
+template <typename CT>
+__global__ void vv_cfg_dpm_kernel(const float* __restrict__ v, float* __restrict__ x, const float* __restrict__ hist_prev,
+                                  float* __restrict__ hist_cur, CT* __restrict__ noisy, float* __restrict__ out_latents,
+                                  int64_t n_half, const VvStepCoef* __restrict__ coefs, int step, float cfg,
+                                  int* __restrict__ status) {
+    const VvStepCoef c = coefs[step];
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n_half; i += int64_t(gridDim.x) * blockDim.x) {
+        const float vc = v[i], vu = v[n_half + i];
+        const float g = vu + cfg * (vc - vu);            // apply_cfg, diffusion_sampler.cpp:35-56
+        const float xs = x[i];
+        const float conv = c.alpha_s * xs - c.sigma_s * g;  // convert_model_output
+        float nx;
+        if (c.order == 1) {
+            nx = c.sample_coeff * xs + c.d0_coeff * conv;  // first_order_update
+        } else {
+            const float d1 = c.inv_r0 * (conv - hist_prev[i]);  // second_order_update
+            nx = c.sample_coeff * xs + c.d0_coeff * conv + 0.5f * c.d0_coeff * d1;
+        }
+        hist_cur[i] = conv;
+        x[i] = nx;
+        if (!isfinite(nx)) atomicCAS(status, 0, kErrNonFinite);
+        if (c.last) {
+            out_latents[i] = nx;
+        } else {
+            const CT h = from_f32<CT>(nx);
+            noisy[i] = h;
+            noisy[n_half + i] = h;
+        }
+    }
+}
+
+// Step 0 set-up: x = initial_speech[:B]; noisy = [x; x] in ct.
+template <typename CT>
+__global__ void vv_init_kernel(const float* __restrict__ init, float* __restrict__ x, CT* __restrict__ noisy, int64_t n_half) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n_half; i += int64_t(gridDim.x) * blockDim.x) {
+        const float v = init[i];
+        x[i] = v;
+        const CT h = from_f32<CT>(v);
+        noisy[i] = h;
+        noisy[n_half + i] = h;
+    }
+}
+
+template <typename CT>
+__global__ void f32_to_ct_kernel(const float* __restrict__ src, int64_t n, CT* __restrict__ dst) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        dst[i] = from_f32<CT>(src[i]);
+}
+
+}  // namespace b2d

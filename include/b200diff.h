@@ -1,0 +1,169 @@
+/*
+ * b200diff.h -- C ABI of the B200 (sm_100a) diffusion denoising library.
+ *
+ * This library replaces, for audio.cpp's diffusion hot path, everything below
+ * the model-family entry points: the ggml graphs, ggml-cuda kernels and the
+ * host-side step loops.  The C++ classes of audio.cpp keep their signatures
+ * and call these functions instead of building ggml graphs.  Each entry point
+ * names the reference interface it replaces (paths inside audio.cpp).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  "host" pointers are ordinary (ideally
+ *     pinned) CPU memory; "dev" pointers are device memory of the context's GPU.
+ *   - All tensors are row-major with the innermost dimension last.  Weight
+ *     tensors keep the ggml/GGUF [out, in] layout and encoding (F32, F16,
+ *     BF16, Q8_0 34-byte blocks); the library converts them once at load.
+ *   - Every function returns B2D_OK (0) or a negative status; the message of
+ *     the last failure on a context is returned by b2d_last_error().  Messages
+ *     reuse the reference's exception texts where one exists.
+ *   - A context is bound to one device and is not thread-safe (the reference
+ *     runtimes are not re-entrant either); independent contexts on different
+ *     devices may be used concurrently from different threads or processes.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).
+ */
+#ifndef B200DIFF_H
+#define B200DIFF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2D_API __attribute__((visibility("default")))
+#else
+#define B2D_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct b2d_ctx b2d_ctx;
+typedef int b2d_status;
+
+enum {
+    B2D_OK = 0,
+    B2D_EINVAL = -1,      /* bad argument / shape (reference: std::runtime_error on validation) */
+    B2D_ECUDA = -2,       /* CUDA runtime / driver error */
+    B2D_ENOMEM = -3,      /* device allocation failed */
+    B2D_ESTATE = -4,      /* call order violated (e.g. sample before load) */
+    B2D_ENONFINITE = -5,  /* non-finite latent produced (reference: "... non-finite latent ...") */
+    B2D_ETIMEOUT = -6,    /* a bounded device-side wait expired; the kernel unwound */
+    B2D_ENODEV = -7       /* no usable sm_100 device */
+};
+
+/* ggml type ids accepted in tensor views (external/ggml/include/ggml.h enum ggml_type). */
+enum { B2D_TYPE_F32 = 0, B2D_TYPE_F16 = 1, B2D_TYPE_Q8_0 = 8, B2D_TYPE_BF16 = 30 };
+
+/* One named weight tensor as stored in GGUF / safetensors (raw bytes, host memory).
+ * dims are in the reference's metadata order ([out, in] for linears).
+ * Replaces TensorSource::require_tensor_data + BackendWeightStore::load_tensor
+ * (include/engine/framework/assets/tensor_source.h:59-120,
+ *  include/engine/framework/core/backend_weight_store.h:50-75). */
+typedef struct {
+    const char* name;
+    int32_t ggml_type;
+    int32_t ndim;
+    int64_t dims[4];
+    const void* data;
+    size_t nbytes;
+} b2d_tensor_view;
+
+/* ---------------------------------------------------------------- context */
+/* Replaces core::init_backend for these graphs (src/framework/core/backend.cpp:94-144). */
+B2D_API b2d_status b2d_create(int device, b2d_ctx** out);
+B2D_API void b2d_destroy(b2d_ctx* ctx);
+B2D_API const char* b2d_last_error(const b2d_ctx* ctx);
+/* Waits for the context's outstanding work and reports any device-side status
+ * (non-finite latent, expired wait) raised since the last check. */
+B2D_API b2d_status b2d_sync(b2d_ctx* ctx, void* stream);
+/* Version string of the library build. */
+B2D_API const char* b2d_version(void);
+
+/* ------------------------------------------------- VibeVoice diffusion head */
+/* Mirrors VibeVoiceDiffusionHeadConfig (include/engine/models/vibevoice/assets.h:56-69). */
+typedef struct {
+    int64_t hidden_size;
+    int64_t latent_size;     /* must be 64 */
+    int64_t head_layers;
+    float head_ffn_ratio;
+    float rms_norm_eps;
+    int64_t ddpm_num_steps;  /* cosine schedule length, 1000 */
+} b2d_vv_head_config;
+
+/* Per-step scalars of VibeVoiceDPMSolverScheduler::step (src/models/vibevoice/scheduler.cpp:165-274). */
+typedef struct {
+    int64_t timestep;
+    float sigma;         /* sigmas_[step] */
+    float sigma_next;    /* sigmas_[step + 1] (0 after the last step) */
+    float alpha_s;       /* convert_model_output: x0 = alpha_s * x - sigma_s * v */
+    float sigma_s;
+    float sample_coeff;  /* sigma_t / sigma_s0 */
+    float d0_coeff;      /* -alpha_t * (exp(-h) - 1) */
+    float inv_r0;        /* 1 / r0 (second-order steps) */
+    int32_t order;       /* 1 or 2 */
+} b2d_vv_step;
+
+/* Host-only (no GPU needed).  Fills `steps` entries with the schedule
+ * VibeVoiceDPMSolverScheduler(ddpm_num_steps).set_timesteps(steps) produces
+ * and the coefficients its step() applies at each index (scheduler.cpp:15-274). */
+B2D_API b2d_status b2d_vv_schedule(int64_t ddpm_num_steps, int64_t steps, b2d_vv_step* out);
+
+/* Loads the prediction head from its GGUF/safetensors tensors
+ * ("model.prediction_head.*", names as load_vibevoice_diffusion_head_weights,
+ *  src/models/vibevoice/diffusion_head.cpp:335-399).
+ * Replaces VibeVoiceDiffusionHeadWeightsRuntime's constructor
+ * (include/engine/models/vibevoice/diffusion_head.h:60-67). */
+B2D_API b2d_status b2d_vv_head_load(b2d_ctx* ctx, const b2d_vv_head_config* config, const b2d_tensor_view* tensors,
+                            int32_t n_tensors);
+
+/* One head evaluation: noisy [frames, latent], condition [frames, hidden] -> out [frames, latent].
+ * Replaces VibeVoiceDiffusionHeadWeightsRuntime::predict (diffusion_head.h:81-87, diffusion_head.cpp:474-493).
+ * Host buffers; synchronous. */
+B2D_API b2d_status b2d_vv_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, int64_t latent_size, float timestep,
+                          const float* condition, int64_t condition_hidden_size, float* out, void* stream);
+
+/* The whole sampling loop: for each of `steps` DPM-Solver++ steps, predict on
+ * [cond || uncond] rows, apply CFG (scale cfg) and the scheduler update, as
+ * sample_vibevoice_speech_latents (include/engine/models/vibevoice/diffusion_sampler.h:23-26,
+ * src/models/vibevoice/diffusion_sampler.cpp:79-121).
+ *   positive_condition, negative_condition: [batch, hidden]
+ *   initial_speech: [2 * batch, latent]   out_latents: [batch, latent]
+ * Host buffers (pinned memory gives asynchronous copies); returns after the
+ * latents are in `out_latents`.  The step loop runs as one captured CUDA graph. */
+B2D_API b2d_status b2d_vv_sample(b2d_ctx* ctx, const float* positive_condition, const float* negative_condition,
+                         const float* initial_speech, int64_t batch, int64_t steps, float cfg, float* out_latents,
+                         void* stream);
+
+/* Same as b2d_vv_sample with device pointers; asynchronous on `stream`
+ * (check b2d_sync for device-side status). */
+B2D_API b2d_status b2d_vv_sample_device(b2d_ctx* ctx, const float* positive_condition, const float* negative_condition,
+                                const float* initial_speech, int64_t batch, int64_t steps, float cfg,
+                                float* out_latents, void* stream);
+
+/* ------------------------------------------------------ kernel-level entries */
+/* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
+ * (external/ggml/src/ggml-quants.c:491-505). */
+B2D_API b2d_status b2d_q8_0_dequantize(b2d_ctx* ctx, const void* q8_dev, int64_t rows, int64_t k, float* out_dev,
+                               void* stream);
+
+/* Epilogue kinds of the tensor-core GEMM C = A * B^T (ggml_mul_mat(B, A),
+ * src/framework/modules/linear_module.cpp:73-108). */
+enum {
+    B2D_EPI_F32 = 0,    /* out_f32 = acc + bias */
+    B2D_EPI_CT = 1,     /* out_{f16|bf16} = acc + bias */
+    B2D_EPI_SWIGLU = 2, /* 256-col tiles [128 a | 128 l] -> out_ct[:, n/2] = silu(a) * l */
+    B2D_EPI_RESID = 3   /* resid += gate * (acc + bias) */
+};
+
+/* A [M, K] and B [N, K] are device fp16 (bf16 = 0) or bf16 (bf16 = 1) matrices.
+ * K % 64 == 0, N % bn == 0, bn in {64, 128, 256}.  bias/gate/resid may be NULL
+ * where unused. */
+B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
+                    int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
+                    float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200DIFF_H */

@@ -1,0 +1,446 @@
+// Test-infrastructure harness around the reference's own CPU implementation of
+// the diffusion hot path.  It links the unmodified audio.cpp translation units
+// (VibeVoice diffusion head / DPM-Solver++ scheduler / sampler, Stable Audio
+// Open 1.0 foundation DiT) and vendored ggml's CPU backend, feeds them weights
+// and inputs from a "B2DB" bundle file written by oracle/bundle.py, and writes
+// the reference's outputs (and wall-clock timings) back as a bundle.
+//
+// Commands (all inputs/outputs are bundles):
+//   q8     <in> <out>                      ggml_quantize_chunk(Q8_0) + dequantize of rows "x"
+//   vvsched <in> <out>                     VibeVoiceDPMSolverScheduler::step over given model outputs
+//   vvpredict <weights> <in> <out> <thr>   one VibeVoiceDiffusionHeadWeightsRuntime::predict
+//   vv <weights> <in> <out> <thr> <reps>   sample_vibevoice_speech_latents (whole step loop)
+//   dit <weights> <in> <out> <thr> <reps> FoundationRfDitRuntime::sample
+//
+// Reference entry points exercised (paths inside audio.cpp):
+//   include/engine/models/vibevoice/diffusion_sampler.h:23  sample_vibevoice_speech_latents
+//   include/engine/models/vibevoice/diffusion_head.h:58-97  VibeVoiceDiffusionHeadWeightsRuntime
+//   include/engine/models/vibevoice/scheduler.h:14-47       VibeVoiceDPMSolverScheduler
+//   include/engine/models/stable_audio/foundation/rf_dit.h:73-106 FoundationRfDitRuntime
+//   external/ggml/src/ggml-quants.c:234-257,491-505         Q8_0 quantize / dequantize
+
+#include "engine/framework/assets/tensor_source.h"
+#include "engine/framework/core/execution_context.h"
+#include "engine/framework/sampling/torch_random.h"
+#include "engine/models/stable_audio/foundation/rf_dit.h"
+#include "engine/models/vibevoice/diffusion_head.h"
+#include "engine/models/vibevoice/diffusion_sampler.h"
+#include "engine/models/vibevoice/scheduler.h"
+
+#include "engine/framework/io/yaml.h"
+
+#include <ggml.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace {
+
+// ---------------------------------------------------------------- bundle I/O
+// Layout: "B2DB" u32 version u32 count, then per entry
+//   u16 name_len, name, u8 dtype, u8 ndim, i64 dims[ndim], u64 nbytes, bytes.
+enum Dtype : uint8_t { F32 = 0, F16 = 1, BF16 = 2, Q8_0 = 3, I64 = 4, I32 = 5, U8 = 6 };
+
+struct Entry {
+    uint8_t dtype = F32;
+    std::vector<int64_t> dims;
+    std::vector<std::byte> bytes;
+};
+
+using Bundle = std::map<std::string, Entry>;
+
+template <typename T>
+void read_pod(std::ifstream & in, T & v) {
+    in.read(reinterpret_cast<char *>(&v), sizeof(T));
+    if (!in) throw std::runtime_error("bundle truncated");
+}
+
+Bundle read_bundle(const std::string & path) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) throw std::runtime_error("cannot open bundle " + path);
+    char magic[4];
+    in.read(magic, 4);
+    if (std::memcmp(magic, "B2DB", 4) != 0) throw std::runtime_error("bad bundle magic: " + path);
+    uint32_t version = 0, count = 0;
+    read_pod(in, version);
+    read_pod(in, count);
+    Bundle out;
+    for (uint32_t i = 0; i < count; ++i) {
+        uint16_t nlen = 0;
+        read_pod(in, nlen);
+        std::string name(nlen, '\0');
+        in.read(name.data(), nlen);
+        Entry e;
+        uint8_t ndim = 0;
+        read_pod(in, e.dtype);
+        read_pod(in, ndim);
+        e.dims.resize(ndim);
+        for (auto & d : e.dims) read_pod(in, d);
+        uint64_t nbytes = 0;
+        read_pod(in, nbytes);
+        e.bytes.resize(nbytes);
+        in.read(reinterpret_cast<char *>(e.bytes.data()), static_cast<std::streamsize>(nbytes));
+        if (!in) throw std::runtime_error("bundle truncated in " + name);
+        out.emplace(std::move(name), std::move(e));
+    }
+    return out;
+}
+
+void write_bundle(const std::string & path, const Bundle & b) {
+    std::ofstream out(path, std::ios::binary);
+    out.write("B2DB", 4);
+    const uint32_t version = 1, count = static_cast<uint32_t>(b.size());
+    out.write(reinterpret_cast<const char *>(&version), 4);
+    out.write(reinterpret_cast<const char *>(&count), 4);
+    for (const auto & [name, e] : b) {
+        const uint16_t nlen = static_cast<uint16_t>(name.size());
+        out.write(reinterpret_cast<const char *>(&nlen), 2);
+        out.write(name.data(), nlen);
+        out.write(reinterpret_cast<const char *>(&e.dtype), 1);
+        const uint8_t ndim = static_cast<uint8_t>(e.dims.size());
+        out.write(reinterpret_cast<const char *>(&ndim), 1);
+        for (int64_t d : e.dims) out.write(reinterpret_cast<const char *>(&d), 8);
+        const uint64_t nbytes = e.bytes.size();
+        out.write(reinterpret_cast<const char *>(&nbytes), 8);
+        out.write(reinterpret_cast<const char *>(e.bytes.data()), static_cast<std::streamsize>(nbytes));
+    }
+    if (!out) throw std::runtime_error("cannot write bundle " + path);
+}
+
+const Entry & need(const Bundle & b, const std::string & name) {
+    auto it = b.find(name);
+    if (it == b.end()) throw std::runtime_error("bundle lacks entry " + name);
+    return it->second;
+}
+
+std::vector<float> f32s(const Bundle & b, const std::string & name) {
+    const auto & e = need(b, name);
+    if (e.dtype != F32) throw std::runtime_error("entry is not f32: " + name);
+    std::vector<float> v(e.bytes.size() / 4);
+    std::memcpy(v.data(), e.bytes.data(), e.bytes.size());
+    return v;
+}
+
+std::vector<int64_t> i64s(const Bundle & b, const std::string & name) {
+    const auto & e = need(b, name);
+    if (e.dtype != I64) throw std::runtime_error("entry is not i64: " + name);
+    std::vector<int64_t> v(e.bytes.size() / 8);
+    std::memcpy(v.data(), e.bytes.data(), e.bytes.size());
+    return v;
+}
+
+float f32_scalar(const Bundle & b, const std::string & name) { return f32s(b, name).at(0); }
+int64_t i64_scalar(const Bundle & b, const std::string & name) { return i64s(b, name).at(0); }
+
+Entry f32_entry(const std::vector<float> & v, std::vector<int64_t> dims) {
+    Entry e;
+    e.dtype = F32;
+    e.dims = std::move(dims);
+    e.bytes.resize(v.size() * 4);
+    std::memcpy(e.bytes.data(), v.data(), e.bytes.size());
+    return e;
+}
+
+Entry raw_entry(uint8_t dtype, const void * p, size_t n, std::vector<int64_t> dims) {
+    Entry e;
+    e.dtype = dtype;
+    e.dims = std::move(dims);
+    e.bytes.resize(n);
+    std::memcpy(e.bytes.data(), p, n);
+    return e;
+}
+
+const char * dtype_name(uint8_t d) {
+    switch (d) {
+        case F32: return "f32";
+        case F16: return "f16";
+        case BF16: return "bf16";
+        case Q8_0: return "q8_0";
+        case I64: return "i64";
+        case I32: return "i32";
+        default: return "u8";
+    }
+}
+
+// ------------------------------------------------- in-memory tensor source
+// Serves a bundle's entries through the reference's TensorSource interface
+// (include/engine/framework/assets/tensor_source.h:59-120) so the reference's
+// own weight loaders and BackendWeightStore upload path run unchanged.
+class BundleTensorSource final : public engine::assets::TensorSource {
+public:
+    explicit BundleTensorSource(Bundle b) : bundle_(std::move(b)) {}
+
+    const std::filesystem::path & source_path() const noexcept override { return path_; }
+    bool has_tensor(std::string_view name) const noexcept override {
+        return bundle_.count(std::string(name)) != 0;
+    }
+    engine::assets::TensorMetadata require_metadata(std::string_view name) const override {
+        const auto & e = need(bundle_, std::string(name));
+        return {std::string(name), dtype_name(e.dtype), e.dims};
+    }
+    std::vector<engine::assets::TensorMetadata> tensors() const override {
+        std::vector<engine::assets::TensorMetadata> out;
+        for (const auto & [n, e] : bundle_) out.push_back({n, dtype_name(e.dtype), e.dims});
+        return out;
+    }
+    engine::assets::RawTensorData require_tensor_data(std::string_view name) const override {
+        const auto & e = need(bundle_, std::string(name));
+        return {{std::string(name), dtype_name(e.dtype), e.dims}, e.bytes};
+    }
+    std::vector<float> require_f32(
+        std::string_view name,
+        const std::optional<std::vector<int64_t>> & expected_shape) const override {
+        const auto & e = need(bundle_, std::string(name));
+        if (expected_shape && *expected_shape != e.dims) {
+            throw std::runtime_error("tensor shape mismatch for " + std::string(name));
+        }
+        return f32s(bundle_, std::string(name));
+    }
+    std::optional<std::vector<float>> optional_f32(
+        std::string_view name,
+        const std::optional<std::vector<int64_t>> & expected_shape) const override {
+        if (!has_tensor(name)) return std::nullopt;
+        return require_f32(name, expected_shape);
+    }
+    int64_t require_i64_scalar(std::string_view name) const override {
+        return i64_scalar(bundle_, std::string(name));
+    }
+
+private:
+    Bundle bundle_;
+    std::filesystem::path path_ = "bundle";
+};
+
+double now_ms() {
+    using namespace std::chrono;
+    return duration<double, std::milli>(steady_clock::now().time_since_epoch()).count();
+}
+
+// ----------------------------------------------------------- VibeVoice
+engine::models::vibevoice::VibeVoiceDiffusionHeadConfig head_config(const Bundle & in) {
+    engine::models::vibevoice::VibeVoiceDiffusionHeadConfig c;
+    c.hidden_size = i64_scalar(in, "hidden_size");
+    c.latent_size = i64_scalar(in, "latent_size");
+    c.head_layers = i64_scalar(in, "head_layers");
+    c.head_ffn_ratio = f32_scalar(in, "head_ffn_ratio");
+    c.rms_norm_eps = f32_scalar(in, "rms_norm_eps");
+    c.ddpm_num_steps = i64_scalar(in, "ddpm_num_steps");
+    c.ddpm_num_inference_steps = i64_scalar(in, "inference_steps");
+    c.ddpm_beta_schedule = "cosine";
+    c.diffusion_type = "ddpm";
+    c.prediction_type = "v_prediction";
+    return c;
+}
+
+std::shared_ptr<const engine::models::vibevoice::VibeVoiceAssets> head_assets(
+    const std::string & weights_path, const Bundle & in) {
+    auto assets = std::make_shared<engine::models::vibevoice::VibeVoiceAssets>();
+    assets->config.diffusion_head = head_config(in);
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(weights_path));
+    return assets;
+}
+
+int cmd_vvsched(const std::string & in_path, const std::string & out_path) {
+    const Bundle in = read_bundle(in_path);
+    auto cfg = head_config(in);
+    const int64_t steps = i64_scalar(in, "inference_steps");
+    auto sample = f32s(in, "sample");
+    const auto outputs = f32s(in, "model_outputs");
+    const size_t n = sample.size();
+    engine::models::vibevoice::VibeVoiceDPMSolverScheduler sched(cfg);
+    sched.set_timesteps(steps);
+    std::vector<float> trace;
+    std::vector<float> ts;
+    for (size_t s = 0; s < sched.timesteps().size(); ++s) {
+        std::vector<float> mo(outputs.begin() + static_cast<std::ptrdiff_t>(s * n),
+                              outputs.begin() + static_cast<std::ptrdiff_t>((s + 1) * n));
+        sample = sched.step(mo, sched.timesteps()[s], sample).prev_sample;
+        trace.insert(trace.end(), sample.begin(), sample.end());
+        ts.push_back(static_cast<float>(sched.timesteps()[s]));
+    }
+    Bundle out;
+    out["trace"] = f32_entry(trace, {steps, static_cast<int64_t>(n)});
+    out["timesteps"] = f32_entry(ts, {steps});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+int cmd_vvpredict(const std::string & w, const std::string & in_path, const std::string & out_path, int threads) {
+    const Bundle in = read_bundle(in_path);
+    auto assets = head_assets(w, in);
+    engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime head(
+        assets, engine::core::BackendType::Cpu, 0, threads);
+    const auto noisy = f32s(in, "noisy");
+    const auto cond = f32s(in, "condition");
+    const int64_t latent = assets->config.diffusion_head.latent_size;
+    const int64_t hidden = assets->config.diffusion_head.hidden_size;
+    const int64_t frames = static_cast<int64_t>(noisy.size()) / latent;
+    auto pred = head.predict(noisy, frames, latent, f32_scalar(in, "timestep"), cond, hidden);
+    Bundle out;
+    out["prediction"] = f32_entry(pred.values, {frames, latent});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+int cmd_vv(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+    const Bundle in = read_bundle(in_path);
+    auto assets = head_assets(w, in);
+    const auto & cfg = assets->config.diffusion_head;
+    engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime head(
+        assets, engine::core::BackendType::Cpu, 0, threads);
+    engine::models::vibevoice::VibeVoiceDPMSolverScheduler sched(cfg);
+    engine::models::vibevoice::VibeVoiceSpeechDiffusionInput input;
+    input.positive_condition = f32s(in, "positive_condition");
+    input.negative_condition = f32s(in, "negative_condition");
+    input.initial_speech = f32s(in, "initial_speech");
+    input.hidden_size = cfg.hidden_size;
+    input.latent_size = cfg.latent_size;
+    input.batch_size = static_cast<int64_t>(input.positive_condition.size()) / cfg.hidden_size;
+    input.inference_steps = i64_scalar(in, "inference_steps");
+    input.guidance_scale = f32_scalar(in, "guidance_scale");
+    sched.set_timesteps(input.inference_steps);
+    std::vector<float> times;
+    std::vector<float> latents;
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        const double t0 = now_ms();
+        auto result = engine::models::vibevoice::sample_vibevoice_speech_latents(head, sched, input);
+        times.push_back(static_cast<float>(now_ms() - t0));
+        latents.clear();
+        for (const auto & l : result) latents.insert(latents.end(), l.values.begin(), l.values.end());
+    }
+    Bundle out;
+    out["latents"] = f32_entry(latents, {input.batch_size, input.latent_size});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+// ---------------------------------------------------------- Stable Audio DiT
+int cmd_dit(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+    namespace sa = engine::models::stable_audio;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<sa::StableAudioAssets>();
+    auto & c = assets->config;
+    c.io_channels = i64_scalar(in, "io_channels");
+    c.embed_dim = i64_scalar(in, "embed_dim");
+    c.depth = i64_scalar(in, "depth");
+    c.num_heads = i64_scalar(in, "num_heads");
+    c.cond_token_dim = i64_scalar(in, "cond_token_dim");
+    c.global_cond_dim = i64_scalar(in, "global_cond_dim");
+    c.prompt_max_length = i64_scalar(in, "prompt_max_length");
+    c.stable_audio_open_v1 = true;
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
+
+    const int64_t batch = i64_scalar(in, "batch");
+    const int64_t tokens = i64_scalar(in, "latent_tokens");
+    const int64_t steps = i64_scalar(in, "steps");
+    sa::StableAudioSamplingState sampling;
+    sampling.batch = batch;
+    sampling.latent_sample_size = tokens;
+    sampling.channels = c.io_channels;
+    sampling.schedule_points = steps + 1;
+    sampling.schedule.assign(static_cast<size_t>(batch * (steps + 1)), 0.0F);
+    sampling.padding_mask = f32s(in, "padding_mask");
+    sampling.noise = f32s(in, "noise");
+
+    sa::StableAudioConditioningInputs cond;
+    const int64_t cross_tokens = c.prompt_max_length + 2;
+    cond.positive.batch = batch;
+    cond.positive.cross_tokens = cross_tokens;
+    cond.positive.cond_dim = c.cond_token_dim;
+    cond.positive.cross_attention = f32s(in, "cross_positive");
+    cond.positive.global = f32s(in, "global");
+    cond.has_negative = i64_scalar(in, "has_negative") != 0;
+    if (cond.has_negative) {
+        cond.negative = cond.positive;
+        cond.negative.cross_attention = f32s(in, "cross_negative");
+    }
+    const float cfg_scale = f32_scalar(in, "cfg_scale");
+    const float apg_scale = f32_scalar(in, "apg_scale");
+    const float sigma_min = f32_scalar(in, "sigma_min");
+    const float sigma_max = f32_scalar(in, "sigma_max");
+    const float rho = f32_scalar(in, "rho");
+
+    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    sa::foundation::FoundationRfDitRuntime dit(exec, assets, engine::assets::TensorStorageType::Native);
+    engine::sampling::TorchCudaSamplingPolicy policy;
+    std::vector<float> times;
+    std::vector<float> result;
+    dit.prepare(sampling, cfg_scale);
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        uint64_t offset = 0;
+        const double t0 = now_ms();
+        result = dit.sample(sampling, cond, 0, offset, policy, "dpmpp-2m", sigma_min, sigma_max, rho, cfg_scale, apg_scale);
+        times.push_back(static_cast<float>(now_ms() - t0));
+    }
+    Bundle out;
+    out["latents"] = f32_entry(result, {batch, c.io_channels, tokens});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+// ---------------------------------------------------------------- Q8_0 KAT
+int cmd_q8(const std::string & in_path, const std::string & out_path) {
+    const Bundle in = read_bundle(in_path);
+    const auto & e = need(in, "x");
+    const auto x = f32s(in, "x");
+    const int64_t cols = e.dims.back();
+    const int64_t rows = static_cast<int64_t>(x.size()) / cols;
+    std::vector<std::byte> q(static_cast<size_t>(rows) * ggml_row_size(GGML_TYPE_Q8_0, cols));
+    ggml_quantize_chunk(GGML_TYPE_Q8_0, x.data(), q.data(), 0, rows, cols, nullptr);
+    std::vector<float> deq(x.size());
+    const auto * traits = ggml_get_type_traits(GGML_TYPE_Q8_0);
+    for (int64_t r = 0; r < rows; ++r) {
+        traits->to_float(q.data() + r * ggml_row_size(GGML_TYPE_Q8_0, cols), deq.data() + r * cols, cols);
+    }
+    Bundle out;
+    out["q8"] = raw_entry(Q8_0, q.data(), q.size(), {rows, cols});
+    out["dequant"] = f32_entry(deq, {rows, cols});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+}  // namespace
+
+// ResourceBundle (linked in through the asset structs) references the YAML
+// parser; the harness never reads YAML, so libyaml is not linked and this
+// definition stands in for it.
+namespace engine::io::yaml {
+FlattenedDocument parse_flattened_document(std::string_view) {
+    throw std::runtime_error("YAML parsing is not available in the oracle harness");
+}
+}  // namespace engine::io::yaml
+
+int main(int argc, char ** argv) {
+    try {
+        if (argc < 2) {
+            std::fprintf(stderr, "usage: %s q8|vvsched|vvpredict|vv|dit ...\n", argv[0]);
+            return 2;
+        }
+        const std::string cmd = argv[1];
+        auto arg = [&](int i) -> std::string {
+            if (i >= argc) throw std::runtime_error("missing argument " + std::to_string(i));
+            return argv[i];
+        };
+        if (cmd == "q8") return cmd_q8(arg(2), arg(3));
+        if (cmd == "vvsched") return cmd_vvsched(arg(2), arg(3));
+        if (cmd == "vvpredict") return cmd_vvpredict(arg(2), arg(3), arg(4), std::stoi(arg(5)));
+        if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        std::fprintf(stderr, "unknown command %s\n", cmd.c_str());
+        return 2;
+    } catch (const std::exception & e) {
+        std::fprintf(stderr, "b2d_ref error: %s\n", e.what());
+        return 1;
+    }
+}

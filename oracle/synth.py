@@ -1,0 +1,257 @@
+"""Seeded synthetic weights and inputs for the hot-path configurations (test oracle).
+
+There are no real checkpoints or prompts in this environment; every config
+uses random-init weights of the reference architecture and random inputs with
+the shapes and distributions the configurations specify:
+
+* weights ~ N(0, 0.02) (seed ``wseed``), stored as F16 / BF16 / Q8_0 exactly as
+  the reference's weight store would encode them (RNE fp16, ggml's bf16
+  rounding, ``quantize_row_q8_0_ref``); RMSNorm weights / LayerNorm gamma =
+  1 + N(0, 0.02), LayerNorm beta = N(0, 0.02), kept in f32;
+* head conditions ~ N(0, 1) (seed 1), null condition = zeros, x_T ~ N(0, 1) (seed 2);
+* DiT: noise ~ N(0, 1), T5 states ~ N(0, 1), global ~ N(0, 1), per-prompt seeds.
+
+Tensor names and shapes follow the reference's loaders:
+``load_vibevoice_diffusion_head_weights`` (src/models/vibevoice/diffusion_head.cpp:335-399)
+and ``load_foundation_rf_dit_weights`` (src/models/stable_audio/foundation/rf_dit.cpp:379-416).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict
+
+import numpy as np
+
+from . import bundle as B
+from . import q8
+
+F16, BF16, Q8_0, F32 = "f16", "bf16", "q8_0", "f32"
+
+
+def _normal(rng: np.random.Generator, shape, std=1.0) -> np.ndarray:
+    return (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
+
+
+def encode_weight(w: np.ndarray, wtype: str) -> B.Tensor:
+    """Encode an fp32 [out, in(, 1)] weight in the stored type."""
+    dims = w.shape
+    flat2d = w.reshape(-1, dims[-1]) if len(dims) == 2 else w.reshape(dims[0], -1)
+    if wtype == F32:
+        return B.Tensor(B.F32, dims, w.reshape(-1))
+    if wtype == F16:
+        return B.Tensor(B.F16, dims, w.astype(np.float16).reshape(-1))
+    if wtype == BF16:
+        return B.Tensor(B.BF16, dims, q8.to_bf16_bits(w).reshape(-1))
+    if wtype == Q8_0:
+        return B.Tensor(B.Q8_0, dims, q8.quantize_q8_0(flat2d).reshape(-1))
+    raise ValueError(wtype)
+
+
+def decode_weight(t: B.Tensor) -> np.ndarray:
+    """Stored weight -> fp32 [out, in] (the values the reference computes with)."""
+    dims = t.dims
+    k = dims[1] if len(dims) >= 2 else dims[0]
+    rows = dims[0]
+    if t.dtype == B.F32:
+        return t.data.reshape(rows, -1).astype(np.float32)
+    if t.dtype == B.F16:
+        return t.data.reshape(rows, -1).astype(np.float32)
+    if t.dtype == B.BF16:
+        return q8.from_bf16_bits(t.data).reshape(rows, -1)
+    if t.dtype == B.Q8_0:
+        return q8.dequantize_q8_0(t.data, int(np.prod(dims[1:])))
+    raise ValueError(t.dtype)
+
+
+# --------------------------------------------------------------- VibeVoice head
+@dataclass
+class HeadConfig:
+    hidden: int = 1536
+    latent: int = 64
+    layers: int = 4
+    ffn_ratio: float = 3.0
+    eps: float = 1e-5
+    ddpm_num_steps: int = 1000
+    wtype: str = F16
+    frames: int = 64
+    steps: int = 10
+    cfg: float = 1.3
+    wseed: int = 0
+    cseed: int = 1
+    xseed: int = 2
+
+    @property
+    def ffn(self) -> int:
+        return int(float(self.hidden) * self.ffn_ratio)
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        return {
+            "hidden_size": B.i64(self.hidden), "latent_size": B.i64(self.latent),
+            "head_layers": B.i64(self.layers), "head_ffn_ratio": B.f32(self.ffn_ratio),
+            "rms_norm_eps": B.f32(self.eps), "ddpm_num_steps": B.i64(self.ddpm_num_steps),
+            "inference_steps": B.i64(self.steps), "guidance_scale": B.f32(self.cfg),
+        }
+
+
+HEAD_CONFIGS = {
+    # BASELINE configs (C1, C2, C5)
+    "vv15_f16_64": HeadConfig(wtype=F16, frames=64),
+    "vv15_q8_1024": HeadConfig(wtype=Q8_0, frames=1024),
+    "vv7_q8_8192": HeadConfig(hidden=3584, wtype=Q8_0, frames=8192),
+    # small parity configs
+    "tiny_f16": HeadConfig(hidden=256, wtype=F16, frames=8),
+    "tiny_q8": HeadConfig(hidden=256, wtype=Q8_0, frames=8),
+    "tiny_bf16": HeadConfig(hidden=256, wtype=BF16, frames=5),
+    "small_q8_ragged": HeadConfig(hidden=512, wtype=Q8_0, frames=100, steps=5),
+    "one_frame_f16": HeadConfig(hidden=256, wtype=F16, frames=1, steps=3),
+    "one_step_q8": HeadConfig(hidden=256, wtype=Q8_0, frames=4, steps=1, cfg=1.0),
+}
+
+HP = "model.prediction_head."
+
+
+def head_weights(cfg: HeadConfig) -> Dict[str, B.Tensor]:
+    rng = np.random.default_rng(cfg.wseed)
+    H, F, L = cfg.hidden, cfg.ffn, cfg.latent
+    w: Dict[str, B.Tensor] = {}
+
+    def lin(name, out, inp):
+        w[HP + name + ".weight"] = encode_weight(_normal(rng, (out, inp), 0.02), cfg.wtype)
+
+    lin("noisy_images_proj", H, L)
+    lin("cond_proj", H, H)
+    lin("t_embedder.mlp.0", H, 256)
+    lin("t_embedder.mlp.2", H, H)
+    for i in range(cfg.layers):
+        p = "layers.%d." % i
+        lin(p + "ffn.gate_proj", F, H)
+        lin(p + "ffn.up_proj", F, H)
+        lin(p + "ffn.down_proj", H, F)
+        w[HP + p + "norm.weight"] = B.f32(1.0 + _normal(rng, (H,), 0.02))
+        lin(p + "adaLN_modulation.1", 3 * H, H)
+    lin("final_layer.adaLN_modulation.1", 2 * H, H)
+    lin("final_layer.linear", L, H)
+    return w
+
+
+def head_inputs(cfg: HeadConfig) -> Dict[str, B.Tensor]:
+    cond = _normal(np.random.default_rng(cfg.cseed), (cfg.frames, cfg.hidden))
+    x0 = _normal(np.random.default_rng(cfg.xseed), (2 * cfg.frames, cfg.latent))
+    d = cfg.scalars()
+    d["positive_condition"] = B.f32(cond)
+    d["negative_condition"] = B.f32(np.zeros_like(cond))
+    d["initial_speech"] = B.f32(x0)
+    return d
+
+
+# ----------------------------------------------------------- Stable Audio DiT
+@dataclass
+class DitConfig:
+    embed_dim: int = 1536
+    depth: int = 24
+    num_heads: int = 24
+    cond_token_dim: int = 768
+    global_cond_dim: int = 1536
+    io_channels: int = 64
+    prompt_max_length: int = 128
+    latent_tokens: int = 1024
+    batch: int = 1
+    steps: int = 100
+    cfg: float = 7.0
+    apg: float = 1.0
+    sigma_min: float = 0.01
+    sigma_max: float = 100.0
+    rho: float = 1.0
+    wtype: str = BF16
+    wseed: int = 0
+    prompt_seeds: tuple = field(default_factory=lambda: (0,))
+
+    @property
+    def head_dim(self) -> int:
+        return self.embed_dim // self.num_heads
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        return {k: B.i64(getattr(self, k)) for k in (
+            "io_channels", "embed_dim", "depth", "num_heads", "cond_token_dim", "global_cond_dim",
+            "prompt_max_length", "latent_tokens", "batch", "steps")} | {
+            k + "": B.f32(getattr(self, a)) for k, a in (
+                ("cfg_scale", "cfg"), ("apg_scale", "apg"), ("sigma_min", "sigma_min"),
+                ("sigma_max", "sigma_max"), ("rho", "rho"))}
+
+
+DIT_CONFIGS = {
+    "sao_bf16_1x1024": DitConfig(),
+    "sao_q8_16x1024": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16))),
+    "tiny_bf16": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
+                           prompt_max_length=14, latent_tokens=64, steps=6),
+    "tiny_q8_b2_noapg": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
+                                  prompt_max_length=14, latent_tokens=48, steps=5, batch=2, apg=0.0,
+                                  wtype=Q8_0, prompt_seeds=(3, 4)),
+    "tiny_f16_ragged": DitConfig(embed_dim=256, depth=1, num_heads=4, cond_token_dim=128, global_cond_dim=256,
+                                 prompt_max_length=14, latent_tokens=37, steps=4, wtype=F16),
+}
+
+DP = "model.model."
+
+
+def dit_weights(cfg: DitConfig) -> Dict[str, B.Tensor]:
+    rng = np.random.default_rng(cfg.wseed)
+    d, C, c = cfg.embed_dim, cfg.io_channels, cfg.cond_token_dim
+    w: Dict[str, B.Tensor] = {}
+
+    def lin(name, out, inp, bias=False, conv=False):
+        shape = (out, inp, 1) if conv else (out, inp)
+        w[DP + name + ".weight"] = encode_weight(_normal(rng, shape, 0.02), cfg.wtype)
+        if bias:
+            w[DP + name + ".bias"] = B.f32(_normal(rng, (out,), 0.02))
+
+    w[DP + "timestep_features.weight"] = B.f32(_normal(rng, (128, 1)))
+    lin("to_cond_embed.0", c, c)
+    lin("to_cond_embed.2", c, c)
+    lin("to_global_embed.0", d, cfg.global_cond_dim)
+    lin("to_global_embed.2", d, d)
+    lin("to_timestep_embed.0", d, 256, bias=True)
+    lin("to_timestep_embed.2", d, d, bias=True)
+    lin("preprocess_conv", C, C, conv=True)
+    lin("postprocess_conv", C, C, conv=True)
+    lin("transformer.project_in", d, C)
+    lin("transformer.project_out", C, d)
+    for i in range(cfg.depth):
+        p = "transformer.layers.%d." % i
+        for n in ("pre_norm", "cross_attend_norm", "ff_norm"):
+            w[DP + p + n + ".gamma"] = B.f32(1.0 + _normal(rng, (d,), 0.02))
+            w[DP + p + n + ".beta"] = B.f32(_normal(rng, (d,), 0.02))
+        lin(p + "self_attn.to_qkv", 3 * d, d)
+        lin(p + "self_attn.to_out", d, d)
+        lin(p + "cross_attn.to_q", d, d)
+        lin(p + "cross_attn.to_kv", 2 * c, c)
+        lin(p + "cross_attn.to_out", d, d)
+        lin(p + "ff.ff.0.proj", 8 * d, d, bias=True)
+        lin(p + "ff.ff.2", d, 4 * d, bias=True)
+    return w
+
+
+def dit_inputs(cfg: DitConfig) -> Dict[str, B.Tensor]:
+    """Per prompt b (seed s_b): noise [64, T], T5 states [P, c] + the two c-halves of a
+    global vector as the 2 number tokens, global [global_cond_dim]; negative cross = zeros."""
+    Bn, T, C, c = cfg.batch, cfg.latent_tokens, cfg.io_channels, cfg.cond_token_dim
+    P = cfg.prompt_max_length
+    noise = np.zeros((Bn, C, T), np.float32)
+    cross = np.zeros((Bn, P + 2, c), np.float32)
+    glob = np.zeros((Bn, cfg.global_cond_dim), np.float32)
+    for b, s in enumerate(cfg.prompt_seeds[:Bn]):
+        rng = np.random.default_rng(1000 + s)
+        noise[b] = _normal(rng, (C, T))
+        cross[b, :P] = _normal(rng, (P, c))
+        g = _normal(rng, (cfg.global_cond_dim,))
+        glob[b] = g
+        cross[b, P] = g[:c]
+        cross[b, P + 1] = g[c:2 * c] if cfg.global_cond_dim >= 2 * c else g[:c]
+    d = cfg.scalars()
+    d["noise"] = B.f32(noise)
+    d["cross_positive"] = B.f32(cross)
+    d["cross_negative"] = B.f32(np.zeros_like(cross))
+    d["global"] = B.f32(glob)
+    d["padding_mask"] = B.f32(np.ones((Bn, T), np.float32))
+    d["has_negative"] = B.i64(1)
+    return d

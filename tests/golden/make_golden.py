@@ -1,0 +1,109 @@
+"""Generates the golden fixtures in this directory by running the reference's
+own CPU implementation (oracle/_ref/b2d_ref_v4: audio.cpp's unmodified hot-path
+sources + vendored ggml CPU backend, AVX-512 build with fp32 dot-product
+accumulation) on the seeded synthetic configurations of oracle/synth.py.
+
+Each fixture <name>.b2db holds the reference outputs plus ``input_sha256``
+(a digest of the weight and input bundles) so a test can detect drift in the
+synthetic generator before comparing.  Run from the repo root:
+
+    python tests/golden/make_golden.py [names...]
+
+It needs oracle/_ref built (make -C oracle/ref REF=<audio.cpp> VARIANT=v4).
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+os.environ.setdefault("B2D_REF_VARIANT", "v4")
+
+from oracle import bundle as B  # noqa: E402
+from oracle import ref_runner, synth  # noqa: E402
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_frame_f16", "one_step_q8",
+                "vv15_f16_64", "vv15_q8_1024"]
+DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged"]
+
+
+def digest(*bundles) -> np.ndarray:
+    h = hashlib.sha256()
+    for b in bundles:
+        for name in sorted(b):
+            t = b[name]
+            h.update(name.encode())
+            h.update(bytes([t.dtype]))
+            h.update(np.asarray(t.dims, np.int64).tobytes())
+            h.update(t.data.tobytes())
+    return np.frombuffer(h.digest(), dtype=np.uint8).copy()
+
+
+def head_golden(name: str) -> None:
+    cfg = synth.HEAD_CONFIGS[name]
+    w, inp = synth.head_weights(cfg), synth.head_inputs(cfg)
+    out = ref_runner.run("vv", inp, w)
+    fixture = {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))}
+    B.write(os.path.join(HERE, "head_%s.b2db" % name), fixture)
+    print("head", name, "ok", out["latents"].dims)
+
+
+def sched_golden() -> None:
+    rng = np.random.default_rng(7)
+    for steps in (1, 2, 10, 20):
+        n = 96
+        sample = rng.standard_normal(n).astype(np.float32)
+        outs = rng.standard_normal((steps, n)).astype(np.float32)
+        inp = synth.HeadConfig(steps=steps).scalars()
+        inp.update({"sample": B.f32(sample), "model_outputs": B.f32(outs)})
+        out = ref_runner.run("vvsched", inp)
+        B.write(os.path.join(HERE, "sched_%d.b2db" % steps),
+                {"sample": B.f32(sample), "model_outputs": B.f32(outs), "trace": out["trace"],
+                 "timesteps": out["timesteps"]})
+        print("sched", steps, "ok")
+
+
+def q8_golden() -> None:
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((16, 256)) * 0.05).astype(np.float32)
+    x[0, :32] = 0.0                      # all-zero block (d = 0)
+    x[1, :32] = np.linspace(-1, 1, 32)   # exact ties around +-0.5 after scaling
+    x[2, 7] = 40.0                       # outlier dominating its block
+    x[3, :] = -x[3, :]
+    out = ref_runner.run("q8", {"x": B.f32(x)})
+    B.write(os.path.join(HERE, "q8_kat.b2db"), {"x": B.f32(x), "q8": out["q8"], "dequant": out["dequant"]})
+    print("q8 ok")
+
+
+def dit_golden(name: str) -> None:
+    cfg = synth.DIT_CONFIGS[name]
+    w, inp = synth.dit_weights(cfg), synth.dit_inputs(cfg)
+    out = ref_runner.run("dit", inp, w)
+    B.write(os.path.join(HERE, "dit_%s.b2db" % name),
+            {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("dit", name, "ok", out["latents"].dims)
+
+
+def main(argv) -> None:
+    names = argv or ["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS]
+    for n in names:
+        if n == "q8":
+            q8_golden()
+        elif n == "sched":
+            sched_golden()
+        elif n.startswith("head:"):
+            head_golden(n[5:])
+        elif n.startswith("dit:"):
+            dit_golden(n[4:])
+        else:
+            raise SystemExit("unknown fixture " + n)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
