@@ -1,0 +1,290 @@
+"""Benchmark of the diffusion denoising hot path on B200.
+
+Workload: VibeVoice-1.5B diffusion head, Q8_0 weights
+(random N(0, 0.02), seeded), 1024 frames per call with CFG pairs (2048 head
+rows), conditions N(0,1) [1024, 1536], null condition zeros, x_T N(0,1),
+10-step DPM-Solver++(2M), CFG 1.3.  One "step" = one whole sampling call
+(sample_vibevoice_speech_latents).  Metric: latent frames/s (CFG rows not
+counted), whole job over all ranks.  N GPUs: one process per GPU, each samples
+its own 1024 frames (weak scaling, no collective on the data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "latent frames/sec (VibeVoice diffusion head)"
+UNIT = "frames/s"
+WORKLOAD = "vv15_q8_1024"
+
+
+def load_package():
+    if "audiocpp_b200" in sys.modules:
+        return sys.modules["audiocpp_b200"]
+    spec = importlib.util.spec_from_file_location("audiocpp_b200", os.path.join(ROOT, "audio.cpp_b200", "__init__.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["audiocpp_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def config_json(cfg, n, extra=None):
+    d = {"workload": WORKLOAD, "model": "VibeVoice-1.5B diffusion head (random-init)", "weights": cfg.wtype,
+         "frames_per_rank": cfg.frames, "head_rows_per_rank": 2 * cfg.frames, "hidden": cfg.hidden,
+         "layers": cfg.layers, "ffn": cfg.ffn, "latent": cfg.latent, "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg,
+         "global_batch_frames": cfg.frames * n, "parallelism": "dp%d (independent frames per GPU)" % n,
+         "l2": "flushed (256 MiB write) before every timed call"}
+    if extra:
+        d.update(extra)
+    return d
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, device: int):
+        self.device, self.samples, self.proc = device, [], None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + q,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": float(self.samples[0][1]),
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def run_cpu_reference(cfg, frames, reps, threads):
+    """The reference's own CPU implementation (oracle/_ref) on `frames` frames of the workload."""
+    from oracle import ref_runner, synth
+    sub = synth.HeadConfig(**{**cfg.__dict__, "frames": frames})
+    inp = synth.head_inputs(sub)
+    w = synth.head_weights(sub)
+    out = ref_runner.run("vv", inp, w, threads=threads, reps=reps)
+    ms = out["wall_ms"].data
+    return ms, ref_runner.variant()
+
+
+def bench_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from oracle import ref_runner, synth
+    cfg = synth.HEAD_CONFIGS[WORKLOAD]
+    threads = os.cpu_count() or 1
+    frames = 128  # bounded sample of the 1024-frame workload (same weights, 10 steps, CFG)
+    if not ref_runner.available():
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) not present"}))
+        return
+    ms, variant = run_cpu_reference(cfg, frames, args.warmup + args.steps, threads)
+    timed = np.array(ms[args.warmup:], np.float64)
+    value = frames / (timed.mean() / 1e3)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": float(timed.mean()), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 graph, Q8_0 weights (ggml CPU)", "data": "synthetic",
+            "impl": "reference",
+            "config": config_json(cfg, 1, {"sample_frames": frames}),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": "%d frames x %d DPM steps x CFG per call, audio.cpp ggml CPU build (%s)" % (
+                                 frames, cfg.steps, variant)},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def gemm_roofline(b2d, ctx, torch, cfg, peaks):
+    """Times the dominant kernel (FFN gate/up GEMM + SwiGLU epilogue, 2048 x 9216 x 1536) with CUDA events."""
+    M, K, N = 2 * cfg.frames, cfg.hidden, 2 * cfg.ffn
+    a = torch.randn(M, K, device="cuda").half()
+    w = (torch.randn(N, K, device="cuda") * 0.02).half()
+    out = torch.empty(M, N // 2, device="cuda", dtype=torch.float16)
+    st = torch.cuda.current_stream()
+    launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, epilogue=b2d.EPI_SWIGLU, bn=256,
+                              out=out.data_ptr(), ldo=N // 2, stream=st.cuda_stream)
+    for _ in range(5):
+        launch()
+    torch.cuda.synchronize()
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        launch()
+    e1.record(st)
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / reps / 1e3
+    flops = 2.0 * M * N * K
+    achieved = flops / dt / 1e12
+    peak = peaks.get("bf16_tflops", 1590.0)
+    return {"kernel": "gemm_tc_kernel<256,SWIGLU,half> (FFN gate/up, %dx%dx%d)" % (M, N, K), "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS)" if "bf16_tflops" in peaks
+            else "fallback 1590", "launch_us": round(dt * 1e6, 2), "flop_per_launch": flops,
+            "traffic": None}
+
+
+def bench_ours(args):
+    import torch
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    b2d = load_package()
+    from oracle import synth  # seeded synthetic weights/inputs (no checkpoints here)
+    cfg = synth.HEAD_CONFIGS[WORKLOAD]
+    w = synth.head_weights(cfg)
+    inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
+    gt = {0: 0, 1: 1, 3: 8, 2: 30}
+    ctx = b2d.Context(local)
+    head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
+                                      weights=[(n, gt[t.dtype], t.dims, t.data) for n, t in w.items()])
+    del w
+    st = torch.cuda.current_stream()
+    dev = [torch.from_numpy(inp[k].array().copy()).cuda() for k in ("positive_condition", "negative_condition",
+                                                                    "initial_speech")]
+    host = [torch.from_numpy(inp[k].array().copy()).pin_memory() for k in ("positive_condition",
+                                                                            "negative_condition", "initial_speech")]
+    out_dev = torch.empty(cfg.frames, 64, device="cuda")
+    out_host = torch.empty(cfg.frames, 64).pin_memory()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(call):
+        for _ in range(args.warmup):
+            call()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            call()
+            e1.record(st)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(total / args.steps)
+
+    dev_call = lambda: head.sample_device(*dev, cfg.steps, cfg.cfg, out_dev, stream=st.cuda_stream)
+    host_call = lambda: head.sample(*host, cfg.steps, cfg.cfg, out=out_host, stream=st.cuda_stream)
+    with ClockSampler(local) as clk:
+        ms = timed(dev_call)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(host_call)
+    assert np.isfinite(out_host.numpy()).all()
+
+    frames_total = cfg.frames * world
+    value = frames_total / (ms / 1e3)
+    e2e = frames_total / (ms_e2e / 1e3)
+    h2d = sum(t.numel() * 4 for t in host)
+    d2h = out_host.numel() * 4
+    launches_per_call = 5 + cfg.steps * (3 * cfg.layers + 6)
+
+    if rank == 0:
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except (OSError, ValueError):
+            peaks = {}
+        roof = gemm_roofline(b2d, ctx, torch, cfg, peaks)
+        flops_call = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
+        line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16 tensor-core operands (Q8_0 dequantised), fp32 accumulate",
+                "data": "synthetic (seeded random weights and inputs)",
+                "config": config_json(cfg, world),
+                "e2e": {"value": round(e2e, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "ms_per_step": round(ms_e2e, 4), "api": "b2d_vv_sample (host buffers, pinned)"},
+                "gpu_launches": launches_per_call * args.steps,
+                "roofline": roof,
+                "whole_call_tflops": round(flops_call / (ms / 1e3) / 1e12, 1),
+                "clocks": clk.summary()}
+        if not args.no_cpu_baseline:
+            frames = 128
+            cms, variant = run_cpu_reference(cfg, frames, 2, os.cpu_count() or 1)
+            v = frames / (float(np.mean(cms[1:])) / 1e3)
+            line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
+                                    "sample": "%d of the 1024 frames, 10 DPM steps + CFG, audio.cpp ggml CPU (%s), "
+                                              "1 warm-up + 1 timed call" % (frames, variant)}
+        print(json.dumps(line))
+    ctx.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        bench_reference(args)
+    else:
+        bench_ours(args)
+
+
+if __name__ == "__main__":
+    main()

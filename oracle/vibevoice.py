@@ -42,15 +42,21 @@ def round_activations(x: np.ndarray, wdtype: int) -> np.ndarray:
 
 
 class Linear:
-    """y = x W^T with ggml CPU activation rounding (LinearModule::build, src/framework/modules/linear_module.cpp:73-108)."""
+    """y = x W^T (LinearModule::build, src/framework/modules/linear_module.cpp:73-108).
 
-    def __init__(self, t: B.Tensor, bias: np.ndarray | None = None):
+    act="ggml" rounds activations like ggml's CPU matmul; act="exact" keeps them
+    fp32, which is the arithmetic the reference graph specifies and the GPU path
+    approximates (fp16/bf16 operands, fp32 accumulation)."""
+
+    def __init__(self, t: B.Tensor, bias: np.ndarray | None = None, act: str = "ggml"):
         self.dtype = t.dtype
         self.w = decode_weight(t).astype(np.float64)
         self.b = bias
+        self.act = act
 
     def __call__(self, x: np.ndarray) -> np.ndarray:
-        xr = round_activations(np.ascontiguousarray(x, np.float32), self.dtype)
+        x = np.ascontiguousarray(x, np.float32)
+        xr = round_activations(x, self.dtype) if self.act == "ggml" else x
         y = (xr.astype(np.float64) @ self.w.T).astype(np.float32)
         if self.b is not None:
             y = (y + self.b).astype(np.float32)
@@ -75,22 +81,23 @@ def timestep_freqs() -> np.ndarray:
 class Head:
     """VibeVoiceDiffusionHeadWeightsRuntime::predict restated (diffusion_head.cpp:474-493)."""
 
-    def __init__(self, weights: Dict[str, B.Tensor], cfg: HeadConfig):
+    def __init__(self, weights: Dict[str, B.Tensor], cfg: HeadConfig, act: str = "ggml"):
         self.cfg = cfg
-        g = lambda n: weights[HP + n + ".weight"]
-        self.noisy = Linear(g("noisy_images_proj"))
-        self.cond = Linear(g("cond_proj"))
-        self.t1 = Linear(g("t_embedder.mlp.0"))
-        self.t2 = Linear(g("t_embedder.mlp.2"))
+        def lin(name):
+            return Linear(weights[HP + name + ".weight"], act=act)
+
+        self.noisy = lin("noisy_images_proj")
+        self.cond = lin("cond_proj")
+        self.t1 = lin("t_embedder.mlp.0")
+        self.t2 = lin("t_embedder.mlp.2")
         self.layers = []
         for i in range(cfg.layers):
             p = "layers.%d." % i
             self.layers.append(dict(
-                gate=Linear(g(p + "ffn.gate_proj")), up=Linear(g(p + "ffn.up_proj")),
-                down=Linear(g(p + "ffn.down_proj")), norm=weights[HP + p + "norm.weight"].data.astype(np.float32),
-                ada=Linear(g(p + "adaLN_modulation.1"))))
-        self.fada = Linear(g("final_layer.adaLN_modulation.1"))
-        self.flin = Linear(g("final_layer.linear"))
+                gate=lin(p + "ffn.gate_proj"), up=lin(p + "ffn.up_proj"), down=lin(p + "ffn.down_proj"),
+                norm=weights[HP + p + "norm.weight"].data.astype(np.float32), ada=lin(p + "adaLN_modulation.1")))
+        self.fada = lin("final_layer.adaLN_modulation.1")
+        self.flin = lin("final_layer.linear")
         self.freqs = timestep_freqs()
 
     def t_embedding(self, t: float, rows: int) -> np.ndarray:

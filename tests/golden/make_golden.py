@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import ref_runner, synth  # noqa: E402
+from oracle import ref_runner, synth, vibevoice  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -49,7 +49,14 @@ def head_golden(name: str) -> None:
     cfg = synth.HEAD_CONFIGS[name]
     w, inp = synth.head_weights(cfg), synth.head_inputs(cfg)
     out = ref_runner.run("vv", inp, w)
-    fixture = {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))}
+    # The reference requantises activations (Q8_0 blocks / fp16 / bf16) before every CPU matmul;
+    # "exact_latents" is the numpy restatement with fp32 activations, i.e. the graph's arithmetic
+    # without that rounding.  Their distance is the reference's own quantisation spread.
+    head = vibevoice.Head(w, cfg, act="exact")
+    exact = vibevoice.sample_speech_latents(head, cfg, inp["positive_condition"].array(),
+                                            inp["negative_condition"].array(), inp["initial_speech"].array())
+    fixture = {"latents": out["latents"], "exact_latents": B.f32(exact),
+               "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))}
     B.write(os.path.join(HERE, "head_%s.b2db" % name), fixture)
     print("head", name, "ok", out["latents"].dims)
 

@@ -1,7 +1,15 @@
 """GPU parity of the VibeVoice diffusion head + DPM-Solver++ sampler, called through
 the C ABI, against the reference's own ggml CPU outputs (tests/golden) and the
-numpy oracle.  Tolerance: final latents within rel-L2 1e-2 (fp16/bf16 tensor-core
-operands, fp32 accumulation) of the reference."""
+numpy oracle.
+
+Tolerances (final latents, rel-L2):
+  * vs the reference: max(1e-2, 1.5 x spread), where spread = distance between the
+    reference and the same arithmetic without its activation requantisation
+    (``exact_latents``).  ggml's CPU matmul rounds activations to Q8_0 blocks before
+    every Q8_0 dot product; at 1024 frames x 10 steps that alone moves the latents
+    1.7 %, so 1e-2 is below the reference's own noise floor there.
+  * vs ``exact_latents`` (fp32 activations): 3e-3 for fp16 operands, 1e-2 for bf16.
+"""
 import numpy as np
 import pytest
 
@@ -35,10 +43,14 @@ def test_sample_matches_reference(b2d, ctx, name):
     inp = synth.head_inputs(cfg)
     out = head.sample(inp["positive_condition"].array(), inp["negative_condition"].array(),
                       inp["initial_speech"].array(), cfg.steps, cfg.cfg)
-    ref = golden("head_" + name)["latents"].array()
+    g = golden("head_" + name)
+    ref, exact = g["latents"].array(), g["exact_latents"].array()
     assert np.isfinite(out).all()
+    spread = rel_l2(exact, ref)
     err = rel_l2(out, ref)
-    assert err < LATENT_TOL, "rel-L2 %.3g vs reference" % err
+    assert err < max(LATENT_TOL, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
+    err_exact = rel_l2(out, exact)
+    assert err_exact < (1e-2 if cfg.wtype == synth.BF16 else 3e-3), "rel-L2 %.3g vs exact oracle" % err_exact
     # graph replay gives identical results
     out2 = head.sample(inp["positive_condition"].array(), inp["negative_condition"].array(),
                        inp["initial_speech"].array(), cfg.steps, cfg.cfg)
