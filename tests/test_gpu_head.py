@@ -65,8 +65,8 @@ def test_predict_matches_port(b2d, ctx, name):
     noisy = rng.standard_normal((frames, 64)).astype(np.float32)
     cond = rng.standard_normal((frames, cfg.hidden)).astype(np.float32)
     out = head.predict(noisy, 571.0, cond)
-    ref = V.Head(w, cfg).predict(noisy, 571.0, cond)
-    assert rel_l2(out, ref) < 5e-3
+    ref = V.Head(w, cfg, act="exact").predict(noisy, 571.0, cond)
+    assert rel_l2(out, ref) < 3e-3
 
 
 def test_sample_after_predict_and_batch_change(b2d, ctx):
