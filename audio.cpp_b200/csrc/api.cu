@@ -120,7 +120,10 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
                                 int(S::SMEM_BYTES)));
         configured = true;
     }
-    const int64_t tiles = ((M + 127) / 128) * (N / BN);
+    const int splits = ep.splits > 1 ? ep.splits : 1;
+    if ((K / 64) % splits) fail(B2D_EINVAL, "split-K %d does not divide the %lld K blocks", splits, (long long)(K / 64));
+    if (splits > 1 && EPI != EPI_F32) fail(B2D_EINVAL, "split-K needs the fp32 partial-output epilogue");
+    const int64_t tiles = ((M + 127) / 128) * (N / BN) * splits;
     if (tiles == 0) return;
     const int grid = int(tiles < num_sms ? tiles : num_sms);
     gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, int(M), int(N), int(K), ep);
@@ -137,10 +140,17 @@ void launch_gemm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
         return;                                                          \
     }
     B2D_G(256, EPI_F32) B2D_G(256, EPI_CT) B2D_G(256, EPI_SWIGLU) B2D_G(256, EPI_RESID)
+    B2D_G(192, EPI_F32) B2D_G(192, EPI_CT) B2D_G(192, EPI_RESID)
     B2D_G(128, EPI_F32) B2D_G(128, EPI_CT) B2D_G(128, EPI_RESID)
     B2D_G(64, EPI_F32) B2D_G(64, EPI_CT) B2D_G(64, EPI_RESID)
 #undef B2D_G
     fail(B2D_EINVAL, "unsupported GEMM tile %d / epilogue %d", bn, epi);
+}
+
+// Fraction of the SM-slots a tile count keeps busy over its waves.
+double waves_eff(int64_t tiles, int sms) {
+    const int64_t waves = (tiles + sms - 1) / sms;
+    return waves == 0 ? 0.0 : double(tiles) / double(waves * sms);
 }
 
 int grid_for(int64_t n, int threads, int num_sms) {
@@ -234,8 +244,9 @@ constexpr int kHeadLatent = 64;
 
 struct HeadWorkspace {
     int64_t batch = 0;  // B; GEMM rows = 2B
-    DevBuf x, cp, sc, ada, h, ffn, v, noisy, cond, cond_ct, init, xstate, hist0, hist1, out, temb, h1, tsteps, coefs, ptstep;
-    CUtensorMap tm_noisy, tm_cond, tm_sc, tm_h, tm_ffn;
+    DevBuf x, cp, sc, ada, h, ffn, v, noisy, cond, cond_ct, init, xstate, hist0, hist1, out, temb, h1, tsteps, coefs, ptstep, vpart, feat_ct, h1pre, h1_ct;
+    int final_splits = 1;
+    CUtensorMap tm_noisy, tm_cond, tm_sc, tm_h, tm_ffn, tm_feat, tm_h1;
     std::map<std::tuple<int64_t, uint32_t>, cudaGraphExec_t> graphs;  // (steps, cfg bits) -> graph
     ~HeadWorkspace() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
@@ -248,8 +259,8 @@ struct HeadModel {
     bool bf16 = false;
     DevBuf w_in, w_cond, w_t1, w_t2, w_ada, w_final, norms;
     std::vector<DevBuf> w_gu, w_down;
-    CUtensorMap tm_in, tm_cond, tm_ada, tm_final;
-    std::vector<CUtensorMap> tm_gu, tm_down;
+    CUtensorMap tm_in, tm_cond, tm_ada, tm_final, tm_t1, tm_t2;
+    std::vector<CUtensorMap> tm_gu, tm_down256, tm_down192;
     std::unique_ptr<HeadWorkspace> ws;
 };
 
@@ -362,11 +373,15 @@ void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
     m.tm_cond = make_tmap(m.w_cond.p, bf, H, H, 256);
     m.tm_ada = make_tmap(m.w_ada.p, bf, m.NADA, H, 256);
     m.tm_final = make_tmap(m.w_final.p, bf, kHeadLatent, H, 64);
+    m.tm_t1 = make_tmap(m.w_t1.p, bf, H, 256, 256);
+    m.tm_t2 = make_tmap(m.w_t2.p, bf, H, H, 256);
     m.tm_gu.clear();
-    m.tm_down.clear();
+    m.tm_down256.clear();
+    m.tm_down192.clear();
     for (int64_t l = 0; l < L; ++l) {
         m.tm_gu.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 256));
-        m.tm_down.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 256));
+        m.tm_down256.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 256));
+        if (H % 192 == 0) m.tm_down192.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 192));
     }
 }
 
@@ -399,7 +414,24 @@ HeadWorkspace& head_workspace(b2d_ctx* ctx, HeadModel& m, int64_t batch) {
     ws->tsteps.alloc(size_t(kMaxTembSteps) * 4);
     ws->coefs.alloc(size_t(kMaxTembSteps) * sizeof(VvStepCoef));
     ws->ptstep.alloc(256);
+    // final projection (N = 64) runs split-K: as many K ranges as keep the SMs busy
+    {
+        const int64_t tiles = (R + 127) / 128, kb = H / 64;
+        int sp = 1;
+        for (int c = 8; c >= 1; --c)
+            if (kb % c == 0 && tiles * c <= ctx->num_sms) {
+                sp = c;
+                break;
+            }
+        ws->final_splits = sp;
+    }
+    ws->vpart.alloc(size_t(ws->final_splits) * R * kHeadLatent * 4);
+    ws->feat_ct.alloc(size_t(kMaxTembSteps) * 256 * e);
+    ws->h1pre.alloc(size_t(kMaxTembSteps) * H * 4);
+    ws->h1_ct.alloc(size_t(kMaxTembSteps) * H * e);
     const bool bf = m.bf16;
+    ws->tm_feat = make_tmap(ws->feat_ct.p, bf, kMaxTembSteps, 256, 128);
+    ws->tm_h1 = make_tmap(ws->h1_ct.p, bf, kMaxTembSteps, H, 128);
     ws->tm_noisy = make_tmap(ws->noisy.p, bf, R, kHeadLatent, 128);
     ws->tm_cond = make_tmap(ws->cond_ct.p, bf, R, H, 128);
     ws->tm_sc = make_tmap(ws->sc.p, bf, R, H, 128);
@@ -450,7 +482,13 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         ep.ldr = H;
         ep.gate = shift + 2 * H;
         ep.ldg = m.NADA;
-        launch_gemm<CT>(256, EPI_RESID, ws.tm_ffn, m.tm_down[size_t(l)], R, H, F, ep, sms, st);
+        // 192-wide tiles when they fill the SMs better (H = 1536: 8 x 16 = 128 tiles vs 96)
+        const int64_t mt = (R + 127) / 128;
+        const bool use192 = !m.tm_down192.empty() && waves_eff(mt * (H / 192), sms) > waves_eff(mt * (H / 256), sms);
+        if (use192)
+            launch_gemm<CT>(192, EPI_RESID, ws.tm_ffn, m.tm_down192[size_t(l)], R, H, F, ep, sms, st);
+        else
+            launch_gemm<CT>(256, EPI_RESID, ws.tm_ffn, m.tm_down256[size_t(l)], R, H, F, ep, sms, st);
     }
     const float* fshift = ada + 3 * H * L;
     rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(ws.x.as<float>(), H, nullptr, fshift, fshift + H,
@@ -458,8 +496,10 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
     CK(cudaGetLastError());
     ep = EpiParams{};
     ep.status = status;
-    ep.out = ws.v.p;
+    ep.out = ws.vpart.p;
     ep.ldo = kHeadLatent;
+    ep.splits = ws.final_splits;
+    ep.split_stride = R * kHeadLatent;
     launch_gemm<CT>(64, EPI_F32, ws.tm_h, m.tm_final, R, kHeadLatent, H, ep, sms, st);
 }
 
@@ -477,14 +517,23 @@ void head_cond_proj(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, cudaStream_t 
     launch_gemm<CT>(256, EPI_F32, ws.tm_cond, m.tm_cond, R, H, H, ep, ctx->num_sms, st);
 }
 
+// t_emb rows for S timesteps: feat = [cos | sin](t f) -> Linear(256->H) -> SiLU -> Linear(H->H),
+// both linears on the tensor-core GEMM (rows = S, masked inside 128-row tiles).
 template <typename CT>
 void head_temb(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, const float* tsteps, int S, cudaStream_t st) {
-    const int H = int(m.H);
-    const int blocks = (H + 7) / 8;
-    temb_stage1_kernel<CT><<<blocks, 256, 0, st>>>(tsteps, S, m.w_t1.as<CT>(), H, ws.h1.as<float>());
+    const int64_t H = m.H;
+    temb_feat_kernel<CT><<<S, 128, 0, st>>>(tsteps, ws.feat_ct.as<CT>());
     CK(cudaGetLastError());
-    temb_stage2_kernel<CT><<<blocks, 256, 0, st>>>(ws.h1.as<float>(), S, m.w_t2.as<CT>(), H, ws.temb.as<float>());
+    EpiParams ep;
+    ep.status = ctx->status.as<int>();
+    ep.out = ws.h1pre.p;
+    ep.ldo = H;
+    launch_gemm<CT>(256, EPI_F32, ws.tm_feat, m.tm_t1, S, H, 256, ep, ctx->num_sms, st);
+    silu_to_ct_kernel<CT><<<grid_for(int64_t(S) * H, 256, ctx->num_sms), 256, 0, st>>>(ws.h1pre.as<float>(),
+                                                                                         int64_t(S) * H, ws.h1_ct.as<CT>());
     CK(cudaGetLastError());
+    ep.out = ws.temb.p;
+    launch_gemm<CT>(256, EPI_F32, ws.tm_h1, m.tm_t2, S, H, H, ep, ctx->num_sms, st);
 }
 
 // The full sampling loop on workspace buffers (ws.cond, ws.init filled; coefs/tsteps uploaded).
@@ -502,7 +551,8 @@ void head_sample_body(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int S, floa
         float* hp = (s & 1) ? ws.hist0.as<float>() : ws.hist1.as<float>();
         float* hc = (s & 1) ? ws.hist1.as<float>() : ws.hist0.as<float>();
         vv_cfg_dpm_kernel<CT><<<grid_for(n_half, 256, sms), 256, 0, st>>>(
-            ws.v.as<float>(), ws.xstate.as<float>(), hp, hc, ws.noisy.as<CT>(), ws.out.as<float>(), n_half,
+            ws.vpart.as<float>(), ws.final_splits, 2 * n_half, ws.xstate.as<float>(), hp, hc, ws.noisy.as<CT>(),
+            ws.out.as<float>(), n_half,
             ws.coefs.as<VvStepCoef>(), s, cfg, ctx->status.as<int>());
         CK(cudaGetLastError());
     }
@@ -589,6 +639,9 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
     head_cond_proj<CT>(ctx, m, ws, st);
     head_temb<CT>(ctx, m, ws, ws.ptstep.as<float>(), 1, st);
     head_forward<CT>(ctx, m, ws, 0, st);
+    sum_partials_kernel<<<grid_for(R * kHeadLatent, 256, ctx->num_sms), 256, 0, st>>>(
+        ws.vpart.as<float>(), ws.final_splits, R * kHeadLatent, ws.v.as<float>());
+    CK(cudaGetLastError());
     CK(cudaMemcpyAsync(out, ws.v.p, size_t(frames) * kHeadLatent * 4, cudaMemcpyDeviceToHost, st));
     check_status_word(ctx, st);
 }

@@ -38,6 +38,8 @@ struct EpiParams {
     const float* gate = nullptr;
     int64_t ldg = 0;
     int* status = nullptr;
+    int splits = 1;             // split-K factor (EPI_F32 only): split s writes out + s * split_stride
+    int64_t split_stride = 0;
 };
 
 template <typename CT>
@@ -45,6 +47,7 @@ struct CtTraits;
 template <>
 struct CtTraits<__half> {
     static constexpr uint32_t kFmt = 0;
+    __device__ static __forceinline__ __half cvt(float a) { return __float2half_rn(a); }
     __device__ static __forceinline__ uint32_t pack2(float a, float b) {
         __half2 h = __floats2half2_rn(a, b);
         return *reinterpret_cast<uint32_t*>(&h);
@@ -53,6 +56,7 @@ struct CtTraits<__half> {
 template <>
 struct CtTraits<__nv_bfloat16> {
     static constexpr uint32_t kFmt = 1;
+    __device__ static __forceinline__ __nv_bfloat16 cvt(float a) { return __float2bfloat16_rn(a); }
     __device__ static __forceinline__ uint32_t pack2(float a, float b) {
         __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
         return *reinterpret_cast<uint32_t*>(&h);
@@ -65,12 +69,13 @@ template <int BN>
 struct GemmShape {
     static constexpr int BM = 128;
     static constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
-    static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
+    static constexpr int STAGES = BN >= 192 ? (BN == 192 ? 5 : 4) : (BN >= 128 ? 6 : 8);
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+    static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;  // power of two
+    static constexpr size_t EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // per-warp transpose buffers
+    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + EPI_STAGE_BYTES;
 };
 
 template <int BN, int EPI, typename CT>
@@ -95,7 +100,10 @@ __global__ void __launch_bounds__(192, 1)
     const int lane = threadIdx.x & 31;
     const int m_tiles = (M + BM - 1) / BM;
     const int num_tiles = m_tiles * (N / BN);
-    const int k_blocks = K / BK;
+    // Work unit u = (tile, split): split-K partitions the K blocks into `splits` equal ranges.
+    const int splits = ep.splits > 1 ? ep.splits : 1;
+    const int num_units = num_tiles * splits;
+    const int k_blocks = K / BK / splits;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -126,10 +134,12 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+                const int tile = u % num_tiles;
+                const int kb0 = (u / num_tiles) * k_blocks;
                 const int m0 = (tile % m_tiles) * BM;
                 const int n0 = (tile / m_tiles) * BN;
-                for (int kb = 0; kb < k_blocks; ++kb) {
+                for (int kb = kb0; kb < kb0 + k_blocks; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
@@ -149,7 +159,7 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, ep.status, kErrTimeoutMma)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
@@ -163,7 +173,7 @@ __global__ void __launch_bounds__(192, 1)
                     for (int k = 0; k < BK / 16; ++k) {
                         // +32 bytes along K inside the 128-byte swizzle row == +2 in the >>4 address field
                         mma_f16_ss(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc,
-                                   (kb | k) != 0 ? 1u : 0u);
+                                   (kb | k) != 0 ? 1u : 0u);  // kb counts within this unit's K range
                     }
                     mma_commit(&empty[stage]);
                     if (++stage == STAGES) {
@@ -177,86 +187,99 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
+        // Epilogue: TMEM -> registers (thread = row).  fp32 and residual outputs then go
+        // through a padded shared-memory transpose (32 x 33 floats per warp) so each warp
+        // instruction reads/writes one contiguous 32-column row segment (coalesced, and the
+        // residual read-modify-write issues all 32 rows' loads before any store instead of serialising).
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
-        const int row_in_tile = quarter * 32 + lane;
+        float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
+        constexpr int CHUNKS = EPI == EPI_SWIGLU ? 4 : BN / 32;
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+            const int tile = u % num_tiles;
+            float* out_f32 = reinterpret_cast<float*>(ep.out) + int64_t(u / num_tiles) * ep.split_stride;
             const int m0 = (tile % m_tiles) * BM;
             const int n0 = (tile / m_tiles) * BN;
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.status, kErrTimeoutEpilogue)) goto done;
             tc_fence_after();
-            const int row = m0 + row_in_tile;
-            const bool live = row < M;
+            const int rbase = m0 + quarter * 32;
+            const int rows_live = M - rbase < 32 ? M - rbase : 32;
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-            if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    float a[32], l[32];
-                    __syncwarp();
-                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), a);
+            for (int c = 0; c < CHUNKS; ++c) {
+                float v[32];
+                __syncwarp();
+                if constexpr (EPI == EPI_SWIGLU) {
+                    float l[32];
+                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
                     tmem_ld_32x32b_x32(tbase + uint32_t(128 + c * 32), l);
                     tmem_ld_wait();
-                    if (live) {
-                        if (ep.bias) {
-                            const float* ba = ep.bias + n0 + c * 32;
-                            const float* bl = ep.bias + n0 + 128 + c * 32;
+                    const float* ba = ep.bias ? ep.bias + n0 + c * 32 : nullptr;
 #pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                a[j] += __ldg(ba + j);
-                                l[j] += __ldg(bl + j);
-                            }
+                    for (int j = 0; j < 32; ++j) {
+                        const float av = ba ? v[j] + __ldg(ba + j) : v[j];
+                        const float lv = ba ? l[j] + __ldg(ba + 128 + j) : l[j];
+                        v[j] = silu_f(av) * lv;
+                    }
+                } else {
+                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+                    tmem_ld_wait();
+                }
+                if constexpr (EPI == EPI_SWIGLU || EPI == EPI_CT) {
+                    // 16-bit outputs: each thread stores its row's 32 values as 4 x 16 B (no smem
+                    // traffic, which would compete with the next tile's tcgen05 operand reads).
+                    const int row = rbase + lane;
+                    if (lane < rows_live) {
+                        const int col0 = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32;
+                        if (EPI == EPI_CT && ep.bias) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + col0 + j);
                         }
                         uint32_t packed[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            packed[j] = CtTraits<CT>::pack2(silu_f(a[2 * j]) * l[2 * j],
-                                                            silu_f(a[2 * j + 1]) * l[2 * j + 1]);
-                        CT* dst = reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + n0 / 2 + c * 32;
-                        uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-                    }
-                }
-            } else {
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    float v[32];
-                    __syncwarp();
-                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
-                    tmem_ld_wait();
-                    if (!live) continue;
-                    const int n = n0 + c * 32;
-                    if (ep.bias) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + n + j);
-                    }
-                    if constexpr (EPI == EPI_F32) {
-                        float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(ep.out) + int64_t(row) * ep.ldo + n);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                    } else if constexpr (EPI == EPI_CT) {
-                        uint32_t packed[16];
-#pragma unroll
                         for (int j = 0; j < 16; ++j) packed[j] = CtTraits<CT>::pack2(v[2 * j], v[2 * j + 1]);
-                        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + n);
+                        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + col0);
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-                    } else {  // EPI_RESID
-                        float4* r4 = reinterpret_cast<float4*>(ep.resid + int64_t(row) * ep.ldr + n);
-                        const float4* g4 =
-                            ep.gate ? reinterpret_cast<const float4*>(ep.gate + int64_t(row) * ep.ldg + n) : nullptr;
+                    }
+                    continue;
+                }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            float4 r = r4[j];
-                            const float4 g = g4 ? g4[j] : make_float4(1.f, 1.f, 1.f, 1.f);
-                            r.x += g.x * v[4 * j];
-                            r.y += g.y * v[4 * j + 1];
-                            r.z += g.z * v[4 * j + 2];
-                            r.w += g.w * v[4 * j + 3];
-                            r4[j] = r;
+                for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
+                __syncwarp();
+                const int col = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32 + lane;
+                const float bcol = (EPI != EPI_SWIGLU && ep.bias) ? __ldg(ep.bias + col) : 0.f;
+                if constexpr (EPI == EPI_RESID) {
+                    float* __restrict__ R = ep.resid;
+                    const float* __restrict__ G = ep.gate;
+#pragma unroll 1
+                    for (int r0 = 0; r0 < rows_live; r0 += 32) {
+                        float rv[32], gv[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int64_t row = rbase + r0 + i;
+                            const bool ok = r0 + i < rows_live;
+                            rv[i] = ok ? R[row * ep.ldr + col] : 0.f;
+                            gv[i] = (ok && G) ? G[row * ep.ldg + col] : 1.f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (r0 + i < rows_live)
+                                R[int64_t(rbase + r0 + i) * ep.ldr + col] = rv[i] + gv[i] * (stg[(r0 + i) * 33 + lane] + bcol);
+                        }
+                    }
+                } else {
+#pragma unroll 4
+                    for (int r = 0; r < 32; ++r) {
+                        if (r < rows_live) {
+                            const float x = stg[r * 33 + lane] + bcol;
+                            const int64_t row = rbase + r;
+                            if constexpr (EPI == EPI_F32)
+                                out_f32[row * ep.ldo + col] = x;
+                            else
+                                reinterpret_cast<CT*>(ep.out)[row * ep.ldo + col] = CtTraits<CT>::cvt(x);
                         }
                     }
                 }

@@ -137,57 +137,33 @@ __global__ void silu_cond_kernel(const float* __restrict__ cp, const float* __re
     }
 }
 
-// ------------------------------------------------ timestep embedding MLP
-// Stage 1: h1[s, n] = silu( sum_k W1[n, k] * feat_s[k] ), feat_s = [cos(t_s f) | sin(t_s f)], f_i = exp(-ln(1e4) i/128)
-// (make_timestep_freqs + build_timestep_embedding, diffusion_head.cpp:59-66,141-163)
-// Stage 2: temb[s, n] = sum_k W2[n, k] * h1[s, k].
-// One warp per output column n, all steps at once (weights read once).
+// ------------------------------------------------ timestep embedding input
+// feat_s = [cos(t_s f_i) | sin(t_s f_i)], f_i = exp(-ln(1e4) i / 128), i < 128
+// (make_timestep_freqs + build_timestep_embedding, diffusion_head.cpp:59-66,141-163).
+// One block of 128 threads per timestep row; the MLP runs on the tensor-core GEMM.
 constexpr int kMaxTembSteps = 32;
 
 template <typename CT>
-__global__ void temb_stage1_kernel(const float* __restrict__ tsteps, int S, const CT* __restrict__ W1, int H,
-                                   float* __restrict__ h1) {
-    __shared__ float feat[kMaxTembSteps][256];
-    for (int i = threadIdx.x; i < S * 128; i += blockDim.x) {
-        const int s = i / 128, j = i % 128;
-        const float f = expf(-logf(10000.0f) * float(j) / 128.0f);
-        const float a = tsteps[s] * f;
-        feat[s][j] = cosf(a);
-        feat[s][128 + j] = sinf(a);
-    }
-    __syncthreads();
-    const int warps = blockDim.x / 32;
-    const int lane = threadIdx.x & 31;
-    for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < H; n += gridDim.x * warps) {
-        float wv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) wv[j] = to_f32(W1[int64_t(n) * 256 + lane * 8 + j]);
-        for (int s = 0; s < S; ++s) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc += wv[j] * feat[s][lane * 8 + j];
-            acc = warp_sum(acc);
-            if (lane == 0) h1[int64_t(s) * H + n] = silu_f(acc);
-        }
-    }
+__global__ void temb_feat_kernel(const float* __restrict__ tsteps, CT* __restrict__ feat) {
+    const int s = blockIdx.x, j = threadIdx.x;
+    const float f = expf(-logf(10000.0f) * float(j) / 128.0f);
+    const float a = tsteps[s] * f;
+    feat[s * 256 + j] = from_f32<CT>(cosf(a));
+    feat[s * 256 + 128 + j] = from_f32<CT>(sinf(a));
 }
 
 template <typename CT>
-__global__ void temb_stage2_kernel(const float* __restrict__ h1, int S, const CT* __restrict__ W2, int H,
-                                   float* __restrict__ temb) {
-    const int warps = blockDim.x / 32;
-    const int lane = threadIdx.x & 31;
-    for (int n = blockIdx.x * warps + (threadIdx.x >> 5); n < H; n += gridDim.x * warps) {
-        float acc[kMaxTembSteps];
-        for (int s = 0; s < S; ++s) acc[s] = 0.f;
-        for (int k = lane; k < H; k += 32) {
-            const float w = to_f32(W2[int64_t(n) * H + k]);
-            for (int s = 0; s < S; ++s) acc[s] += w * h1[int64_t(s) * H + k];
-        }
-        for (int s = 0; s < S; ++s) {
-            const float v = warp_sum(acc[s]);
-            if (lane == 0) temb[int64_t(s) * H + n] = v;
-        }
+__global__ void silu_to_ct_kernel(const float* __restrict__ src, int64_t n, CT* __restrict__ dst) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        dst[i] = from_f32<CT>(silu_f(src[i]));
+}
+
+// out[i] = sum over split-K partials part[s * n + i] (fixed order: deterministic).
+__global__ void sum_partials_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        float v = 0.f;
+        for (int s = 0; s < splits; ++s) v += part[s * n + i];
+        out[i] = v;
     }
 }
 
@@ -205,17 +181,22 @@ struct VvStepCoef {
     int pad;
 };
 
-// v: head output [2B, 64] (cond rows then uncond rows).  x: sampler state [B, 64].
+// v: head output [2B, 64] (cond rows then uncond rows) as `splits` split-K partials
+// spaced `split_stride` apart, summed here in a fixed order.  x: sampler state [B, 64].
 // hist_prev / hist_cur: converted outputs of the previous / this step [B, 64].
 // noisy: next head input [2B, 64] in ct, both halves = x (duplicate_positive_half).
 template <typename CT>
-__global__ void vv_cfg_dpm_kernel(const float* __restrict__ v, float* __restrict__ x, const float* __restrict__ hist_prev,
+__global__ void vv_cfg_dpm_kernel(const float* __restrict__ v, int splits, int64_t split_stride, float* __restrict__ x, const float* __restrict__ hist_prev,
                                   float* __restrict__ hist_cur, CT* __restrict__ noisy, float* __restrict__ out_latents,
                                   int64_t n_half, const VvStepCoef* __restrict__ coefs, int step, float cfg,
                                   int* __restrict__ status) {
     const VvStepCoef c = coefs[step];
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n_half; i += int64_t(gridDim.x) * blockDim.x) {
-        const float vc = v[i], vu = v[n_half + i];
+        float vc = 0.f, vu = 0.f;
+        for (int s = 0; s < splits; ++s) {
+            vc += v[s * split_stride + i];
+            vu += v[s * split_stride + n_half + i];
+        }
         const float g = vu + cfg * (vc - vu);            // apply_cfg, diffusion_sampler.cpp:35-56
         const float xs = x[i];
         const float conv = c.alpha_s * xs - c.sigma_s * g;  // convert_model_output
