@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm"]
+            "b2d_gemm", "b2d_gemm_splitk_noalloc"]
 
 
 class B2DError(RuntimeError):
@@ -79,6 +79,8 @@ def lib() -> C.CDLL:
         L.b2d_vv_sample_device.argtypes = [P, P, P, P, I64, I64, F, P, P]
         L.b2d_q8_0_dequantize.argtypes = [P, P, I64, I64, P, P]
         L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
+        L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
+                                              C.c_size_t]
         _lib = L
     return _lib
 

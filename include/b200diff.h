@@ -162,6 +162,32 @@ B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const
                     int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);
 
+/* ------------------------------------------------- allocation-free variant */
+/* No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory -- hosts that only pass the library buffers they
+ * carved from their own pool or arena, or that forbid cudaMalloc while serving.
+ *
+ * out[m, n] (fp32, leading dim ldo) = A * B^T (+ bias), A [m, k] and B [n, k]
+ * fp16 (bf16 = 0) or bf16 (bf16 = 1) device matrices, computed by the same
+ * tcgen05 kernel as b2d_gemm with `splits`-way split-K.  The split partials
+ * live in a fixed file-scope device array of B2D_NOALLOC_SCRATCH_FLOATS floats
+ * (32 MiB), which every GPU that loads this library keeps until the process
+ * exits; the call itself allocates nothing.
+ *   - Needs no b2d_ctx; runs on the current device.  The first call on a device
+ *     looks up the array's device address (cudaGetSymbolAddress); make that
+ *     first call before any stream capture.
+ *   - Rejects splits * m * n > B2D_NOALLOC_SCRATCH_FLOATS (B2D_EINVAL).
+ *   - All calls share the one array, so calls that overlap on the GPU (other
+ *     streams, other threads) race; serialise them.  The partials need no
+ *     clearing (each split writes its whole slice); the status word is cleared
+ *     at the start of every call.
+ *   - k % 64 == 0, bn in {64, 128, 256}, n % bn == 0, splits divides k / 64.
+ *   - err / err_len (may be NULL / 0) receive a message when the call fails. */
+#define B2D_NOALLOC_SCRATCH_FLOATS (8ll * 1024 * 1024)
+B2D_API b2d_status b2d_gemm_splitk_noalloc(int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
+                                           int64_t k, int32_t splits, int32_t bn, const float* bias_dev,
+                                           float* out_dev, int64_t ldo, void* stream, char* err, size_t err_len);
+
 #ifdef __cplusplus
 }
 #endif
