@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc"]
+            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention"]
 
 
 class B2DError(RuntimeError):
@@ -52,6 +52,19 @@ class VvStep(C.Structure):
     _fields_ = [("timestep", C.c_int64), ("sigma", C.c_float), ("sigma_next", C.c_float), ("alpha_s", C.c_float),
                 ("sigma_s", C.c_float), ("sample_coeff", C.c_float), ("d0_coeff", C.c_float),
                 ("inv_r0", C.c_float), ("order", C.c_int32)]
+
+
+class DitConfig(C.Structure):
+    _fields_ = [("embed_dim", C.c_int64), ("depth", C.c_int64), ("num_heads", C.c_int64),
+                ("cond_token_dim", C.c_int64), ("global_cond_dim", C.c_int64), ("io_channels", C.c_int64),
+                ("prompt_max_length", C.c_int64)]
+
+
+class DitRequest(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("latent_tokens", C.c_int64), ("steps", C.c_int64), ("noise", C.c_void_p),
+                ("padding_mask", C.c_void_p), ("cross_positive", C.c_void_p), ("cross_negative", C.c_void_p),
+                ("global_cond", C.c_void_p), ("sigma_min", C.c_float), ("sigma_max", C.c_float), ("rho", C.c_float),
+                ("cfg_scale", C.c_float), ("apg_scale", C.c_float), ("sampler", C.c_int32)]
 
 
 _lib = None
@@ -81,6 +94,10 @@ def lib() -> C.CDLL:
         L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
+        L.b2d_attention.argtypes = [P, I32, P, I64, I64, P, P, I64, I64, P, I64, I64, I32, I32, I32, I32, I32, P]
+        L.b2d_dit_load.argtypes = [P, C.POINTER(DitConfig), C.POINTER(TensorView), I32]
+        L.b2d_dit_sample.argtypes = [P, C.POINTER(DitRequest), P, P]
+        L.b2d_dit_sample_device.argtypes = [P, C.POINTER(DitRequest), P, P]
         _lib = L
     return _lib
 
@@ -142,6 +159,13 @@ class Context:
         self.check(lib().b2d_q8_0_dequantize(self._h, C.c_void_p(q8_dev), rows, k, C.c_void_p(out_dev),
                                              C.c_void_p(stream)))
 
+    def attention(self, q: int, q_row: int, q_seq: int, k: int, v: int, kv_row: int, kv_seq: int, o: int,
+                  o_row: int, o_seq: int, lq: int, lk: int, heads: int, kv_rep: int = 1, nseq: int = 1,
+                  bf16: bool = False, stream: int = 0) -> None:
+        self.check(lib().b2d_attention(self._h, int(bf16), C.c_void_p(q), q_row, q_seq, C.c_void_p(k), C.c_void_p(v),
+                                       kv_row, kv_seq, C.c_void_p(o), o_row, o_seq, lq, lk, heads, kv_rep, nseq,
+                                       C.c_void_p(stream)))
+
     def gemm(self, a_dev: int, b_dev: int, m: int, n: int, k: int, *, bf16: bool = False, epilogue: int = EPI_F32,
              bn: int = 256, bias: int = 0, out: int = 0, ldo: int = 0, resid: int = 0, ldr: int = 0, gate: int = 0,
              ldg: int = 0, stream: int = 0) -> None:
@@ -151,6 +175,66 @@ class Context:
 
 
 WeightSpec = Tuple[str, int, Tuple[int, ...], np.ndarray]  # (name, ggml type, dims, raw payload)
+
+
+def _views(specs):
+    """(name, ggml_type, dims, payload) list -> (TensorView array, keep-alive list)."""
+    specs = list(specs)
+    views = (TensorView * len(specs))()
+    keep = []
+    for i, (name, gtype, dims, payload) in enumerate(specs):
+        payload = np.ascontiguousarray(payload)
+        nb = name.encode()
+        keep += [payload, nb]
+        views[i].name = nb
+        views[i].ggml_type = gtype
+        views[i].ndim = len(dims)
+        for j, dd in enumerate(dims):
+            views[i].dims[j] = dd
+        views[i].data = payload.ctypes.data
+        views[i].nbytes = payload.nbytes
+    return views, keep
+
+
+class StableAudioDiT:
+    """FoundationRfDitRuntime (include/engine/models/stable_audio/foundation/rf_dit.h:73-106) on a B200 context.
+
+    ``weights``: (name, ggml_type, dims, payload) with the GGUF names ``model.model.*``."""
+
+    def __init__(self, ctx: Context, embed_dim: int = 1536, depth: int = 24, num_heads: int = 24,
+                 cond_token_dim: int = 768, global_cond_dim: int = 1536, io_channels: int = 64,
+                 prompt_max_length: int = 128, weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = DitConfig(embed_dim, depth, num_heads, cond_token_dim, global_cond_dim, io_channels,
+                             prompt_max_length)
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_dit_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    def _request(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
+                 sigma_max, rho, cfg_scale, apg_scale):
+        b, _, t = noise.shape
+        return DitRequest(b, t, steps, _ptr(noise), _ptr(padding_mask), _ptr(cross_positive),
+                          _ptr(cross_negative) if cross_negative is not None else None, _ptr(global_cond),
+                          sigma_min, sigma_max, rho, cfg_scale, apg_scale, 0)
+
+    def sample(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps=100, sigma_min=0.01,
+               sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, out=None, stream: int = 0):
+        """Host arrays (numpy / pinned torch) -> latents [B, 64, T] (dpmpp-2m)."""
+        arrs = [np.ascontiguousarray(a, np.float32) if isinstance(a, np.ndarray) else a
+                for a in (noise, padding_mask, cross_positive, cross_negative, global_cond)]
+        rq = self._request(*arrs, steps, sigma_min, sigma_max, rho, cfg_scale, apg_scale)
+        if out is None:
+            out = np.empty(arrs[0].shape, np.float32)
+        self.ctx.check(lib().b2d_dit_sample(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)), C.c_void_p(stream)))
+        return out
+
+    def sample_device(self, noise, padding_mask, cross_positive, cross_negative, global_cond, out, steps=100,
+                      sigma_min=0.01, sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, stream: int = 0):
+        rq = self._request(noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
+                           sigma_max, rho, cfg_scale, apg_scale)
+        self.ctx.check(lib().b2d_dit_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
+                                                   C.c_void_p(stream)))
+        return out
 
 
 class VibeVoiceDiffusionHead:

@@ -14,6 +14,8 @@
 #include <vector>
 
 #include "../../include/b200diff.h"
+#include "attention.cuh"
+#include "dit_kernels.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -253,6 +255,8 @@ struct HeadWorkspace {
     }
 };
 
+struct DitModel;
+
 struct HeadModel {
     b2d_vv_head_config cfg{};
     int64_t H = 0, F = 0, NADA = 0;
@@ -273,6 +277,7 @@ struct b2d_ctx {
     DevBuf status;  // int device-side status word
     cudaStream_t load_stream = nullptr;
     std::unique_ptr<HeadModel> head;
+    std::unique_ptr<DitModel> dit;
 };
 
 namespace {
@@ -646,6 +651,8 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
     check_status_word(ctx, st);
 }
 
+#include "dit_runtime.inc"
+
 }  // namespace
 
 // =================================================================== C ABI
@@ -683,6 +690,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         DeviceGuard g(ctx->device);
         cudaDeviceSynchronize();
         ctx->head.reset();
+        ctx->dit.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -808,6 +816,83 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
         else
             launch_gemm<__half>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
     });
+}
+
+b2d_status b2d_attention(b2d_ctx* ctx, int32_t bf16, const void* q, int64_t q_row, int64_t q_seq, const void* k,
+                         const void* v, int64_t kv_row, int64_t kv_seq, void* o, int64_t o_row, int64_t o_seq,
+                         int32_t lq, int32_t lk, int32_t heads, int32_t kv_rep, int32_t nseq, void* stream) {
+    return guarded(ctx, [&] {
+        if (!q || !k || !v || !o || lq <= 0 || lk <= 0 || heads <= 0 || kv_rep <= 0 || nseq <= 0 ||
+            heads % kv_rep)
+            fail(B2D_EINVAL, "invalid attention shape");
+        if ((q_row | kv_row | q_seq | kv_seq) % 8 || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                                                      reinterpret_cast<uintptr_t>(v)) % 16)
+            fail(B2D_EINVAL, "attention operands need 16-byte aligned rows");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (bf16)
+            dit_attention<__nv_bfloat16>(q, q_row, q_seq, k, v, kv_row, kv_seq, o, o_row, o_seq, lq, lk, kv_rep,
+                                         heads, nseq, st);
+        else
+            dit_attention<__half>(q, q_row, q_seq, k, v, kv_row, kv_seq, o, o_row, o_seq, lq, lk, kv_rep, heads,
+                                  nseq, st);
+    });
+}
+
+b2d_status b2d_dit_load(b2d_ctx* ctx, const b2d_dit_config* config, const b2d_tensor_view* tensors,
+                        int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0))
+            fail(B2D_EINVAL, "Stable Audio Foundation RF DiT runtime requires assets");
+        const b2d_dit_config& c = *config;
+        if (c.num_heads <= 0 || c.embed_dim % c.num_heads != 0)
+            fail(B2D_EINVAL, "Stable Audio Foundation RF DiT head dimensions are invalid");
+        if (c.embed_dim / c.num_heads != 64) fail(B2D_EINVAL, "head_dim must be 64 on this path");
+        if (c.cond_token_dim <= 0 || c.cond_token_dim % 64 != 0)
+            fail(B2D_EINVAL, "Stable Audio Foundation RF DiT context head dimensions are invalid");
+        if (c.num_heads % (c.cond_token_dim / 64) != 0)
+            fail(B2D_EINVAL, "Stable Audio Foundation cross-attention head repeat mismatch");
+        if (c.io_channels != 64) fail(B2D_EINVAL, "io_channels must be 64 on this path");
+        if (c.embed_dim % 256 || c.cond_token_dim % 128 || c.global_cond_dim % 64 || c.depth <= 0)
+            fail(B2D_EINVAL, "embed_dim must be a multiple of 256 and cond_token_dim of 128");
+        auto m = std::make_unique<DitModel>();
+        m->cfg = c;
+        m->d = c.embed_dim;
+        m->heads = c.num_heads;
+        m->c = c.cond_token_dim;
+        m->gd = c.global_cond_dim;
+        m->P2 = c.prompt_max_length + 2;
+        m->ffi = 4 * c.embed_dim;
+        m->kvh = c.cond_token_dim / 64;
+        const b2d_tensor_view* probe =
+            find_tensor(tensors, n_tensors, "model.model.transformer.layers.0.self_attn.to_qkv.weight");
+        m->bf16 = probe && probe->ggml_type == B2D_TYPE_BF16;
+        ctx->dit.reset();
+        if (m->bf16)
+            dit_load_t<__nv_bfloat16>(ctx, *m, tensors, n_tensors);
+        else
+            dit_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->dit = std::move(m);
+    });
+}
+
+static b2d_status dit_sample_common(b2d_ctx* ctx, const b2d_dit_request* rq, float* out, void* stream, bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->dit) fail(B2D_ESTATE, "Stable Audio Foundation RF DiT weights are not loaded");
+        if (!rq || !out) fail(B2D_EINVAL, "Stable Audio Foundation RF DiT request is null");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (ctx->dit->bf16)
+            dit_sample<__nv_bfloat16>(ctx, *rq, out, st, host);
+        else
+            dit_sample<__half>(ctx, *rq, out, st, host);
+    });
+}
+
+b2d_status b2d_dit_sample(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents, void* stream) {
+    return dit_sample_common(ctx, request, out_latents, stream, true);
+}
+
+b2d_status b2d_dit_sample_device(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents, void* stream) {
+    return dit_sample_common(ctx, request, out_latents, stream, false);
 }
 
 }  // extern "C"

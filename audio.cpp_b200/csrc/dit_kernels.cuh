@@ -1,0 +1,271 @@
+// Memory-bound kernels of the Stable Audio Open 1.0 DiT step
+// (src/models/stable_audio/foundation/rf_dit.cpp): LayerNorm, partial NEOX RoPE
+// with the V padding mask, the global-token row, the sampler's input transpose,
+// and the fused CFG/APG + DPM++ 2M update with its per-sequence reductions.
+#pragma once
+
+#include "kernels.cuh"
+
+namespace b2d {
+
+// LayerNorm over d (<= 4096): y = ct((x - mean) / sqrt(var + eps) * gamma + beta)
+// (ggml_norm + affine, src/framework/modules/norm_modules.cpp:200-228).  One CTA (128 thr) per row.
+template <typename CT>
+__global__ void __launch_bounds__(128) layernorm_kernel(const float* __restrict__ x, int d, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, float eps, CT* __restrict__ out) {
+    constexpr int MAXV = 8;
+    const int64_t row = blockIdx.x;
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * d);
+    const int n4 = d / 4;
+    float4 v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = threadIdx.x + i * 128;
+        v[i] = idx < n4 ? x4[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
+    __shared__ float red[4];
+    __shared__ float bc;
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) bc = (red[0] + red[1] + red[2] + red[3]) / float(d);
+    __syncthreads();
+    const float mean = bc;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = threadIdx.x + i * 128;
+        if (idx < n4) {
+            const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+            q += a * a + b * b + c * c + e * e;
+        }
+    }
+    q = warp_sum(q);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = q;
+    __syncthreads();
+    if (threadIdx.x == 0) bc = (red[0] + red[1] + red[2] + red[3]) / float(d);
+    __syncthreads();
+    const float rstd = 1.0f / sqrtf(bc + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(beta);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = threadIdx.x + i * 128;
+        if (idx < n4) {
+            const float4 gg = g4[idx], bb = b4[idx];
+            const float a = (v[i].x - mean) * rstd * gg.x + bb.x;
+            const float b = (v[i].y - mean) * rstd * gg.y + bb.y;
+            const float c = (v[i].z - mean) * rstd * gg.z + bb.z;
+            const float e = (v[i].w - mean) * rstd * gg.w + bb.w;
+            reinterpret_cast<uint2*>(out + row * d)[idx] =
+                make_uint2(CtTraits<CT>::pack2(a, b), CtTraits<CT>::pack2(c, e));
+        }
+    }
+}
+
+// In-place on the fused qkv rows [rows, 3d] (row = seq * L + pos): NEOX RoPE on the first
+// 2*half dims of every q and k head (pairs (i, i + half)), V scaled by the padding mask.
+// cos/sin tables [L, half] follow ggml's rope cache (theta_i = pos * scale^i in fp32).
+template <typename CT>
+__global__ void rope_mask_kernel(CT* __restrict__ qkv, int64_t rows, int L, int d, int heads, int half,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                 const float* __restrict__ pad) {
+    const int64_t total = rows * heads;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t row = i / heads;
+        const int h = int(i % heads);
+        const int pos = int(row % L);
+        CT* base = qkv + row * 3 * d + h * 64;
+        const float* c = cos_t + pos * half;
+        const float* s = sin_t + pos * half;
+#pragma unroll 4
+        for (int j = 0; j < half; ++j) {
+            const float cj = c[j], sj = s[j];
+            float x0 = to_f32(base[j]), x1 = to_f32(base[j + half]);
+            base[j] = from_f32<CT>(x0 * cj - x1 * sj);
+            base[j + half] = from_f32<CT>(x0 * sj + x1 * cj);
+            x0 = to_f32(base[d + j]);
+            x1 = to_f32(base[d + j + half]);
+            base[d + j] = from_f32<CT>(x0 * cj - x1 * sj);
+            base[d + j + half] = from_f32<CT>(x0 * sj + x1 * cj);
+        }
+        const float m = pad[row];
+        if (m != 1.0f) {
+            CT* vb = base + 2 * d;
+            for (int j = 0; j < 64; ++j) vb[j] = from_f32<CT>(to_f32(vb[j]) * m);
+        }
+    }
+}
+
+// Global-token rows: h[seq, 0, :] = gpre[seq, :] + temb[step, :]   (rf_dit.cpp:545-552)
+__global__ void dit_global_row_kernel(float* __restrict__ h, int64_t seq_rows, const float* __restrict__ gpre,
+                                      const float* __restrict__ temb, int d, int nseq) {
+    const int64_t total = int64_t(nseq) * d;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t s = i / d, c = i % d;
+        h[s * seq_rows * d + c] = gpre[i] + temb[c];
+    }
+}
+
+// Timestep features for every sampler step: [cos(2 pi t w_i) | sin(2 pi t w_i)], learned w (rf_dit.cpp:939-950).
+template <typename CT>
+__global__ void dit_tfeat_kernel(const float* __restrict__ tvals, const float* __restrict__ w, CT* __restrict__ feat) {
+    const int s = blockIdx.x, i = threadIdx.x;  // 128 threads
+    const float arg = tvals[s] * w[i] * 2.0f * 3.14159265358979323846f;
+    feat[s * 256 + i] = from_f32<CT>(cosf(arg));
+    feat[s * 256 + 128 + i] = from_f32<CT>(sinf(arg));
+}
+
+// Per-step sampler scalars, computed on the host in fp32 exactly as
+// Graph::sample_dpmpp_2m / build_cfg_model_output (rf_dit.cpp:798-883, 988-1028).
+struct DitStepCoef {
+    float c_in, c_skip, c_out;
+    float alpha, sigma;          // cos / sin(t pi / 2) for the CFG x0 algebra
+    float x_scale, d_scale;      // sigma_next / sigma, -expm1(-h)
+    float d_coeff, old_coeff;    // second-order blend (first step: 1, 0)
+    float c_in_next;             // next step's input scale (unused on the last step)
+    float cfg_scale, apg_scale;
+    float sig;                   // sigma of this step (sigma_0 scales the initial noise)
+    int final_step;              // sigma_next == 0: x = denoised
+    int first_step;              // no history yet: first-order update
+};
+
+// Step input: X[bb, t, c] = ct(x[b, c, t] * c_in), bb over the (CFG-doubled) graph batch.
+template <typename CT>
+__global__ void dit_step_input_kernel(const float* __restrict__ x, int B, int Bg, int T,
+                                      const DitStepCoef* __restrict__ coefs, CT* __restrict__ X) {
+    const float c_in = coefs[0].c_in;
+    const int64_t total = int64_t(Bg) * T * 64;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int c = int(i % 64);
+        const int64_t r = i / 64;
+        const int t = int(r % T);
+        const int bb = int(r / T);
+        X[i] = from_f32<CT>(x[(int64_t(bb % B) * 64 + c) * T + t] * c_in);
+    }
+}
+
+// raw model output y[bb, t, c] = sum of split-K partials at hidden row bb*(T+1) + t + 1.
+__device__ __forceinline__ float dit_raw(const float* part, int splits, int64_t split_stride, int bb, int T, int t,
+                                         int c) {
+    const int64_t idx = (int64_t(bb) * (T + 1) + t + 1) * 64 + c;
+    float v = 0.f;
+    for (int s = 0; s < splits; ++s) v += part[s * split_stride + idx];
+    return v;
+}
+
+// APG reductions per prompt b: s1 = sum (x0_c * m)^2, s2 = sum (x0_c - x0_u) * (x0_c * m).
+__global__ void __launch_bounds__(1024) dit_apg_reduce_kernel(const float* __restrict__ part, int splits,
+                                                              int64_t split_stride, const float* __restrict__ x,
+                                                              const float* __restrict__ mask, int B, int T,
+                                                              const DitStepCoef* __restrict__ coefs, int step,
+                                                              float* __restrict__ sums) {
+    const DitStepCoef k = coefs[step];
+    const int b = blockIdx.x;
+    double s1 = 0.0, s2 = 0.0;
+    for (int i = threadIdx.x; i < T * 64; i += blockDim.x) {
+        const int t = i / 64, c = i % 64;
+        const float xin = x[(int64_t(b) * 64 + c) * T + t] * k.c_in;
+        const float xa = xin * k.alpha;
+        const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * k.sigma;
+        const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * k.sigma;
+        const float cm = cx0 * mask[int64_t(b) * T + t];
+        s1 += double(cm) * cm;
+        s2 += double(cx0 - ux0) * cm;
+    }
+    __shared__ double r1[32], r2[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        r1[threadIdx.x >> 5] = s1;
+        r2[threadIdx.x >> 5] = s2;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = 0.0, c = 0.0;
+        for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+            a += r1[w];
+            c += r2[w];
+        }
+        const float n = sqrtf(float(a) + 1e-16f);
+        sums[2 * b] = n;
+        sums[2 * b + 1] = float(c) / n;  // dot(diff, x0_c m / n)
+    }
+}
+
+// Fused: CFG/APG combine (or the raw output without CFG), denoised = out * c_out + x * c_skip,
+// DPM++ 2M update of x [B, 64, T] (BCT), history, next step's input, non-finite check.
+template <typename CT>
+__global__ void dit_update_kernel(const float* __restrict__ part, int splits, int64_t split_stride,
+                                  float* __restrict__ x, float* __restrict__ old, const float* __restrict__ mask,
+                                  const float* __restrict__ sums, int B, int Bg, int T, int use_cfg,
+                                  const DitStepCoef* __restrict__ coefs, int step, CT* __restrict__ Xnext,
+                                  float* __restrict__ out, int* __restrict__ status) {
+    const DitStepCoef k = coefs[step];
+    const int64_t total = int64_t(B) * 64 * T;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int t = int(i % T);
+        const int c = int((i / T) % 64);
+        const int b = int(i / (int64_t(T) * 64));
+        const float xv = x[i];
+        float mo;
+        if (use_cfg) {
+            const float xa = (xv * k.c_in) * k.alpha;
+            const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * k.sigma;
+            const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * k.sigma;
+            const float diff = cx0 - ux0;
+            const float m = mask[int64_t(b) * T + t];
+            const float n = sums[2 * b], dot = sums[2 * b + 1];
+            const float v1 = (cx0 * m) / n;
+            const float orth = (diff - dot * v1) * m;
+            const float cd = k.apg_scale * orth + (1.0f - k.apg_scale) * diff;
+            const float den = cx0 + (k.cfg_scale - 1.0f) * cd;
+            mo = (xa - den) / k.sigma;
+        } else {
+            mo = dit_raw(part, splits, split_stride, b, T, t, c);
+        }
+        const float denoised = mo * k.c_out + xv * k.c_skip;
+        float nx;
+        if (k.final_step) {
+            nx = denoised;
+        } else {
+            const float dd = k.first_step ? denoised : k.d_coeff * denoised + k.old_coeff * old[i];
+            nx = k.x_scale * xv + k.d_scale * dd;
+            old[i] = denoised;
+        }
+        if (!isfinite(mo) || !isfinite(nx)) atomicCAS(status, 0, kErrNonFinite);
+        x[i] = nx;
+        if (k.final_step) {
+            out[i] = nx;
+        } else {
+            const CT h = from_f32<CT>(nx * k.c_in_next);
+            for (int bb = b; bb < Bg; bb += B) Xnext[(int64_t(bb) * T + t) * 64 + c] = h;
+        }
+    }
+}
+
+// x = noise * sigma_0   (rf_dit.cpp:810-813)
+__global__ void dit_init_kernel(const float* __restrict__ noise, int64_t n, const DitStepCoef* __restrict__ coefs,
+                                float* __restrict__ x) {
+    const float s0 = coefs[0].sig;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        x[i] = noise[i] * s0;
+}
+
+// Per hidden row padding factor: 1 for the global token, the latent mask for token rows
+// (make_padding_mask, rf_dit.cpp:1085-1095).
+__global__ void dit_padrow_kernel(const float* __restrict__ mask, int B, int Bg, int T, float* __restrict__ padrow) {
+    const int64_t total = int64_t(Bg) * (T + 1);
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int bb = int(i / (T + 1)), t = int(i % (T + 1));
+        padrow[i] = t == 0 ? 1.0f : mask[int64_t(bb % B) * T + t - 1];
+    }
+}
+
+}  // namespace b2d

@@ -40,6 +40,8 @@ struct EpiParams {
     int* status = nullptr;
     int splits = 1;             // split-K factor (EPI_F32 only): split s writes out + s * split_stride
     int64_t split_stride = 0;
+    int seg_rows = 0;           // EPI_F32 row remap: output row = r + (r / seg_rows + 1) * seg_pad
+    int seg_pad = 0;
 };
 
 template <typename CT>
@@ -275,11 +277,13 @@ __global__ void __launch_bounds__(192, 1)
                     for (int r = 0; r < 32; ++r) {
                         if (r < rows_live) {
                             const float x = stg[r * 33 + lane] + bcol;
-                            const int64_t row = rbase + r;
-                            if constexpr (EPI == EPI_F32)
+                            int64_t row = rbase + r;
+                            if constexpr (EPI == EPI_F32) {
+                                if (ep.seg_rows) row += (row / ep.seg_rows + 1) * ep.seg_pad;
                                 out_f32[row * ep.ldo + col] = x;
-                            else
+                            } else {
                                 reinterpret_cast<CT*>(ep.out)[row * ep.ldo + col] = CtTraits<CT>::cvt(x);
+                            }
                         }
                     }
                 }

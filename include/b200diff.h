@@ -140,6 +140,56 @@ B2D_API b2d_status b2d_vv_sample_device(b2d_ctx* ctx, const float* positive_cond
                                 const float* initial_speech, int64_t batch, int64_t steps, float cfg,
                                 float* out_latents, void* stream);
 
+/* -------------------------------------- Stable Audio Open 1.0 ("foundation") DiT */
+/* Mirrors the StableAudioConfig fields the foundation DiT uses
+ * (include/engine/models/stable_audio/assets.h:14-84).  head_dim = embed_dim / num_heads must be 64. */
+typedef struct {
+    int64_t embed_dim;          /* 1536 */
+    int64_t depth;              /* 24 */
+    int64_t num_heads;          /* 24 */
+    int64_t cond_token_dim;     /* 768: cross-attention KV heads = cond_token_dim / 64, repeated to num_heads */
+    int64_t global_cond_dim;    /* 1536 */
+    int64_t io_channels;        /* must be 64 */
+    int64_t prompt_max_length;  /* 128: cross tokens = prompt_max_length + 2 */
+} b2d_dit_config;
+
+enum { B2D_SAMPLER_DPMPP_2M = 0 };
+
+/* One FoundationRfDitRuntime::sample request (include/engine/models/stable_audio/foundation/rf_dit.h:73-106)
+ * with its StableAudioSamplingState / StableAudioConditioningInputs payloads (fp32, row-major):
+ *   noise [batch, 64, latent_tokens] (BCT), padding_mask [batch, latent_tokens],
+ *   cross_positive / cross_negative [batch, prompt_max_length + 2, cond_token_dim] (negative may be NULL: zeros),
+ *   global_cond [batch, global_cond_dim].
+ * CFG runs when cfg_scale != 1 (graph batch 2 * batch, APG with apg_scale), as the reference's graph cache key. */
+typedef struct {
+    int64_t batch;
+    int64_t latent_tokens;
+    int64_t steps;
+    const float* noise;
+    const float* padding_mask;
+    const float* cross_positive;
+    const float* cross_negative;
+    const float* global_cond;
+    float sigma_min, sigma_max, rho;
+    float cfg_scale, apg_scale;
+    int32_t sampler;            /* B2D_SAMPLER_DPMPP_2M ("dpmpp-2m") */
+} b2d_dit_request;
+
+/* Loads the DiT from its GGUF tensors ("model.model.*", names as load_foundation_rf_dit_weights,
+ * src/models/stable_audio/foundation/rf_dit.cpp:379-416).  Replaces the weight load in
+ * FoundationRfDitRuntime::prepare (rf_dit.cpp:1173-1180). */
+B2D_API b2d_status b2d_dit_load(b2d_ctx* ctx, const b2d_dit_config* config, const b2d_tensor_view* tensors,
+                                int32_t n_tensors);
+
+/* The whole sampling loop (Graph::sample_dpmpp_2m, rf_dit.cpp:798-883, with the in-graph CFG/APG of
+ * build_cfg_model_output, :988-1028) as one captured CUDA graph.  Host buffers; returns latents
+ * [batch, 64, latent_tokens] (BCT) in out_latents.  Replaces FoundationRfDitRuntime::sample. */
+B2D_API b2d_status b2d_dit_sample(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents, void* stream);
+
+/* Same with every pointer of the request and out_latents in device memory; asynchronous. */
+B2D_API b2d_status b2d_dit_sample_device(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents,
+                                         void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
@@ -161,6 +211,16 @@ enum {
 B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
                     int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);
+
+/* Flash attention, head_dim 64, scale 1/8: for each sequence s < nseq and head h < heads,
+ * O[s, :, h] = softmax(Q[s, :, h] K[s, :, h / kv_rep]^T / 8) V[s, :, h / kv_rep]
+ * (ggml_flash_attn_ext as rf_attention uses it, src/models/stable_audio/foundation/rf_dit.cpp:175-198).
+ * Q/K/V/O are device fp16 (bf16 = 0) or bf16 matrices; element (s, i, h, j) of Q sits at
+ * q + s * q_seq + i * q_row + h * 64 + j (strides in elements), likewise K, V (kv_*) and O (o_*). */
+B2D_API b2d_status b2d_attention(b2d_ctx* ctx, int32_t bf16, const void* q, int64_t q_row, int64_t q_seq,
+                                 const void* k, const void* v, int64_t kv_row, int64_t kv_seq, void* o,
+                                 int64_t o_row, int64_t o_seq, int32_t lq, int32_t lk, int32_t heads, int32_t kv_rep,
+                                 int32_t nseq, void* stream);
 
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot

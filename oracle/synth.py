@@ -182,6 +182,9 @@ class DitConfig:
 DIT_CONFIGS = {
     "sao_bf16_1x1024": DitConfig(),
     "sao_q8_16x1024": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16))),
+    # full-size parity cases (BASELINE C3/C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
+    "sao_bf16_1x1024_2steps": DitConfig(steps=2),
+    "sao_q8_1x1024_2steps": DitConfig(wtype=Q8_0, steps=2, prompt_seeds=(5,)),
     "tiny_bf16": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
                            prompt_max_length=14, latent_tokens=64, steps=6),
     "tiny_q8_b2_noapg": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
@@ -201,7 +204,10 @@ def dit_weights(cfg: DitConfig) -> Dict[str, B.Tensor]:
 
     def lin(name, out, inp, bias=False, conv=False):
         shape = (out, inp, 1) if conv else (out, inp)
-        w[DP + name + ".weight"] = encode_weight(_normal(rng, shape, 0.02), cfg.wtype)
+        # a [out, in, 1] conv weight has last dim 1, which GGUF cannot store as Q8_0 blocks;
+        # the reference's weight store keeps such tensors in F32 (backend_weight_store.h:237-255)
+        wtype = F32 if (conv and cfg.wtype == Q8_0) else cfg.wtype
+        w[DP + name + ".weight"] = encode_weight(_normal(rng, shape, 0.02), wtype)
         if bias:
             w[DP + name + ".bias"] = B.f32(_normal(rng, (out,), 0.02))
 

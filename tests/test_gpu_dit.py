@@ -1,0 +1,105 @@
+"""GPU parity of the Stable Audio Open 1.0 DiT path through the C ABI:
+* the flash-attention kernel against a torch fp32 softmax(QK^T/8)V (self-attention
+  shape, and the cross-attention shape with 130 keys and repeated KV heads);
+* whole DPM++ 2M sampling runs against the reference's own ggml CPU outputs
+  (tests/golden/dit_*.b2db) and the fp32-activation numpy restatement.
+
+Latent tolerance (rel-L2): vs the reference max(2e-2, 1.5 x spread) where spread is
+the reference's distance to the same arithmetic without its activation rounding;
+vs the fp32-activation restatement 2e-2 (bf16 operands) / 1e-2 (fp16 operands).
+"""
+import numpy as np
+import pytest
+
+from oracle import synth
+from tests.helpers import golden, rel_l2, weight_specs
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _attn_ref(q, k, v, rep):
+    # q [S, Lq, H, 64], k/v [S, Lk, KVH, 64]
+    k = k.float().repeat_interleave(rep, dim=2)
+    v = v.float().repeat_interleave(rep, dim=2)
+    s = torch.einsum("sqhd,skhd->shqk", q.float(), k) / 8.0
+    return torch.einsum("shqk,skhd->sqhd", torch.softmax(s, dim=-1), v)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("lq,lk,heads,rep,nseq", [(1025, 1025, 4, 1, 2), (1025, 130, 4, 2, 2), (37, 16, 2, 1, 3),
+                                                  (200, 64, 3, 3, 1)])
+def test_attention_kernel(ctx, bf16, lq, lk, heads, rep, nseq):
+    dt = torch.bfloat16 if bf16 else torch.float16
+    g = torch.Generator(device="cuda").manual_seed(lq + lk)
+    q = torch.randn(nseq, lq, heads, 64, device="cuda", generator=g).to(dt)
+    k = torch.randn(nseq, lk, heads // rep, 64, device="cuda", generator=g).to(dt)
+    v = torch.randn(nseq, lk, heads // rep, 64, device="cuda", generator=g).to(dt)
+    o = torch.zeros(nseq, lq, heads, 64, device="cuda", dtype=dt)
+    ctx.attention(q.data_ptr(), heads * 64, lq * heads * 64, k.data_ptr(), v.data_ptr(), (heads // rep) * 64,
+                  lk * (heads // rep) * 64, o.data_ptr(), heads * 64, lq * heads * 64, lq, lk, heads, rep, nseq,
+                  bf16=bf16)
+    torch.cuda.synchronize()
+    ref = _attn_ref(q, k, v, rep)
+    err = float((o.float() - ref).norm() / ref.norm())
+    assert err < (1e-2 if bf16 else 2e-3), err
+
+
+_dits = {}
+
+
+def make_dit(b2d, ctx, name):
+    if name not in _dits:
+        cfg = synth.DIT_CONFIGS[name]
+        w = synth.dit_weights(cfg)
+        _dits.clear()
+        _dits[name] = (cfg, b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim,
+                                               cfg.global_cond_dim, cfg.io_channels, cfg.prompt_max_length,
+                                               weights=weight_specs(w)))
+    return _dits[name]
+
+
+def run(cfg, dit, inp):
+    return dit.sample(inp["noise"].array(), inp["padding_mask"].array(), inp["cross_positive"].array(),
+                      inp["cross_negative"].array(), inp["global"].array(), steps=cfg.steps,
+                      sigma_min=cfg.sigma_min, sigma_max=cfg.sigma_max, rho=cfg.rho, cfg_scale=cfg.cfg,
+                      apg_scale=cfg.apg)
+
+
+@pytest.mark.parametrize("name", ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "sao_bf16_1x1024_2steps",
+                                  "sao_q8_1x1024_2steps"])
+def test_dit_sample_matches_reference(b2d, ctx, name):
+    cfg, dit = make_dit(b2d, ctx, name)
+    inp = synth.dit_inputs(cfg)
+    out = run(cfg, dit, inp)
+    g = golden("dit_" + name)
+    ref, exact = g["latents"].array(), g["exact_latents"].array()
+    assert np.isfinite(out).all()
+    spread = rel_l2(exact, ref)
+    err = rel_l2(out, ref)
+    err_exact = rel_l2(out, exact)
+    print("%s: vs ref %.3g (spread %.3g), vs exact %.3g" % (name, err, spread, err_exact))
+    assert err < max(2e-2, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
+    assert err_exact < (2e-2 if cfg.wtype == synth.BF16 else 1e-2), "rel-L2 %.3g vs exact oracle" % err_exact
+    out2 = run(cfg, dit, inp)
+    assert np.array_equal(out, out2)
+
+
+def test_dit_without_cfg_and_device_api(b2d, ctx):
+    cfg, dit = make_dit(b2d, ctx, "tiny_bf16")
+    inp = synth.dit_inputs(cfg)
+    host = dit.sample(inp["noise"].array(), inp["padding_mask"].array(), inp["cross_positive"].array(), None,
+                      inp["global"].array(), steps=3, cfg_scale=1.0)
+    assert np.isfinite(host).all()
+    from oracle import dit as D
+    cfg1 = synth.DitConfig(**{**cfg.__dict__, "steps": 3, "cfg": 1.0})
+    ref = D.sample_dpmpp_2m(D.Dit(synth.dit_weights(cfg), cfg1, act="exact"), cfg1, inp)
+    assert rel_l2(host, ref) < 2e-2
+    dev = [torch.from_numpy(inp[k].array().copy()).cuda() for k in ("noise", "padding_mask", "cross_positive",
+                                                                    "global")]
+    out = torch.empty_like(dev[0])
+    dit.sample_device(dev[0], dev[1], dev[2], None, dev[3], out, steps=3, cfg_scale=1.0,
+                      stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    ctx.sync()
+    assert np.array_equal(out.cpu().numpy(), host)
