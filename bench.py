@@ -170,6 +170,143 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
             "traffic": None}
 
 
+DIT_WORKLOAD = "sao_bf16_1x1024"
+
+
+def gemm_time(b2d, ctx, torch, M, N, K, epilogue, bn=256, bf16=False, reps=30):
+    """Average device time of one tcgen05 GEMM launch (CUDA events on the launching stream)."""
+    dt = torch.bfloat16 if bf16 else torch.float16
+    a = torch.randn(M, K, device="cuda").to(dt)
+    w = (torch.randn(N, K, device="cuda") * 0.02).to(dt)
+    out = torch.empty(M, N, device="cuda")
+    st = torch.cuda.current_stream()
+    ldo = N // 2 if epilogue == b2d.EPI_SWIGLU else N
+    launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, bf16=bf16, epilogue=epilogue, bn=bn,
+                              out=out.data_ptr(), ldo=ldo, stream=st.cuda_stream)
+    for _ in range(3):
+        launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        launch()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps / 1e3
+
+
+def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
+    """C3: Stable-Audio-Open-1.0 DiT, BF16, 1 prompt + CFG (2 sequences) x 1024 frames, 100-step DPM++ 2M,
+    CFG 7, APG 1.  Per rank its own prompt (weak scaling).  Metric: sequence-steps/s over all ranks."""
+    from oracle import synth
+    cfg = synth.DIT_CONFIGS[DIT_WORKLOAD]
+    cfg = synth.DitConfig(**{**cfg.__dict__, "prompt_seeds": (rank,)})
+    w = synth.dit_weights(cfg)
+    gt = {0: 0, 1: 1, 3: 8, 2: 30}
+    dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
+                             cfg.io_channels, cfg.prompt_max_length,
+                             weights=[(n, gt[t.dtype], t.dims, t.data) for n, t in w.items()])
+    del w
+    inp = synth.dit_inputs(cfg)
+    keys = ("noise", "padding_mask", "cross_positive", "cross_negative", "global")
+    dev = [torch.from_numpy(inp[k].array().copy()).cuda() for k in keys]
+    host = [torch.from_numpy(inp[k].array().copy()).pin_memory() for k in keys]
+    out_dev = torch.empty_like(dev[0])
+    out_host = torch.empty(dev[0].shape).pin_memory()
+    st = torch.cuda.current_stream()
+    kw = dict(steps=cfg.steps, sigma_min=cfg.sigma_min, sigma_max=cfg.sigma_max, rho=cfg.rho, cfg_scale=cfg.cfg,
+              apg_scale=cfg.apg, stream=st.cuda_stream)
+    calls, warm = max(1, min(args.steps, args.dit_steps)), max(1, min(args.warmup, args.dit_warmup))
+    ms = timed(lambda: dit.sample_device(*dev, out_dev, **kw), calls, warm)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(lambda: dit.sample(*host, out=out_host, **kw), calls, 1)
+    seq_steps = 2 * cfg.batch * cfg.steps * world
+    res = {"metric": "denoise sequence-steps/sec (DiT)", "value": round(seq_steps / (ms / 1e3), 2),
+           "unit": "seq-steps/s", "ms_per_call": round(ms, 2), "timed_calls": calls, "warmup_calls": warm,
+           "prompt_steps_per_s": round(seq_steps / 2 / (ms / 1e3), 2),
+           "config": {"workload": DIT_WORKLOAD, "model": "Stable-Audio-Open-1.0-shaped DiT (random-init)",
+                      "weights": cfg.wtype, "sequences_per_rank": 2 * cfg.batch, "tokens": cfg.latent_tokens + 1,
+                      "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg, "apg_scale": cfg.apg, "n_gpus": world},
+           "dtype": "bf16 tensor-core operands, fp32 accumulate",
+           "e2e": {"value": round(seq_steps / (ms_e2e / 1e3), 2), "unit": "seq-steps/s",
+                   "h2d_bytes_per_step": sum(t.numel() * 4 for t in host), "d2h_bytes_per_step": out_host.numel() * 4,
+                   "api": "b2d_dit_sample (host buffers, pinned)"},
+           "gpu_launches_per_call": 14 + cfg.steps * (4 + cfg.depth * 11) + 2 * cfg.steps,
+           "whole_call_tflops": round(2 * cfg.batch * cfg.steps * 2.264e12 / (ms / 1e3) / 1e12, 1)}
+    assert np.isfinite(out_host.numpy()).all()
+    if rank == 0:
+        R = 2 * cfg.batch * (cfg.latent_tokens + 1)
+        t_ff = gemm_time(b2d, ctx, torch, R, 8 * cfg.embed_dim, cfg.embed_dim, b2d.EPI_SWIGLU, bf16=True)
+        fl = 2.0 * R * 8 * cfg.embed_dim * cfg.embed_dim
+        peak = peaks.get("bf16_tflops", 1590.0)
+        res["roofline"] = {"kernel": "gemm_tc_kernel<256,SWIGLU,bf16> (FFN in, %dx%dx%d)" % (R, 8 * cfg.embed_dim,
+                                                                                            cfg.embed_dim),
+                           "bound": "tensor", "achieved": round(fl / t_ff / 1e12, 1), "peak": peak,
+                           "unit": "TFLOP/s", "frac": round(fl / t_ff / 1e12 / peak, 4), "traffic": None}
+        if not args.no_cpu_baseline:
+            from oracle import ref_runner
+            if ref_runner.available():
+                c1 = synth.DitConfig(**{**cfg.__dict__, "steps": 1})
+                o = ref_runner.run("dit", synth.dit_inputs(c1), synth.dit_weights(c1), reps=1)
+                cms = float(o["wall_ms"].data[0])
+                res["cpu_baseline"] = {"value": round(2 * cfg.batch / (cms / 1e3), 4), "unit": "seq-steps/s",
+                                       "cores": os.cpu_count(), "kind": "reference",
+                                       "sample": "1 DPM++ step of the 2-sequence C3 workload, audio.cpp ggml CPU (%s)"
+                                                 % ref_runner.variant()}
+    return res
+
+
+def make_timer(torch, args, world, st):
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(call, steps, warmup):
+        for _ in range(warmup):
+            call()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        total = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            call()
+            e1.record(st)
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        return max_over_ranks(total / steps)
+    return timed
+
+
+def bench_dit_only(args, torch, b2d, world, rank, local):
+    """--workload dit: time only the DiT (used for DiT profiling); prints the DiT result as the line."""
+    ctx = b2d.Context(local)
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        peaks = {}
+    st = torch.cuda.current_stream()
+    with ClockSampler(local) as clk:
+        res = bench_dit(args, torch, b2d, ctx, world, rank, make_timer(torch, args, world, st), peaks)
+    if rank == 0:
+        res.update({"n_gpus": world, "steps": res["timed_calls"], "warmup": res["warmup_calls"],
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "data": "synthetic (seeded random weights and inputs)", "clocks": clk.summary()})
+        print(json.dumps(res))
+    ctx.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def bench_ours(args):
     import torch
     world, rank, local = dist_setup()
@@ -180,6 +317,8 @@ def bench_ours(args):
     b2d = load_package()
     from oracle import synth  # seeded synthetic weights/inputs (no checkpoints here)
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
+    if args.workload == "dit":
+        return bench_dit_only(args, torch, b2d, world, rank, local)
     w = synth.head_weights(cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
@@ -207,14 +346,15 @@ def bench_ours(args):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         return float(t.item())
 
-    def timed(call):
-        for _ in range(args.warmup):
+    def timed(call, steps=None, warmup=None):
+        steps = args.steps if steps is None else steps
+        for _ in range(args.warmup if warmup is None else warmup):
             call()
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         total = 0.0
-        for _ in range(args.steps):
+        for _ in range(steps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
@@ -224,7 +364,7 @@ def bench_ours(args):
             total += e0.elapsed_time(e1)
         torch.cuda.synchronize()
         barrier()
-        return max_over_ranks(total / args.steps)
+        return max_over_ranks(total / steps)
 
     dev_call = lambda: head.sample_device(*dev, cfg.steps, cfg.cfg, out_dev, stream=st.cuda_stream)
     host_call = lambda: head.sample(*host, cfg.steps, cfg.cfg, out=out_host, stream=st.cuda_stream)
@@ -241,11 +381,14 @@ def bench_ours(args):
     d2h = out_host.numel() * 4
     launches_per_call = 5 + cfg.steps * (3 * cfg.layers + 6)
 
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        peaks = {}
+    dit_res = None
+    if args.workload in ("all", "dit"):
+        dit_res = bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks)
     if rank == 0:
-        try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except (OSError, ValueError):
-            peaks = {}
         roof = gemm_roofline(b2d, ctx, torch, cfg, peaks)
         flops_call = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
         line = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -266,6 +409,8 @@ def bench_ours(args):
             line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
                                     "sample": "%d of the 1024 frames, 10 DPM steps + CFG, audio.cpp ggml CPU (%s), "
                                               "1 warm-up + 1 timed call" % (frames, variant)}
+        if dit_res is not None:
+            line["dit"] = dit_res
         print(json.dumps(line))
     ctx.close()
     if world > 1:
@@ -279,6 +424,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="all", choices=["all", "head", "dit"],
+                    help="head = VibeVoice head (headline metric); dit = also/only time the Stable Audio DiT")
+    ap.add_argument("--dit-steps", type=int, default=3, help="timed DiT sampling calls (each 100 DPM++ steps)")
+    ap.add_argument("--dit-warmup", type=int, default=1)
     args = ap.parse_args()
     if args.impl == "reference":
         bench_reference(args)
