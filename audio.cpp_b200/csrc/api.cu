@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -678,6 +679,7 @@ b2d_status b2d_create(int device, b2d_ctx** out) {
         CK(cudaMemset(ctx->status.p, 0, 256));
         CK(cudaStreamCreateWithFlags(&ctx->load_stream, cudaStreamNonBlocking));
         encode_fn();
+        if (const char* mt = std::getenv("B2D_ATTN_MT")) g_attn_mt = std::atoi(mt);
     });
     if (s != B2D_OK) return s;
     *out = ctx.release();

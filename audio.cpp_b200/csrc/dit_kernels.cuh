@@ -66,40 +66,6 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const float* __restrict_
     }
 }
 
-// In-place on the fused qkv rows [rows, 3d] (row = seq * L + pos): NEOX RoPE on the first
-// 2*half dims of every q and k head (pairs (i, i + half)), V scaled by the padding mask.
-// cos/sin tables [L, half] follow ggml's rope cache (theta_i = pos * scale^i in fp32).
-template <typename CT>
-__global__ void rope_mask_kernel(CT* __restrict__ qkv, int64_t rows, int L, int d, int heads, int half,
-                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                 const float* __restrict__ pad) {
-    const int64_t total = rows * heads;
-    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t row = i / heads;
-        const int h = int(i % heads);
-        const int pos = int(row % L);
-        CT* base = qkv + row * 3 * d + h * 64;
-        const float* c = cos_t + pos * half;
-        const float* s = sin_t + pos * half;
-#pragma unroll 4
-        for (int j = 0; j < half; ++j) {
-            const float cj = c[j], sj = s[j];
-            float x0 = to_f32(base[j]), x1 = to_f32(base[j + half]);
-            base[j] = from_f32<CT>(x0 * cj - x1 * sj);
-            base[j + half] = from_f32<CT>(x0 * sj + x1 * cj);
-            x0 = to_f32(base[d + j]);
-            x1 = to_f32(base[d + j + half]);
-            base[d + j] = from_f32<CT>(x0 * cj - x1 * sj);
-            base[d + j + half] = from_f32<CT>(x0 * sj + x1 * cj);
-        }
-        const float m = pad[row];
-        if (m != 1.0f) {
-            CT* vb = base + 2 * d;
-            for (int j = 0; j < 64; ++j) vb[j] = from_f32<CT>(to_f32(vb[j]) * m);
-        }
-    }
-}
-
 // Global-token rows: h[seq, 0, :] = gpre[seq, :] + temb[step, :]   (rf_dit.cpp:545-552)
 __global__ void dit_global_row_kernel(float* __restrict__ h, int64_t seq_rows, const float* __restrict__ gpre,
                                       const float* __restrict__ temb, int d, int nseq) {
@@ -158,15 +124,22 @@ __device__ __forceinline__ float dit_raw(const float* part, int splits, int64_t 
 }
 
 // APG reductions per prompt b: s1 = sum (x0_c * m)^2, s2 = sum (x0_c - x0_u) * (x0_c * m).
-__global__ void __launch_bounds__(1024) dit_apg_reduce_kernel(const float* __restrict__ part, int splits,
+// Stage 1: kApgChunks CTAs per prompt each reduce a contiguous slice in double; stage 2 folds the
+// chunk partials in a fixed order (deterministic) and writes n = sqrt(s1 + 1e-16), dot = s2 / n.
+constexpr int kApgChunks = 64;
+
+__global__ void __launch_bounds__(256) dit_apg_partial_kernel(const float* __restrict__ part, int splits,
                                                               int64_t split_stride, const float* __restrict__ x,
                                                               const float* __restrict__ mask, int B, int T,
                                                               const DitStepCoef* __restrict__ coefs, int step,
-                                                              float* __restrict__ sums) {
+                                                              double* __restrict__ partials) {
     const DitStepCoef k = coefs[step];
-    const int b = blockIdx.x;
+    const int b = blockIdx.y, chunk = blockIdx.x;
+    const int n = T * 64;
+    const int per = (n + kApgChunks - 1) / kApgChunks;
+    const int i0 = chunk * per, i1 = min(n, i0 + per);
     double s1 = 0.0, s2 = 0.0;
-    for (int i = threadIdx.x; i < T * 64; i += blockDim.x) {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const int t = i / 64, c = i % 64;
         const float xin = x[(int64_t(b) * 64 + c) * T + t] * k.c_in;
         const float xa = xin * k.alpha;
@@ -176,7 +149,7 @@ __global__ void __launch_bounds__(1024) dit_apg_reduce_kernel(const float* __res
         s1 += double(cm) * cm;
         s2 += double(cx0 - ux0) * cm;
     }
-    __shared__ double r1[32], r2[32];
+    __shared__ double r1[8], r2[8];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         s1 += __shfl_xor_sync(0xffffffffu, s1, o);
@@ -189,13 +162,26 @@ __global__ void __launch_bounds__(1024) dit_apg_reduce_kernel(const float* __res
     __syncthreads();
     if (threadIdx.x == 0) {
         double a = 0.0, c = 0.0;
-        for (int w = 0; w < int(blockDim.x >> 5); ++w) {
+        for (int w = 0; w < 8; ++w) {
             a += r1[w];
             c += r2[w];
         }
-        const float n = sqrtf(float(a) + 1e-16f);
-        sums[2 * b] = n;
-        sums[2 * b + 1] = float(c) / n;  // dot(diff, x0_c m / n)
+        partials[(int64_t(b) * kApgChunks + chunk) * 2] = a;
+        partials[(int64_t(b) * kApgChunks + chunk) * 2 + 1] = c;
+    }
+}
+
+__global__ void dit_apg_finish_kernel(const double* __restrict__ partials, float* __restrict__ sums) {
+    const int b = blockIdx.x;
+    if (threadIdx.x == 0) {
+        double a = 0.0, c = 0.0;
+        for (int i = 0; i < kApgChunks; ++i) {
+            a += partials[(int64_t(b) * kApgChunks + i) * 2];
+            c += partials[(int64_t(b) * kApgChunks + i) * 2 + 1];
+        }
+        const float nrm = sqrtf(float(a) + 1e-16f);
+        sums[2 * b] = nrm;
+        sums[2 * b + 1] = float(c) / nrm;
     }
 }
 

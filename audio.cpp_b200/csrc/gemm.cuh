@@ -42,6 +42,14 @@ struct EpiParams {
     int64_t split_stride = 0;
     int seg_rows = 0;           // EPI_F32 row remap: output row = r + (r / seg_rows + 1) * seg_pad
     int seg_pad = 0;
+    // EPI_CT on a fused [q | k | v] projection: NEOX RoPE on dims [0, 32) of every 64-wide head in
+    // columns < rope_cols (pairs j, j + 16), position = row % rope_L, tables [rope_L, 16];
+    // columns >= rope_cols (V) are scaled by vmask[row].
+    const float* rope_cos = nullptr;
+    const float* rope_sin = nullptr;
+    int rope_L = 0;
+    int rope_cols = 0;
+    const float* vmask = nullptr;
 };
 
 template <typename CT>
@@ -234,6 +242,25 @@ __global__ void __launch_bounds__(192, 1)
                     const int row = rbase + lane;
                     if (lane < rows_live) {
                         const int col0 = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32;
+                        if (EPI == EPI_CT && ep.rope_cos) {
+                            if (col0 < ep.rope_cols) {
+                                if ((col0 & 63) == 0) {
+                                    const int pos = row % ep.rope_L;
+                                    const float* cs = ep.rope_cos + pos * 16;
+                                    const float* sn = ep.rope_sin + pos * 16;
+#pragma unroll
+                                    for (int j = 0; j < 16; ++j) {
+                                        const float x0 = v[j], x1 = v[j + 16], cj = __ldg(cs + j), sj = __ldg(sn + j);
+                                        v[j] = x0 * cj - x1 * sj;
+                                        v[j + 16] = x0 * sj + x1 * cj;
+                                    }
+                                }
+                            } else if (ep.vmask) {
+                                const float mv = __ldg(ep.vmask + row);
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) v[j] *= mv;
+                            }
+                        }
                         if (EPI == EPI_CT && ep.bias) {
 #pragma unroll
                             for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + col0 + j);

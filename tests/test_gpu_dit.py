@@ -6,7 +6,8 @@
 
 Latent tolerance (rel-L2): vs the reference max(2e-2, 1.5 x spread) where spread is
 the reference's distance to the same arithmetic without its activation rounding;
-vs the fp32-activation restatement 2e-2 (bf16 operands) / 1e-2 (fp16 operands).
+vs the fp32-activation restatement max(2e-2 (bf16 operands) / 1e-2 (fp16 operands), 1.5 x spread):
+from sigma_max = 100 a 2-step run amplifies bf16 activation rounding to ~3.4 % in the reference itself.
 """
 import numpy as np
 import pytest
@@ -80,7 +81,8 @@ def test_dit_sample_matches_reference(b2d, ctx, name):
     err_exact = rel_l2(out, exact)
     print("%s: vs ref %.3g (spread %.3g), vs exact %.3g" % (name, err, spread, err_exact))
     assert err < max(2e-2, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
-    assert err_exact < (2e-2 if cfg.wtype == synth.BF16 else 1e-2), "rel-L2 %.3g vs exact oracle" % err_exact
+    assert err_exact < max(2e-2 if cfg.wtype == synth.BF16 else 1e-2, 1.5 * spread), \
+        "rel-L2 %.3g vs exact oracle (spread %.3g)" % (err_exact, spread)
     out2 = run(cfg, dit, inp)
     assert np.array_equal(out, out2)
 
