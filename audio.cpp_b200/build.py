@@ -37,14 +37,37 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= t for p in DEPS if os.path.exists(p))
 
 
+ENGINE_LIB = os.path.join(HERE, "libb2d_engine.so")
+ENGINE_TEST = os.path.join(HERE, "test_engine")
+HOST = os.path.join(HERE, "host")
+
+
+def build_host(force: bool = False, verbose: bool = False) -> None:
+    """The audio.cpp-facing C++ classes (host/engine_b200.*) as libb2d_engine.so, and their C++ test."""
+    srcs = [os.path.join(HOST, f) for f in ("engine_b200.cpp", "engine_b200.h")]
+    newest = max(os.path.getmtime(p) for p in srcs + [LIB, os.path.join(HOST, "test_engine.cpp")])
+    if not force and os.path.exists(ENGINE_TEST) and os.path.exists(ENGINE_LIB) and \
+            min(os.path.getmtime(ENGINE_LIB), os.path.getmtime(ENGINE_TEST)) >= newest:
+        return
+    common = ["g++", "-std=c++17", "-O2", "-fPIC", "-Wall"]
+    cmds = [common + ["-shared", "-o", ENGINE_LIB, os.path.join(HOST, "engine_b200.cpp"), "-L" + HERE, "-lb200diff",
+                      "-Wl,-rpath,$ORIGIN"],
+            common + ["-o", ENGINE_TEST, os.path.join(HOST, "test_engine.cpp"), "-L" + HERE, "-lb2d_engine",
+                      "-lb200diff", "-Wl,-rpath,$ORIGIN"]]
+    for cmd in cmds:
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return LIB
-    cmd = [nvcc()] + NVCC_FLAGS + ["-o", LIB + ".tmp"] + SOURCES
-    if verbose:
-        print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
-    os.replace(LIB + ".tmp", LIB)
+    if force or not up_to_date():
+        cmd = [nvcc()] + NVCC_FLAGS + ["-o", LIB + ".tmp"] + SOURCES
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        os.replace(LIB + ".tmp", LIB)
+    build_host(force, verbose)
     return LIB
 
 

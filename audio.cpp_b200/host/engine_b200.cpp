@@ -1,0 +1,230 @@
+// Implementation of the audio.cpp-facing C++ classes (engine_b200.h) over the b200diff C ABI.
+#include "engine_b200.h"
+
+#include <stdexcept>
+#include <string>
+
+namespace engine::b200 {
+
+Device::Device(int device) {
+    const b2d_status s = b2d_create(device, &ctx_);
+    if (s != B2D_OK) {
+        throw std::runtime_error("b200diff: no usable sm_100 device " + std::to_string(device) + " (status " +
+                                 std::to_string(s) + ")");
+    }
+}
+
+Device::~Device() { b2d_destroy(ctx_); }
+
+void Device::check(b2d_status status) const {
+    if (status != B2D_OK) throw std::runtime_error(b2d_last_error(ctx_));
+}
+
+std::vector<b2d_tensor_view> views_of(const std::vector<RawTensor> & tensors) {
+    std::vector<b2d_tensor_view> views;
+    views.reserve(tensors.size());
+    for (const auto & t : tensors) {
+        b2d_tensor_view v{};
+        v.name = t.name.c_str();
+        v.ggml_type = t.ggml_type;
+        v.ndim = static_cast<int32_t>(t.dims.size());
+        for (size_t i = 0; i < t.dims.size() && i < 4; ++i) v.dims[i] = t.dims[i];
+        v.data = t.bytes.data();
+        v.nbytes = t.bytes.size();
+        views.push_back(v);
+    }
+    return views;
+}
+
+}  // namespace engine::b200
+
+namespace engine::models::vibevoice {
+
+// ----------------------------------------------------------------- scheduler
+// Validation and messages as VibeVoiceDPMSolverScheduler (src/models/vibevoice/scheduler.cpp:95-274).
+VibeVoiceDPMSolverScheduler::VibeVoiceDPMSolverScheduler(const VibeVoiceDiffusionHeadConfig & config)
+    : config_(config) {
+    if (config_.diffusion_type != "ddpm") throw std::runtime_error("VibeVoice scheduler only supports ddpm diffusion_type");
+    if (config_.ddpm_beta_schedule != "cosine")
+        throw std::runtime_error("VibeVoice scheduler only supports cosine beta schedule");
+    if (config_.prediction_type != "v_prediction")
+        throw std::runtime_error("VibeVoice scheduler only supports v_prediction");
+    if (config_.ddpm_num_steps <= 0 || config_.ddpm_num_inference_steps <= 0)
+        throw std::runtime_error("VibeVoice scheduler requires positive DDPM step counts");
+}
+
+void VibeVoiceDPMSolverScheduler::set_timesteps(int64_t inference_steps) {
+    if (inference_steps <= 0) throw std::runtime_error("VibeVoice scheduler inference steps must be positive");
+    table_.assign(static_cast<size_t>(inference_steps), b2d_vv_step{});
+    if (b2d_vv_schedule(config_.ddpm_num_steps, inference_steps, table_.data()) != B2D_OK)
+        throw std::runtime_error("VibeVoice scheduler requires positive timestep counts");
+    timesteps_.clear();
+    for (const auto & s : table_) timesteps_.push_back(s.timestep);
+    reset_step_state();
+}
+
+void VibeVoiceDPMSolverScheduler::reset_step_state() {
+    previous_.clear();
+    step_index_ = -1;
+}
+
+VibeVoiceSchedulerStepResult VibeVoiceDPMSolverScheduler::step(const std::vector<float> & model_output,
+                                                               int64_t timestep, const std::vector<float> & sample) {
+    if (table_.empty()) throw std::runtime_error("VibeVoice scheduler set_timesteps must be called before step");
+    if (model_output.size() != sample.size())
+        throw std::runtime_error("VibeVoice scheduler size mismatch for convert_model_output");
+    if (step_index_ < 0) {
+        step_index_ = static_cast<int64_t>(timesteps_.size()) - 1;
+        for (size_t i = 0; i < timesteps_.size(); ++i)
+            if (timesteps_[i] == timestep) {
+                step_index_ = static_cast<int64_t>(i);
+                break;
+            }
+    }
+    if (step_index_ >= static_cast<int64_t>(table_.size()))
+        throw std::runtime_error("VibeVoice scheduler step index is invalid");
+    const b2d_vv_step & s = table_[static_cast<size_t>(step_index_)];
+    std::vector<float> conv(sample.size()), out(sample.size());
+    for (size_t i = 0; i < sample.size(); ++i) conv[i] = s.alpha_s * sample[i] - s.sigma_s * model_output[i];
+    if (s.order == 1 || previous_.size() != sample.size()) {
+        for (size_t i = 0; i < sample.size(); ++i) out[i] = s.sample_coeff * sample[i] + s.d0_coeff * conv[i];
+    } else {
+        for (size_t i = 0; i < sample.size(); ++i) {
+            const float d1 = s.inv_r0 * (conv[i] - previous_[i]);
+            out[i] = s.sample_coeff * sample[i] + s.d0_coeff * conv[i] + 0.5F * s.d0_coeff * d1;
+        }
+    }
+    previous_ = std::move(conv);
+    ++step_index_;
+    return {std::move(out)};
+}
+
+// ------------------------------------------------------------ head runtime
+VibeVoiceDiffusionHeadWeightsRuntime::VibeVoiceDiffusionHeadWeightsRuntime(
+    const VibeVoiceDiffusionHeadConfig & config, const std::vector<engine::b200::RawTensor> & tensors, int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    const auto views = engine::b200::views_of(tensors);
+    const b2d_vv_head_config c{config.hidden_size, config.latent_size, config.head_layers, config.head_ffn_ratio,
+                               config.rms_norm_eps, config.ddpm_num_steps};
+    device_->check(b2d_vv_head_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+VibeVoiceDiffusionPrediction VibeVoiceDiffusionHeadWeightsRuntime::predict(
+    const std::vector<float> & noisy_images, int64_t frames, int64_t latent_size, float timestep,
+    const std::vector<float> & condition, int64_t condition_hidden_size) const {
+    if (frames <= 0 || latent_size != config_.latent_size || condition_hidden_size != config_.hidden_size)
+        throw std::runtime_error("VibeVoice diffusion head received invalid input shape");
+    if (static_cast<int64_t>(noisy_images.size()) != frames * latent_size)
+        throw std::runtime_error("VibeVoice diffusion head noisy latent payload size mismatch");
+    if (static_cast<int64_t>(condition.size()) != frames * condition_hidden_size)
+        throw std::runtime_error("VibeVoice diffusion head condition payload size mismatch");
+    VibeVoiceDiffusionPrediction out;
+    out.frames = frames;
+    out.latent_size = latent_size;
+    out.values.resize(static_cast<size_t>(frames * latent_size));
+    device_->check(b2d_vv_predict(device_->ctx(), noisy_images.data(), frames, latent_size, timestep,
+                                  condition.data(), condition_hidden_size, out.values.data(), nullptr));
+    return out;
+}
+
+// Validation and messages as sample_vibevoice_speech_latents (src/models/vibevoice/diffusion_sampler.cpp:79-121);
+// the step loop itself runs on the GPU (b2d_vv_sample).
+std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
+    const VibeVoiceDiffusionHeadWeightsRuntime & prediction_head, VibeVoiceDPMSolverScheduler & scheduler,
+    const VibeVoiceSpeechDiffusionInput & input) {
+    if (input.batch_size <= 0 || input.hidden_size <= 0 || input.latent_size <= 0)
+        throw std::runtime_error("VibeVoice diffusion sampler requires positive dimensions");
+    if (input.inference_steps <= 0)
+        throw std::runtime_error("VibeVoice diffusion sampler requires positive inference steps");
+    auto require = [](const std::vector<float> & v, int64_t n, const char * label) {
+        if (static_cast<int64_t>(v.size()) != n)
+            throw std::runtime_error(std::string("VibeVoice diffusion sampler payload size mismatch for ") + label);
+    };
+    require(input.positive_condition, input.batch_size * input.hidden_size, "positive_condition");
+    require(input.negative_condition, input.batch_size * input.hidden_size, "negative_condition");
+    require(input.initial_speech, 2 * input.batch_size * input.latent_size, "initial_speech");
+    if (static_cast<int64_t>(scheduler.timesteps().size()) != input.inference_steps)
+        throw std::runtime_error("VibeVoice diffusion scheduler timesteps do not match request inference steps");
+    if (input.hidden_size != prediction_head.config().hidden_size ||
+        input.latent_size != prediction_head.config().latent_size)
+        throw std::runtime_error("VibeVoice diffusion head received invalid input shape");
+    scheduler.reset_step_state();
+    std::vector<float> latents(static_cast<size_t>(input.batch_size * input.latent_size));
+    prediction_head.check(b2d_vv_sample(prediction_head.ctx(), input.positive_condition.data(),
+                                        input.negative_condition.data(), input.initial_speech.data(),
+                                        input.batch_size, input.inference_steps, input.guidance_scale,
+                                        latents.data(), nullptr));
+    std::vector<VibeVoiceTokenizerLatents> out(static_cast<size_t>(input.batch_size));
+    for (int64_t b = 0; b < input.batch_size; ++b) {
+        auto & l = out[static_cast<size_t>(b)];
+        l.frames = 1;
+        l.dim = input.latent_size;
+        l.values.assign(latents.begin() + b * input.latent_size, latents.begin() + (b + 1) * input.latent_size);
+    }
+    return out;
+}
+
+}  // namespace engine::models::vibevoice
+
+namespace engine::models::stable_audio::foundation {
+
+FoundationRfDitRuntime::FoundationRfDitRuntime(const StableAudioConfig & config,
+                                               const std::vector<engine::b200::RawTensor> & tensors, int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    const auto views = engine::b200::views_of(tensors);
+    const b2d_dit_config c{config.embed_dim, config.depth, config.num_heads, config.cond_token_dim,
+                           config.global_cond_dim, config.io_channels, config.prompt_max_length};
+    device_->check(b2d_dit_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+void FoundationRfDitRuntime::prepare(const StableAudioSamplingState & sampling, float) const {
+    if (sampling.batch <= 0 || sampling.latent_sample_size <= 0)
+        throw std::runtime_error("Stable Audio Foundation RF DiT graph requires positive batch and latent length");
+}
+
+// Validation and messages as Graph::sample / validate_inputs (src/models/stable_audio/foundation/rf_dit.cpp:461-511,
+// 1030-1047); the whole sampler runs on the GPU (b2d_dit_sample).
+std::vector<float> FoundationRfDitRuntime::sample(const StableAudioSamplingState & sampling,
+                                                  const StableAudioConditioningInputs & conditioning, uint64_t,
+                                                  uint64_t &, std::string_view sampler_type, float sigma_min,
+                                                  float sigma_max, float rho, float cfg_scale,
+                                                  float apg_scale) const {
+    prepare(sampling, cfg_scale);
+    if (!sampler_type.empty() && sampler_type != "euler" && sampler_type != "pingpong" && sampler_type != "dpmpp-2m" &&
+        sampler_type != "dpmpp-3m-sde")
+        throw std::runtime_error("Stable Audio Foundation sampler_type is not supported for the v sampler");
+    if (sampler_type != "dpmpp-2m")
+        throw std::runtime_error("b200diff: only the dpmpp-2m sampler runs on the GPU path");
+    const int64_t B = sampling.batch, T = sampling.latent_sample_size, P2 = config_.prompt_max_length + 2;
+    if (conditioning.positive.batch != B || conditioning.positive.cross_tokens != P2 ||
+        conditioning.positive.cond_dim != config_.cond_token_dim ||
+        static_cast<int64_t>(conditioning.positive.global.size()) != B * config_.global_cond_dim)
+        throw std::runtime_error("Stable Audio Foundation RF DiT positive conditioning shape mismatch");
+    if (conditioning.has_negative &&
+        (conditioning.negative.batch != B || conditioning.negative.cross_tokens != P2 ||
+         conditioning.negative.cond_dim != config_.cond_token_dim))
+        throw std::runtime_error("Stable Audio Foundation RF DiT negative conditioning shape mismatch");
+    if (static_cast<int64_t>(sampling.noise.size()) != B * config_.io_channels * T ||
+        static_cast<int64_t>(sampling.padding_mask.size()) != B * T || sampling.schedule_points <= 1)
+        throw std::runtime_error("Stable Audio Foundation RF DiT graph shape mismatch");
+    b2d_dit_request rq{};
+    rq.batch = B;
+    rq.latent_tokens = T;
+    rq.steps = sampling.schedule_points - 1;
+    rq.noise = sampling.noise.data();
+    rq.padding_mask = sampling.padding_mask.data();
+    rq.cross_positive = conditioning.positive.cross_attention.data();
+    rq.cross_negative = conditioning.has_negative ? conditioning.negative.cross_attention.data() : nullptr;
+    rq.global_cond = conditioning.positive.global.data();
+    rq.sigma_min = sigma_min;
+    rq.sigma_max = sigma_max;
+    rq.rho = rho;
+    rq.cfg_scale = cfg_scale;
+    rq.apg_scale = apg_scale;
+    rq.sampler = B2D_SAMPLER_DPMPP_2M;
+    std::vector<float> out(sampling.noise.size());
+    device_->check(b2d_dit_sample(device_->ctx(), &rq, out.data(), nullptr));
+    return out;
+}
+
+}  // namespace engine::models::stable_audio::foundation

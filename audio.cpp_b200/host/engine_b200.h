@@ -1,0 +1,187 @@
+// C++ host layer over the b200diff C ABI, mirroring audio.cpp's entry points for the
+// diffusion hot path: same class / function names, same argument meaning, same
+// std::runtime_error texts.  An audio.cpp build swaps its ggml-graph bodies for
+// these (the weight tensors come from its TensorSource as raw GGUF bytes).
+//
+//   engine::models::vibevoice::VibeVoiceDPMSolverScheduler          include/engine/models/vibevoice/scheduler.h:14-47
+//   engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime include/engine/models/vibevoice/diffusion_head.h:58-97
+//   engine::models::vibevoice::sample_vibevoice_speech_latents       include/engine/models/vibevoice/diffusion_sampler.h:23-26
+//   engine::models::stable_audio::foundation::FoundationRfDitRuntime include/engine/models/stable_audio/foundation/rf_dit.h:73-106
+#pragma once
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <string_view>
+#include <vector>
+
+#include "../../include/b200diff.h"
+
+namespace engine::b200 {
+
+// One weight tensor as stored in the checkpoint (ggml type id, [out, in] dims, raw bytes).
+struct RawTensor {
+    std::string name;
+    int ggml_type = B2D_TYPE_F32;
+    std::vector<int64_t> dims;
+    std::vector<uint8_t> bytes;
+};
+
+// Owns one b2d_ctx (one device).
+class Device {
+public:
+    explicit Device(int device);
+    ~Device();
+    Device(const Device &) = delete;
+    Device & operator=(const Device &) = delete;
+    b2d_ctx * ctx() const noexcept { return ctx_; }
+    void check(b2d_status status) const;  // throws std::runtime_error(b2d_last_error)
+
+private:
+    b2d_ctx * ctx_ = nullptr;
+};
+
+std::vector<b2d_tensor_view> views_of(const std::vector<RawTensor> & tensors);
+
+}  // namespace engine::b200
+
+namespace engine::models::vibevoice {
+
+struct VibeVoiceDiffusionHeadConfig {
+    int64_t ddpm_num_inference_steps = 20;
+    int64_t ddpm_num_steps = 1000;
+    std::string ddpm_beta_schedule = "cosine";
+    std::string diffusion_type = "ddpm";
+    std::string prediction_type = "v_prediction";
+    float head_ffn_ratio = 3.0F;
+    int64_t head_layers = 4;
+    int64_t hidden_size = 0;
+    int64_t latent_size = 0;
+    float rms_norm_eps = 1.0e-5F;
+};
+
+struct VibeVoiceDiffusionPrediction {
+    std::vector<float> values;
+    int64_t frames = 0;
+    int64_t latent_size = 0;
+};
+
+struct VibeVoiceTokenizerLatents {
+    std::vector<float> values;
+    int64_t frames = 0;
+    int64_t dim = 0;
+};
+
+struct VibeVoiceSchedulerStepResult {
+    std::vector<float> prev_sample;
+};
+
+// Host scheduler: timesteps and per-step coefficients from b2d_vv_schedule; step() applies
+// the DPM-Solver++(2M) update to host vectors exactly as the reference does.
+class VibeVoiceDPMSolverScheduler final {
+public:
+    explicit VibeVoiceDPMSolverScheduler(const VibeVoiceDiffusionHeadConfig & config);
+    void set_timesteps(int64_t inference_steps);
+    void reset_step_state();
+    const std::vector<int64_t> & timesteps() const noexcept { return timesteps_; }
+    VibeVoiceSchedulerStepResult step(const std::vector<float> & model_output, int64_t timestep,
+                                      const std::vector<float> & sample);
+    const VibeVoiceDiffusionHeadConfig & config() const noexcept { return config_; }
+
+private:
+    VibeVoiceDiffusionHeadConfig config_;
+    std::vector<b2d_vv_step> table_;
+    std::vector<int64_t> timesteps_;
+    std::vector<float> previous_;
+    int64_t step_index_ = -1;
+};
+
+class VibeVoiceDiffusionHeadWeightsRuntime final {
+public:
+    VibeVoiceDiffusionHeadWeightsRuntime(const VibeVoiceDiffusionHeadConfig & config,
+                                         const std::vector<engine::b200::RawTensor> & tensors, int device);
+    VibeVoiceDiffusionPrediction predict(const std::vector<float> & noisy_images, int64_t frames, int64_t latent_size,
+                                         float timestep, const std::vector<float> & condition,
+                                         int64_t condition_hidden_size) const;
+    const VibeVoiceDiffusionHeadConfig & config() const noexcept { return config_; }
+    b2d_ctx * ctx() const noexcept { return device_->ctx(); }
+    void check(b2d_status s) const { device_->check(s); }
+
+private:
+    VibeVoiceDiffusionHeadConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
+};
+
+struct VibeVoiceSpeechDiffusionInput {
+    std::vector<float> positive_condition;
+    std::vector<float> negative_condition;
+    std::vector<float> initial_speech;
+    int64_t batch_size = 0;
+    int64_t hidden_size = 0;
+    int64_t latent_size = 0;
+    int64_t inference_steps = 0;
+    float guidance_scale = 1.0F;
+};
+
+std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
+    const VibeVoiceDiffusionHeadWeightsRuntime & prediction_head, VibeVoiceDPMSolverScheduler & scheduler,
+    const VibeVoiceSpeechDiffusionInput & input);
+
+}  // namespace engine::models::vibevoice
+
+namespace engine::models::stable_audio {
+
+struct StableAudioConfig {
+    int64_t io_channels = 64;
+    int64_t prompt_max_length = 128;
+    int64_t embed_dim = 1536;
+    int64_t depth = 24;
+    int64_t num_heads = 24;
+    int64_t cond_token_dim = 768;
+    int64_t global_cond_dim = 1536;
+};
+
+struct StableAudioSamplingState {
+    int64_t audio_sample_size = 0;
+    int64_t latent_sample_size = 0;
+    int64_t batch = 0;
+    int64_t channels = 0;
+    int64_t schedule_points = 0;
+    std::vector<float> schedule;
+    std::vector<float> padding_mask;
+    std::vector<float> noise;
+};
+
+struct StableAudioConditionedInput {
+    int64_t batch = 0;
+    int64_t cross_tokens = 0;
+    int64_t cond_dim = 0;
+    std::vector<float> cross_attention;
+    std::vector<float> global;
+};
+
+struct StableAudioConditioningInputs {
+    StableAudioConditionedInput positive;
+    StableAudioConditionedInput negative;
+    bool has_negative = false;
+};
+
+namespace foundation {
+
+class FoundationRfDitRuntime {
+public:
+    FoundationRfDitRuntime(const StableAudioConfig & config, const std::vector<engine::b200::RawTensor> & tensors,
+                           int device);
+    void prepare(const StableAudioSamplingState & sampling, float cfg_scale) const;
+    std::vector<float> sample(const StableAudioSamplingState & sampling,
+                              const StableAudioConditioningInputs & conditioning, uint64_t seed,
+                              uint64_t & rng_offset_blocks, std::string_view sampler_type, float sigma_min,
+                              float sigma_max, float rho, float cfg_scale, float apg_scale) const;
+
+private:
+    StableAudioConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
+};
+
+}  // namespace foundation
+}  // namespace engine::models::stable_audio

@@ -373,6 +373,21 @@ def bench_ours(args):
     ctx.sync(st.cuda_stream)
     ms_e2e = timed(host_call)
     assert np.isfinite(out_host.numpy()).all()
+    # the one collective of the data-parallel path: gather every rank's latents (outside the timed steps)
+    gather_ms = 0.0
+    if world > 1:
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("b2d_parallel", os.path.join(ROOT, "audio.cpp_b200", "parallel.py"))
+        par = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(par)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.distributed.barrier()
+        g0.record(st)
+        full = par.gather_rows(out_dev, cfg.frames * world, world)
+        g1.record(st)
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(g0.elapsed_time(g1))
+        assert full.shape[0] == cfg.frames * world
 
     frames_total = cfg.frames * world
     value = frames_total / (ms / 1e3)
@@ -399,6 +414,7 @@ def bench_ours(args):
                 "e2e": {"value": round(e2e, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "ms_per_step": round(ms_e2e, 4), "api": "b2d_vv_sample (host buffers, pinned)"},
                 "gpu_launches": launches_per_call * args.steps,
+                "final_gather_ms": round(gather_ms, 4),
                 "roofline": roof,
                 "whole_call_tflops": round(flops_call / (ms / 1e3) / 1e12, 1),
                 "clocks": clk.summary()}

@@ -1,0 +1,101 @@
+"""CPU tests of the multi-GPU host logic (audio.cpp_b200/parallel.py) with world_size-2
+gloo process groups: sharding keeps CFG pairs together, the final gather restores the
+global order, and a rank that fails before the gather is reported on the host."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_range_partitions():
+    par = _parallel()
+    for n in (0, 1, 7, 8, 1024, 8193):
+        for world in (1, 2, 3, 8):
+            spans = [par.shard_range(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            assert max(h - l for l, h in spans) - min(h - l for l, h in spans) <= 1
+    with pytest.raises(ValueError):
+        par.shard_range(4, 2, 2)
+
+
+def _parallel():
+    import importlib.util
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("b2d_parallel", os.path.join(root, "audio.cpp_b200", "parallel.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_head_shard_keeps_cfg_pairs():
+    par = _parallel()
+    B, H = 7, 4
+    pos = np.arange(B * H, dtype=np.float32).reshape(B, H)
+    neg = -pos
+    init = np.arange(2 * B * 64, dtype=np.float32).reshape(2 * B, 64)
+    for rank in range(3):
+        p, n, i, (lo, hi) = par.shard_head_inputs(pos, neg, init, 3, rank)
+        assert np.array_equal(p, pos[lo:hi]) and np.array_equal(n, neg[lo:hi])
+        assert np.array_equal(i[:hi - lo], init[lo:hi]) and np.array_equal(i[hi - lo:], init[B + lo:B + hi])
+
+
+def _worker(rank, world, port, n_total, fail_rank, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    par = _parallel()
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        lo, hi = par.shard_range(n_total, world, rank)
+        if rank == fail_rank:
+            raise RuntimeError("injected failure on rank %d" % rank)
+        # stand-in for this rank's sampled latents: row r = r (global index) in every column
+        local = torch.arange(lo, hi, dtype=torch.float32)[:, None].repeat(1, 64)
+        full = par.gather_rows(local, n_total, world)
+        q.put((rank, "ok", full[:, 0].tolist()))
+    except Exception as e:  # reported to the parent on the host, never through a device fault
+        q.put((rank, "error", str(e)))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _spawn(n_total, fail_rank=-1):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, n_total, fail_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    return sorted(res)
+
+
+@pytest.mark.parametrize("n_total", [8, 9])
+def test_gather_restores_order_gloo(n_total):
+    res = _spawn(n_total)
+    for rank, status, rows in res:
+        assert status == "ok", rows
+        assert rows == list(range(n_total))
+
+
+def test_failed_rank_is_reported_on_host():
+    res = dict((r, (s, m)) for r, s, m in _spawn(8, fail_rank=1))
+    assert res[1][0] == "error" and "injected failure" in res[1][1]
+    # the surviving rank's gather ends with an error (peer gone / timeout), not a hang
+    assert res[0][0] == "error"
