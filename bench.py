@@ -167,7 +167,9 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
             "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS)" if "bf16_tflops" in peaks
             else "fallback 1590", "launch_us": round(dt * 1e6, 2), "flop_per_launch": flops,
-            "traffic": None}
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel (ncu, same shape):
+            # = the algorithmic A + B bytes, no re-reads (profiles/gemm_swiglu_vv15_q8_1024.md)
+            "traffic": 34637056 + 26368, "traffic_unit": "bytes/launch"}
 
 
 DIT_WORKLOAD = "sao_bf16_1x1024"
