@@ -133,6 +133,40 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
     CK(cudaGetLastError());
 }
 
+// 2-SM (cta_group::2) 256 x 256 pair tiles; B operands need a 128-row TMA box.
+int g_gemm_pair = -1;  // -1 automatic, 0 off, 1 forced (B2D_GEMM_PAIR)
+
+template <int EPI, typename CT>
+void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb128, int64_t M, int64_t N, int64_t K,
+                        const EpiParams& ep, int num_sms, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        CK(cudaFuncSetAttribute(gemm_tc2_kernel<EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(GemmPairShape::SMEM_BYTES)));
+        configured = true;
+    }
+    const int64_t units = ((M + 255) / 256) * (N / 256);
+    if (units == 0) return;
+    const int64_t pairs = units < num_sms / 2 ? units : num_sms / 2;
+    gemm_tc2_kernel<EPI, CT><<<unsigned(2 * pairs), 192, GemmPairShape::SMEM_BYTES, st>>>(ta, tb128, int(M), int(N),
+                                                                                            int(K), ep);
+    CK(cudaGetLastError());
+}
+
+template <typename CT>
+void launch_gemm_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb128, int64_t M, int64_t N, int64_t K,
+                      const EpiParams& ep, int num_sms, cudaStream_t st) {
+    if (N % 256) fail(B2D_EINVAL, "pair GEMM N (%lld) must be a multiple of 256", (long long)N);
+    if (ep.splits > 1) fail(B2D_EINVAL, "pair GEMM has no split-K");
+    switch (epi) {
+        case EPI_F32: launch_gemm_pair_t<EPI_F32, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
+        case EPI_CT: launch_gemm_pair_t<EPI_CT, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
+        case EPI_SWIGLU: launch_gemm_pair_t<EPI_SWIGLU, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
+        case EPI_RESID: launch_gemm_pair_t<EPI_RESID, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
+        default: fail(B2D_EINVAL, "unsupported pair GEMM epilogue %d", epi);
+    }
+}
+
 template <typename CT>
 void launch_gemm(int bn, int epi, const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K,
                  const EpiParams& ep, int num_sms, cudaStream_t st) {
@@ -265,7 +299,7 @@ struct HeadModel {
     DevBuf w_in, w_cond, w_t1, w_t2, w_ada, w_final, norms;
     std::vector<DevBuf> w_gu, w_down;
     CUtensorMap tm_in, tm_cond, tm_ada, tm_final, tm_t1, tm_t2;
-    std::vector<CUtensorMap> tm_gu, tm_down256, tm_down192;
+    std::vector<CUtensorMap> tm_gu, tm_gu128, tm_down256, tm_down192;
     std::unique_ptr<HeadWorkspace> ws;
 };
 
@@ -382,10 +416,12 @@ void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
     m.tm_t1 = make_tmap(m.w_t1.p, bf, H, 256, 256);
     m.tm_t2 = make_tmap(m.w_t2.p, bf, H, H, 256);
     m.tm_gu.clear();
+    m.tm_gu128.clear();
     m.tm_down256.clear();
     m.tm_down192.clear();
     for (int64_t l = 0; l < L; ++l) {
         m.tm_gu.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 256));
+        m.tm_gu128.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 128));  // 2-SM pair tiles
         m.tm_down256.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 256));
         if (H % 192 == 0) m.tm_down192.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 192));
     }
@@ -481,7 +517,8 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         ep.status = status;
         ep.out = ws.ffn.p;
         ep.ldo = F;
-        launch_gemm<CT>(256, EPI_SWIGLU, ws.tm_h, m.tm_gu[size_t(l)], R, 2 * F, H, ep, sms, st);
+        // SwiGLU GEMMs run on 2-SM 256 x 256 pair tiles (measured faster at every head shape)
+        launch_gemm_pair<CT>(EPI_SWIGLU, ws.tm_h, m.tm_gu128[size_t(l)], R, 2 * F, H, ep, sms, st);
         ep = EpiParams{};
         ep.status = status;
         ep.resid = ws.x.as<float>();
@@ -799,10 +836,11 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream) {
     return guarded(ctx, [&] {
         if (m <= 0 || n <= 0 || k <= 0) fail(B2D_EINVAL, "GEMM dimensions must be positive");
-        if (epilogue == EPI_SWIGLU && bn != 256) fail(B2D_EINVAL, "SwiGLU epilogue needs 256-column tiles");
+        if (epilogue == EPI_SWIGLU && bn != 256 && bn != 512) fail(B2D_EINVAL, "SwiGLU epilogue needs 256-column tiles");
         if (epilogue == EPI_RESID ? !resid_dev : !out_dev) fail(B2D_EINVAL, "GEMM output is null");
+        const bool pair = bn == 512;  // 512 selects the 2-SM 256 x 256 pair-tile kernel
         const CUtensorMap ta = make_tmap(a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128);
-        const CUtensorMap tb = make_tmap(b_dev, bf16 != 0, uint64_t(n), uint64_t(k), uint32_t(bn));
+        const CUtensorMap tb = make_tmap(b_dev, bf16 != 0, uint64_t(n), uint64_t(k), pair ? 128u : uint32_t(bn));
         EpiParams ep;
         ep.out = out_dev;
         ep.ldo = ldo;
@@ -813,10 +851,16 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
         ep.ldg = ldg;
         ep.status = ctx->status.as<int>();
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        if (bf16)
+        if (pair) {
+            if (bf16)
+                launch_gemm_pair<__nv_bfloat16>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+            else
+                launch_gemm_pair<__half>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+        } else if (bf16) {
             launch_gemm<__nv_bfloat16>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
-        else
+        } else {
             launch_gemm<__half>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+        }
     });
 }
 

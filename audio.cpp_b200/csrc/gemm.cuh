@@ -73,7 +73,9 @@ struct CtTraits<__nv_bfloat16> {
     }
 };
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// SiLU with the hardware exp2 and fast reciprocal-division intrinsics (a few ulp; the result is
+// rounded to fp16/bf16 or consumed by an fp32 accumulation downstream).
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <int BN>
 struct GemmShape {
@@ -87,6 +89,112 @@ struct GemmShape {
     static constexpr size_t EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // per-warp transpose buffers
     static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + EPI_STAGE_BYTES;
 };
+
+// Drains one 128-row accumulator tile (this warp's 32 TMEM lanes at `tbase`) through the epilogue.
+template <int BN, int EPI, typename CT>
+__device__ __forceinline__ void epilogue_tile(uint32_t tbase, int rbase, int rows_live, int n0, float* out_f32,
+                                              const EpiParams& ep, float* stg, int lane) {
+    constexpr int CHUNKS = EPI == EPI_SWIGLU ? 4 : BN / 32;
+#pragma unroll 1
+        for (int c = 0; c < CHUNKS; ++c) {
+            float v[32];
+            __syncwarp();
+            if constexpr (EPI == EPI_SWIGLU) {
+                float l[32];
+                tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+                tmem_ld_32x32b_x32(tbase + uint32_t(128 + c * 32), l);
+                tmem_ld_wait();
+                const float* ba = ep.bias ? ep.bias + n0 + c * 32 : nullptr;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float av = ba ? v[j] + __ldg(ba + j) : v[j];
+                    const float lv = ba ? l[j] + __ldg(ba + 128 + j) : l[j];
+                    v[j] = silu_f(av) * lv;
+                }
+            } else {
+                tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+                tmem_ld_wait();
+            }
+            if constexpr (EPI == EPI_SWIGLU || EPI == EPI_CT) {
+                // 16-bit outputs: each thread stores its row's 32 values as 4 x 16 B (no smem
+                // traffic, which would compete with the next tile's tcgen05 operand reads).
+                const int row = rbase + lane;
+                if (lane < rows_live) {
+                    const int col0 = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32;
+                    if (EPI == EPI_CT && ep.rope_cos) {
+                        if (col0 < ep.rope_cols) {
+                            if ((col0 & 63) == 0) {
+                                const int pos = row % ep.rope_L;
+                                const float* cs = ep.rope_cos + pos * 16;
+                                const float* sn = ep.rope_sin + pos * 16;
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) {
+                                    const float x0 = v[j], x1 = v[j + 16], cj = __ldg(cs + j), sj = __ldg(sn + j);
+                                    v[j] = x0 * cj - x1 * sj;
+                                    v[j + 16] = x0 * sj + x1 * cj;
+                                }
+                            }
+                        } else if (ep.vmask) {
+                            const float mv = __ldg(ep.vmask + row);
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] *= mv;
+                        }
+                    }
+                    if (EPI == EPI_CT && ep.bias) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + col0 + j);
+                    }
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) packed[j] = CtTraits<CT>::pack2(v[2 * j], v[2 * j + 1]);
+                    uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + col0);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+                }
+                continue;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
+            __syncwarp();
+            const int col = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32 + lane;
+            const float bcol = (EPI != EPI_SWIGLU && ep.bias) ? __ldg(ep.bias + col) : 0.f;
+            if constexpr (EPI == EPI_RESID) {
+                float* __restrict__ R = ep.resid;
+                const float* __restrict__ G = ep.gate;
+#pragma unroll 1
+                for (int r0 = 0; r0 < rows_live; r0 += 32) {
+                    float rv[32], gv[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int64_t row = rbase + r0 + i;
+                        const bool ok = r0 + i < rows_live;
+                        rv[i] = ok ? R[row * ep.ldr + col] : 0.f;
+                        gv[i] = (ok && G) ? G[row * ep.ldg + col] : 1.f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (r0 + i < rows_live)
+                            R[int64_t(rbase + r0 + i) * ep.ldr + col] = rv[i] + gv[i] * (stg[(r0 + i) * 33 + lane] + bcol);
+                    }
+                }
+            } else {
+#pragma unroll 4
+                for (int r = 0; r < 32; ++r) {
+                    if (r < rows_live) {
+                        const float x = stg[r * 33 + lane] + bcol;
+                        int64_t row = rbase + r;
+                        if constexpr (EPI == EPI_F32) {
+                            if (ep.seg_rows) row += (row / ep.seg_rows + 1) * ep.seg_pad;
+                            out_f32[row * ep.ldo + col] = x;
+                        } else {
+                            reinterpret_cast<CT*>(ep.out)[row * ep.ldo + col] = CtTraits<CT>::cvt(x);
+                        }
+                    }
+                }
+            }
+        }
+}
 
 template <int BN, int EPI, typename CT>
 __global__ void __launch_bounds__(192, 1)
@@ -203,7 +311,6 @@ __global__ void __launch_bounds__(192, 1)
         // residual read-modify-write issues all 32 rows' loads before any store instead of serialising).
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
         float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
-        constexpr int CHUNKS = EPI == EPI_SWIGLU ? 4 : BN / 32;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
@@ -216,105 +323,7 @@ __global__ void __launch_bounds__(192, 1)
             const int rbase = m0 + quarter * 32;
             const int rows_live = M - rbase < 32 ? M - rbase : 32;
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < CHUNKS; ++c) {
-                float v[32];
-                __syncwarp();
-                if constexpr (EPI == EPI_SWIGLU) {
-                    float l[32];
-                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
-                    tmem_ld_32x32b_x32(tbase + uint32_t(128 + c * 32), l);
-                    tmem_ld_wait();
-                    const float* ba = ep.bias ? ep.bias + n0 + c * 32 : nullptr;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float av = ba ? v[j] + __ldg(ba + j) : v[j];
-                        const float lv = ba ? l[j] + __ldg(ba + 128 + j) : l[j];
-                        v[j] = silu_f(av) * lv;
-                    }
-                } else {
-                    tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
-                    tmem_ld_wait();
-                }
-                if constexpr (EPI == EPI_SWIGLU || EPI == EPI_CT) {
-                    // 16-bit outputs: each thread stores its row's 32 values as 4 x 16 B (no smem
-                    // traffic, which would compete with the next tile's tcgen05 operand reads).
-                    const int row = rbase + lane;
-                    if (lane < rows_live) {
-                        const int col0 = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32;
-                        if (EPI == EPI_CT && ep.rope_cos) {
-                            if (col0 < ep.rope_cols) {
-                                if ((col0 & 63) == 0) {
-                                    const int pos = row % ep.rope_L;
-                                    const float* cs = ep.rope_cos + pos * 16;
-                                    const float* sn = ep.rope_sin + pos * 16;
-#pragma unroll
-                                    for (int j = 0; j < 16; ++j) {
-                                        const float x0 = v[j], x1 = v[j + 16], cj = __ldg(cs + j), sj = __ldg(sn + j);
-                                        v[j] = x0 * cj - x1 * sj;
-                                        v[j + 16] = x0 * sj + x1 * cj;
-                                    }
-                                }
-                            } else if (ep.vmask) {
-                                const float mv = __ldg(ep.vmask + row);
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) v[j] *= mv;
-                            }
-                        }
-                        if (EPI == EPI_CT && ep.bias) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + col0 + j);
-                        }
-                        uint32_t packed[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) packed[j] = CtTraits<CT>::pack2(v[2 * j], v[2 * j + 1]);
-                        uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<CT*>(ep.out) + int64_t(row) * ep.ldo + col0);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-                    }
-                    continue;
-                }
-#pragma unroll
-                for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
-                __syncwarp();
-                const int col = (EPI == EPI_SWIGLU ? n0 / 2 : n0) + c * 32 + lane;
-                const float bcol = (EPI != EPI_SWIGLU && ep.bias) ? __ldg(ep.bias + col) : 0.f;
-                if constexpr (EPI == EPI_RESID) {
-                    float* __restrict__ R = ep.resid;
-                    const float* __restrict__ G = ep.gate;
-#pragma unroll 1
-                    for (int r0 = 0; r0 < rows_live; r0 += 32) {
-                        float rv[32], gv[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int64_t row = rbase + r0 + i;
-                            const bool ok = r0 + i < rows_live;
-                            rv[i] = ok ? R[row * ep.ldr + col] : 0.f;
-                            gv[i] = (ok && G) ? G[row * ep.ldg + col] : 1.f;
-                        }
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (r0 + i < rows_live)
-                                R[int64_t(rbase + r0 + i) * ep.ldr + col] = rv[i] + gv[i] * (stg[(r0 + i) * 33 + lane] + bcol);
-                        }
-                    }
-                } else {
-#pragma unroll 4
-                    for (int r = 0; r < 32; ++r) {
-                        if (r < rows_live) {
-                            const float x = stg[r * 33 + lane] + bcol;
-                            int64_t row = rbase + r;
-                            if constexpr (EPI == EPI_F32) {
-                                if (ep.seg_rows) row += (row / ep.seg_rows + 1) * ep.seg_pad;
-                                out_f32[row * ep.ldo + col] = x;
-                            } else {
-                                reinterpret_cast<CT*>(ep.out)[row * ep.ldo + col] = CtTraits<CT>::cvt(x);
-                            }
-                        }
-                    }
-                }
-            }
+            epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, out_f32, ep, stg, lane);
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             acc ^= 1;
@@ -327,6 +336,158 @@ done:
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, S::TMEM_COLS);
+    }
+}
+
+// 2-SM variant: a cluster of 2 CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2
+// (M = 256 split across the pair's TMEM, N = 256).  Each CTA loads its own 128 rows of A and
+// its own 128 rows (half) of B, so per SM the operand traffic per FLOP is 2/3 of the
+// single-CTA 128 x 256 tile.  The leader CTA (rank 0) issues the MMAs; TMA completion of
+// both halves is counted on the leader's full barrier; commits multicast to both CTAs'
+// empty / tmem-full barriers; both epilogues release the accumulator on the leader's
+// tmem-empty barrier.  No TMA multicast is used.
+struct GemmPairShape {
+    static constexpr int BM = 128;  // rows per CTA (256 per pair)
+    static constexpr int BN = 256;  // columns per pair tile (128 rows of B per CTA)
+    static constexpr int BK = 64;
+    static constexpr int STAGES = 6;
+    static constexpr uint32_t A_BYTES = BM * BK * 2;
+    static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + 4 * 32 * 33 * 4;
+};
+
+template <int EPI, typename CT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                    int K, EpiParams ep) {
+    using S = GemmPairShape;
+    constexpr int BM = S::BM, BN = S::BN, BK = S::BK, STAGES = S::STAGES;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pm = (M + 2 * BM - 1) / (2 * BM);  // 256-row pair tiles
+    const int num_units = pm * (N / BN);
+    const int k_blocks = K / BK;
+    const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 256);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int u = cluster; u < num_units; u += nclusters) {
+                const int m0 = (u % pm) * 2 * BM + int(rank) * BM;
+                const int n0 = (u / pm) * BN + int(rank) * (BN / 2);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
+                    if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
+                    const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
+                    uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
+                    tma_load_2d_pair(sa, &tmA, bar, kb * BK, m0);
+                    tma_load_2d_pair(sa + S::A_BYTES, &tmB, bar, kb * BK, n0);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(CtTraits<CT>::kFmt, 2 * BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int u = cluster; u < num_units; u += nclusters) {
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, ep.status, kErrTimeoutMma)) goto done;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, ep.status, kErrTimeoutMma)) goto done;
+                    tc_fence_after();
+                    uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
+                    const uint64_t adesc = smem_desc_sw128(sa);
+                    const uint64_t bdesc = smem_desc_sw128(sa + S::A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16_pair(d_tmem, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc,
+                                     (kb | k) != 0 ? 1u : 0u);
+                    mma_commit_pair(&empty[stage], 0x3);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                mma_commit_pair(&tfull[acc], 0x3);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+        }
+    } else {
+        const int quarter = warp & 3;
+        float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
+        const uint32_t tempty_leader[2] = {map_to_cta(smem_u32(&tempty[0]), 0), map_to_cta(smem_u32(&tempty[1]), 0)};
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int u = cluster; u < num_units; u += nclusters) {
+            const int n0 = (u / pm) * BN;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.status, kErrTimeoutEpilogue)) goto done;
+            tc_fence_after();
+            const int rbase = (u % pm) * 2 * BM + int(rank) * BM + quarter * 32;
+            const int rows_live = M - rbase < 32 ? M - rbase : 32;
+            const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+            epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, reinterpret_cast<float*>(ep.out), ep, stg, lane);
+            tc_fence_before();
+            mbar_arrive_cluster(tempty_leader[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
     }
 }
 

@@ -147,7 +147,8 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
     w = (torch.randn(N, K, device="cuda") * 0.02).half()
     out = torch.empty(M, N // 2, device="cuda", dtype=torch.float16)
     st = torch.cuda.current_stream()
-    launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, epilogue=b2d.EPI_SWIGLU, bn=256,
+    # bn=512: the 2-SM (cta_group::2) 256 x 256 pair-tile kernel the head runs for this GEMM
+    launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, epilogue=b2d.EPI_SWIGLU, bn=512,
                               out=out.data_ptr(), ldo=N // 2, stream=st.cuda_stream)
     for _ in range(5):
         launch()
@@ -163,11 +164,11 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
     flops = 2.0 * M * N * K
     achieved = flops / dt / 1e12
     peak = peaks.get("bf16_tflops", 1590.0)
-    return {"kernel": "gemm_tc_kernel<256,SWIGLU,half> (FFN gate/up, %dx%dx%d)" % (M, N, K), "bound": "tensor",
+    return {"kernel": "gemm_tc2_kernel<SWIGLU,half> 2-SM (FFN gate/up, %dx%dx%d)" % (M, N, K), "bound": "tensor",
             "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS)" if "bf16_tflops" in peaks
             else "fallback 1590", "launch_us": round(dt * 1e6, 2), "flop_per_launch": flops,
-            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel (ncu, same shape):
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM shape (ncu, 1-SM kernel):
             # = the algorithmic A + B bytes, no re-reads (profiles/gemm_swiglu_vv15_q8_1024.md)
             "traffic": 34637056 + 26368, "traffic_unit": "bytes/launch"}
 
@@ -237,10 +238,10 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     assert np.isfinite(out_host.numpy()).all()
     if rank == 0:
         R = 2 * cfg.batch * (cfg.latent_tokens + 1)
-        t_ff = gemm_time(b2d, ctx, torch, R, 8 * cfg.embed_dim, cfg.embed_dim, b2d.EPI_SWIGLU, bf16=True)
+        t_ff = gemm_time(b2d, ctx, torch, R, 8 * cfg.embed_dim, cfg.embed_dim, b2d.EPI_SWIGLU, bn=512, bf16=True)
         fl = 2.0 * R * 8 * cfg.embed_dim * cfg.embed_dim
         peak = peaks.get("bf16_tflops", 1590.0)
-        res["roofline"] = {"kernel": "gemm_tc_kernel<256,SWIGLU,bf16> (FFN in, %dx%dx%d)" % (R, 8 * cfg.embed_dim,
+        res["roofline"] = {"kernel": "gemm_tc2_kernel<SWIGLU,bf16> 2-SM (FFN in, %dx%dx%d)" % (R, 8 * cfg.embed_dim,
                                                                                             cfg.embed_dim),
                            "bound": "tensor", "achieved": round(fl / t_ff / 1e12, 1), "peak": peak,
                            "unit": "TFLOP/s", "frac": round(fl / t_ff / 1e12 / peak, 4), "traffic": None}
