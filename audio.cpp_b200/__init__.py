@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention"]
+            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn"]
 
 
 class B2DError(RuntimeError):
@@ -64,7 +64,12 @@ class DitRequest(C.Structure):
     _fields_ = [("batch", C.c_int64), ("latent_tokens", C.c_int64), ("steps", C.c_int64), ("noise", C.c_void_p),
                 ("padding_mask", C.c_void_p), ("cross_positive", C.c_void_p), ("cross_negative", C.c_void_p),
                 ("global_cond", C.c_void_p), ("sigma_min", C.c_float), ("sigma_max", C.c_float), ("rho", C.c_float),
-                ("cfg_scale", C.c_float), ("apg_scale", C.c_float), ("sampler", C.c_int32)]
+                ("cfg_scale", C.c_float), ("apg_scale", C.c_float), ("sampler", C.c_int32), ("schedule", C.c_void_p),
+                ("seed", C.c_uint64), ("rng_offset_blocks", C.POINTER(C.c_uint64)),
+                ("rng_multiprocessor_count", C.c_int64), ("rng_max_threads_per_multiprocessor", C.c_int64)]
+
+
+SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
 
 
 _lib = None
@@ -95,6 +100,7 @@ def lib() -> C.CDLL:
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
         L.b2d_attention.argtypes = [P, I32, P, I64, I64, P, P, I64, I64, P, I64, I64, I32, I32, I32, I32, I32, P]
+        L.b2d_torch_randn.argtypes = [P, I32, C.c_uint64, C.c_uint64, I64, I64, I64, I32, P, P]
         L.b2d_dit_load.argtypes = [P, C.POINTER(DitConfig), C.POINTER(TensorView), I32]
         L.b2d_dit_sample.argtypes = [P, C.POINTER(DitRequest), P, P]
         L.b2d_dit_sample_device.argtypes = [P, C.POINTER(DitRequest), P, P]
@@ -159,6 +165,12 @@ class Context:
         self.check(lib().b2d_q8_0_dequantize(self._h, C.c_void_p(q8_dev), rows, k, C.c_void_p(out_dev),
                                              C.c_void_p(stream)))
 
+    def torch_randn(self, out_dev: int, count: int, seed: int, offset: int = 0, layout: int = 0, sms: int = 1,
+                    max_threads: int = 256, bf16: bool = False, stream: int = 0) -> None:
+        """torch-CUDA-compatible normals into a device float buffer (layout 0 per-index, 1 TensorIterator)."""
+        self.check(lib().b2d_torch_randn(self._h, layout, seed, offset, count, sms, max_threads, int(bf16),
+                                         C.c_void_p(out_dev), C.c_void_p(stream)))
+
     def attention(self, q: int, q_row: int, q_seq: int, k: int, v: int, kv_row: int, kv_seq: int, o: int,
                   o_row: int, o_seq: int, lq: int, lk: int, heads: int, kv_rep: int = 1, nseq: int = 1,
                   bf16: bool = False, stream: int = 0) -> None:
@@ -211,27 +223,39 @@ class StableAudioDiT:
         ctx.check(lib().b2d_dit_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
 
     def _request(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
-                 sigma_max, rho, cfg_scale, apg_scale):
+                 sigma_max, rho, cfg_scale, apg_scale, sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0,
+                 rng_policy=(1, 256)):
         b, _, t = noise.shape
+        self._offset = C.c_uint64(rng_offset)
         return DitRequest(b, t, steps, _ptr(noise), _ptr(padding_mask), _ptr(cross_positive),
                           _ptr(cross_negative) if cross_negative is not None else None, _ptr(global_cond),
-                          sigma_min, sigma_max, rho, cfg_scale, apg_scale, 0)
+                          sigma_min, sigma_max, rho, cfg_scale, apg_scale, SAMPLERS[sampler],
+                          _ptr(schedule) if schedule is not None else None, seed, C.pointer(self._offset),
+                          rng_policy[0], rng_policy[1])
+
+    @property
+    def rng_offset_blocks(self) -> int:
+        """TensorIterator Philox offset after the last call (the reference's rng_offset_blocks out-parameter)."""
+        return int(self._offset.value)
 
     def sample(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps=100, sigma_min=0.01,
-               sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, out=None, stream: int = 0):
-        """Host arrays (numpy / pinned torch) -> latents [B, 64, T] (dpmpp-2m)."""
+               sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, out=None, stream: int = 0,
+               sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256)):
+        """Host arrays (numpy / pinned torch) -> latents [B, 64, T]."""
         arrs = [np.ascontiguousarray(a, np.float32) if isinstance(a, np.ndarray) else a
-                for a in (noise, padding_mask, cross_positive, cross_negative, global_cond)]
-        rq = self._request(*arrs, steps, sigma_min, sigma_max, rho, cfg_scale, apg_scale)
+                for a in (noise, padding_mask, cross_positive, cross_negative, global_cond, schedule)]
+        rq = self._request(*arrs[:5], steps, sigma_min, sigma_max, rho, cfg_scale, apg_scale, sampler, arrs[5], seed,
+                           rng_offset, rng_policy)
         if out is None:
             out = np.empty(arrs[0].shape, np.float32)
         self.ctx.check(lib().b2d_dit_sample(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)), C.c_void_p(stream)))
         return out
 
     def sample_device(self, noise, padding_mask, cross_positive, cross_negative, global_cond, out, steps=100,
-                      sigma_min=0.01, sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, stream: int = 0):
+                      sigma_min=0.01, sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, stream: int = 0,
+                      sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256)):
         rq = self._request(noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
-                           sigma_max, rho, cfg_scale, apg_scale)
+                           sigma_max, rho, cfg_scale, apg_scale, sampler, schedule, seed, rng_offset, rng_policy)
         self.ctx.check(lib().b2d_dit_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
                                                    C.c_void_p(stream)))
         return out

@@ -864,6 +864,21 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
     });
 }
 
+b2d_status b2d_torch_randn(b2d_ctx* ctx, int32_t layout, uint64_t seed, uint64_t offset, int64_t count,
+                           int64_t multiprocessor_count, int64_t max_threads_per_multiprocessor, int32_t bf16,
+                           float* out_dev, void* stream) {
+    return guarded(ctx, [&] {
+        if (count <= 0 || !out_dev || (layout != 0 && layout != 1)) fail(B2D_EINVAL, "invalid randn request");
+        if (layout == 1 && (multiprocessor_count <= 0 || max_threads_per_multiprocessor <= 0))
+            fail(B2D_EINVAL, "torch CUDA TensorIterator randn requires CUDA device properties");
+        const uint64_t stride =
+            layout == 1 ? torch_iterator_stride(uint64_t(count), multiprocessor_count, max_threads_per_multiprocessor) : 0;
+        torch_randn_kernel<<<grid_for(count, 256, ctx->num_sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            layout, seed, offset, stride, count, bf16, out_dev);
+        CK(cudaGetLastError());
+    });
+}
+
 b2d_status b2d_attention(b2d_ctx* ctx, int32_t bf16, const void* q, int64_t q_row, int64_t q_seq, const void* k,
                          const void* v, int64_t kv_row, int64_t kv_seq, void* o, int64_t o_row, int64_t o_seq,
                          int32_t lq, int32_t lk, int32_t heads, int32_t kv_rep, int32_t nseq, void* stream) {

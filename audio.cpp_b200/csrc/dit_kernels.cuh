@@ -5,6 +5,7 @@
 #pragma once
 
 #include "kernels.cuh"
+#include "philox.cuh"
 
 namespace b2d {
 
@@ -66,13 +67,14 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const float* __restrict_
     }
 }
 
-// Global-token rows: h[seq, 0, :] = gpre[seq, :] + temb[step, :]   (rf_dit.cpp:545-552)
+// Global-token rows: h[seq, 0, :] = gpre[seq, :] + temb[step, seq % B, :]   (rf_dit.cpp:545-552);
+// temb holds one row per (step, prompt) since v-DDIM gives every prompt its own timestep.
 __global__ void dit_global_row_kernel(float* __restrict__ h, int64_t seq_rows, const float* __restrict__ gpre,
-                                      const float* __restrict__ temb, int d, int nseq) {
+                                      const float* __restrict__ temb_step, int B, int d, int nseq) {
     const int64_t total = int64_t(nseq) * d;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         const int64_t s = i / d, c = i % d;
-        h[s * seq_rows * d + c] = gpre[i] + temb[c];
+        h[s * seq_rows * d + c] = gpre[i] + temb_step[(s % B) * d + c];
     }
 }
 
@@ -85,18 +87,30 @@ __global__ void dit_tfeat_kernel(const float* __restrict__ tvals, const float* _
     feat[s * 256 + 128 + i] = from_f32<CT>(sinf(arg));
 }
 
-// Per-step sampler scalars, computed on the host in fp32 exactly as
-// Graph::sample_dpmpp_2m / build_cfg_model_output (rf_dit.cpp:798-883, 988-1028).
+// Per-step sampler scalars, computed on the host in fp32 exactly as the reference's samplers
+// (Graph::sample_dpmpp_2m :798-883, sample_dpmpp_3m_sde :680-796, sample_v_ddim :514-604 of
+// src/models/stable_audio/foundation/rf_dit.cpp).
+enum DitSamplerMode : int { kDpmpp2m = 0, kDpmpp3mSde = 1, kVDdim = 2 };
+
 struct DitStepCoef {
-    float c_in, c_skip, c_out;
-    float alpha, sigma;          // cos / sin(t pi / 2) for the CFG x0 algebra
-    float x_scale, d_scale;      // sigma_next / sigma, -expm1(-h)
-    float d_coeff, old_coeff;    // second-order blend (first step: 1, 0)
-    float c_in_next;             // next step's input scale (unused on the last step)
+    float c_in, c_skip, c_out;   // denoiser scalings (v-DDIM: c_in = 1, c_skip/c_out unused)
+    float x_scale, d_scale;      // 2M: sigma_next/sigma, -expm1(-h); 3M: exp(-2h), -expm1(-2h)
+    float d_coeff, old_coeff;    // 2M second-order blend
+    float c_in_next;             // next step's input scale
     float cfg_scale, apg_scale;
-    float sig;                   // sigma of this step (sigma_0 scales the initial noise)
-    int final_step;              // sigma_next == 0: x = denoised
-    int first_step;              // no history yet: first-order update
+    float sig;                   // sigma of this step (sigma_0 scales the initial noise; v-DDIM: 1)
+    float phi2, phi3, r0, r1;    // 3M history corrections
+    float noise_scale;           // 3M: sigma_next * sqrt(-expm1(-2h))
+    int mode;                    // DitSamplerMode
+    int final_step;              // last step: x = denoised (2M/3M) or pred (v-DDIM)
+    int first_step;
+    int hist;                    // 3M: previous denoised outputs available (0, 1, 2)
+    unsigned long long seed, rng_offset, rng_stride;  // 3M noise: TensorIterator Philox stream of this step
+};
+
+// Per (step, prompt): alpha / sigma = cos / sin(t pi / 2) of this and the next timestep.
+struct DitBatchCoef {
+    float alpha, sigma, alpha_next, sigma_next;
 };
 
 // Step input: X[bb, t, c] = ct(x[b, c, t] * c_in), bb over the (CFG-doubled) graph batch.
@@ -131,10 +145,12 @@ constexpr int kApgChunks = 64;
 __global__ void __launch_bounds__(256) dit_apg_partial_kernel(const float* __restrict__ part, int splits,
                                                               int64_t split_stride, const float* __restrict__ x,
                                                               const float* __restrict__ mask, int B, int T,
-                                                              const DitStepCoef* __restrict__ coefs, int step,
+                                                              const DitStepCoef* __restrict__ coefs,
+                                                              const DitBatchCoef* __restrict__ bcoefs, int step,
                                                               double* __restrict__ partials) {
     const DitStepCoef k = coefs[step];
     const int b = blockIdx.y, chunk = blockIdx.x;
+    const DitBatchCoef kb = bcoefs[int64_t(step) * B + b];
     const int n = T * 64;
     const int per = (n + kApgChunks - 1) / kApgChunks;
     const int i0 = chunk * per, i1 = min(n, i0 + per);
@@ -142,9 +158,9 @@ __global__ void __launch_bounds__(256) dit_apg_partial_kernel(const float* __res
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const int t = i / 64, c = i % 64;
         const float xin = x[(int64_t(b) * 64 + c) * T + t] * k.c_in;
-        const float xa = xin * k.alpha;
-        const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * k.sigma;
-        const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * k.sigma;
+        const float xa = xin * kb.alpha;
+        const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * kb.sigma;
+        const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * kb.sigma;
         const float cm = cx0 * mask[int64_t(b) * T + t];
         s1 += double(cm) * cm;
         s2 += double(cx0 - ux0) * cm;
@@ -185,13 +201,16 @@ __global__ void dit_apg_finish_kernel(const double* __restrict__ partials, float
     }
 }
 
-// Fused: CFG/APG combine (or the raw output without CFG), denoised = out * c_out + x * c_skip,
-// DPM++ 2M update of x [B, 64, T] (BCT), history, next step's input, non-finite check.
+// Fused: CFG/APG combine (or the raw output without CFG), then the sampler update of
+// x [B, 64, T] (BCT): DPM++ 2M, DPM++ 3M SDE (history ring + inline Philox noise) or v-DDIM;
+// writes this step's denoised output to hist_cur and the next step's input; non-finite check.
 template <typename CT>
 __global__ void dit_update_kernel(const float* __restrict__ part, int splits, int64_t split_stride,
-                                  float* __restrict__ x, float* __restrict__ old, const float* __restrict__ mask,
-                                  const float* __restrict__ sums, int B, int Bg, int T, int use_cfg,
-                                  const DitStepCoef* __restrict__ coefs, int step, CT* __restrict__ Xnext,
+                                  float* __restrict__ x, float* __restrict__ hist_cur,
+                                  const float* __restrict__ hist_p1, const float* __restrict__ hist_p2,
+                                  const float* __restrict__ mask, const float* __restrict__ sums, int B, int Bg, int T,
+                                  int use_cfg, const DitStepCoef* __restrict__ coefs,
+                                  const DitBatchCoef* __restrict__ bcoefs, int step, CT* __restrict__ Xnext,
                                   float* __restrict__ out, int* __restrict__ status) {
     const DitStepCoef k = coefs[step];
     const int64_t total = int64_t(B) * 64 * T;
@@ -199,12 +218,13 @@ __global__ void dit_update_kernel(const float* __restrict__ part, int splits, in
         const int t = int(i % T);
         const int c = int((i / T) % 64);
         const int b = int(i / (int64_t(T) * 64));
+        const DitBatchCoef kb = bcoefs[int64_t(step) * B + b];
         const float xv = x[i];
         float mo;
-        if (use_cfg) {
-            const float xa = (xv * k.c_in) * k.alpha;
-            const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * k.sigma;
-            const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * k.sigma;
+        if (use_cfg) {  // build_cfg_model_output, rf_dit.cpp:988-1028
+            const float xa = (xv * k.c_in) * kb.alpha;
+            const float cx0 = xa - dit_raw(part, splits, split_stride, b, T, t, c) * kb.sigma;
+            const float ux0 = xa - dit_raw(part, splits, split_stride, b + B, T, t, c) * kb.sigma;
             const float diff = cx0 - ux0;
             const float m = mask[int64_t(b) * T + t];
             const float n = sums[2 * b], dot = sums[2 * b + 1];
@@ -212,20 +232,45 @@ __global__ void dit_update_kernel(const float* __restrict__ part, int splits, in
             const float orth = (diff - dot * v1) * m;
             const float cd = k.apg_scale * orth + (1.0f - k.apg_scale) * diff;
             const float den = cx0 + (k.cfg_scale - 1.0f) * cd;
-            mo = (xa - den) / k.sigma;
+            mo = (xa - den) / kb.sigma;
         } else {
             mo = dit_raw(part, splits, split_stride, b, T, t, c);
         }
-        const float denoised = mo * k.c_out + xv * k.c_skip;
         float nx;
-        if (k.final_step) {
-            nx = denoised;
+        bool bad = !isfinite(mo);
+        if (k.mode == kVDdim) {
+            const float pred = xv * kb.alpha - mo * kb.sigma;
+            if (k.final_step) {
+                nx = pred;
+            } else {
+                const float eps = xv * kb.sigma + mo * kb.alpha;
+                nx = pred * kb.alpha_next + eps * kb.sigma_next;
+            }
         } else {
-            const float dd = k.first_step ? denoised : k.d_coeff * denoised + k.old_coeff * old[i];
-            nx = k.x_scale * xv + k.d_scale * dd;
-            old[i] = denoised;
+            const float denoised = mo * k.c_out + xv * k.c_skip;
+            bad = bad || !isfinite(denoised);
+            if (k.final_step) {
+                nx = denoised;
+            } else if (k.mode == kDpmpp2m) {
+                const float dd = k.first_step ? denoised : k.d_coeff * denoised + k.old_coeff * hist_p1[i];
+                nx = k.x_scale * xv + k.d_scale * dd;
+            } else {  // DPM++ 3M SDE
+                nx = k.x_scale * xv + k.d_scale * denoised;
+                if (k.hist >= 2) {
+                    const float d1_0 = (denoised - hist_p1[i]) / k.r0;
+                    const float d1_1 = (hist_p1[i] - hist_p2[i]) / k.r1;
+                    const float d1 = d1_0 + (d1_0 - d1_1) * k.r0 / (k.r0 + k.r1);
+                    const float d2 = (d1_0 - d1_1) / (k.r0 + k.r1);
+                    nx += k.phi2 * d1 - k.phi3 * d2;
+                } else if (k.hist == 1) {
+                    nx += k.phi2 * ((denoised - hist_p1[i]) / k.r0);
+                }
+                nx += torch_iterator_randn_at(k.seed, k.rng_offset, k.rng_stride, uint64_t(i)) * k.noise_scale;
+            }
+            hist_cur[i] = denoised;
         }
-        if (!isfinite(mo) || !isfinite(nx)) atomicCAS(status, 0, kErrNonFinite);
+        bad = bad || !isfinite(nx);
+        if (bad) atomicCAS(status, 0, kErrNonFinite);
         x[i] = nx;
         if (k.final_step) {
             out[i] = nx;

@@ -185,16 +185,19 @@ void FoundationRfDitRuntime::prepare(const StableAudioSamplingState & sampling, 
 // Validation and messages as Graph::sample / validate_inputs (src/models/stable_audio/foundation/rf_dit.cpp:461-511,
 // 1030-1047); the whole sampler runs on the GPU (b2d_dit_sample).
 std::vector<float> FoundationRfDitRuntime::sample(const StableAudioSamplingState & sampling,
-                                                  const StableAudioConditioningInputs & conditioning, uint64_t,
-                                                  uint64_t &, std::string_view sampler_type, float sigma_min,
-                                                  float sigma_max, float rho, float cfg_scale,
-                                                  float apg_scale) const {
+                                                  const StableAudioConditioningInputs & conditioning, uint64_t seed,
+                                                  uint64_t & rng_offset_blocks,
+                                                  const engine::sampling::TorchCudaSamplingPolicy & rng_policy,
+                                                  std::string_view sampler_type, float sigma_min, float sigma_max,
+                                                  float rho, float cfg_scale, float apg_scale) const {
     prepare(sampling, cfg_scale);
     if (!sampler_type.empty() && sampler_type != "euler" && sampler_type != "pingpong" && sampler_type != "dpmpp-2m" &&
         sampler_type != "dpmpp-3m-sde")
         throw std::runtime_error("Stable Audio Foundation sampler_type is not supported for the v sampler");
-    if (sampler_type != "dpmpp-2m")
-        throw std::runtime_error("b200diff: only the dpmpp-2m sampler runs on the GPU path");
+    // "dpmpp-2m" and "dpmpp-3m-sde" by name; everything else accepted above is the v-DDIM sampler
+    const int32_t sampler = sampler_type == "dpmpp-2m"       ? B2D_SAMPLER_DPMPP_2M
+                            : sampler_type == "dpmpp-3m-sde" ? B2D_SAMPLER_DPMPP_3M_SDE
+                                                             : B2D_SAMPLER_V_DDIM;
     const int64_t B = sampling.batch, T = sampling.latent_sample_size, P2 = config_.prompt_max_length + 2;
     if (conditioning.positive.batch != B || conditioning.positive.cross_tokens != P2 ||
         conditioning.positive.cond_dim != config_.cond_token_dim ||
@@ -205,8 +208,11 @@ std::vector<float> FoundationRfDitRuntime::sample(const StableAudioSamplingState
          conditioning.negative.cond_dim != config_.cond_token_dim))
         throw std::runtime_error("Stable Audio Foundation RF DiT negative conditioning shape mismatch");
     if (static_cast<int64_t>(sampling.noise.size()) != B * config_.io_channels * T ||
-        static_cast<int64_t>(sampling.padding_mask.size()) != B * T || sampling.schedule_points <= 1)
+        static_cast<int64_t>(sampling.padding_mask.size()) != B * T)
         throw std::runtime_error("Stable Audio Foundation RF DiT graph shape mismatch");
+    if (sampling.schedule_points <= 1 ||
+        (sampler == B2D_SAMPLER_V_DDIM && static_cast<int64_t>(sampling.schedule.size()) != B * sampling.schedule_points))
+        throw std::runtime_error("Stable Audio Foundation RF DiT schedule shape mismatch");
     b2d_dit_request rq{};
     rq.batch = B;
     rq.latent_tokens = T;
@@ -221,7 +227,12 @@ std::vector<float> FoundationRfDitRuntime::sample(const StableAudioSamplingState
     rq.rho = rho;
     rq.cfg_scale = cfg_scale;
     rq.apg_scale = apg_scale;
-    rq.sampler = B2D_SAMPLER_DPMPP_2M;
+    rq.sampler = sampler;
+    rq.schedule = sampling.schedule.empty() ? nullptr : sampling.schedule.data();
+    rq.seed = seed;
+    rq.rng_offset_blocks = &rng_offset_blocks;
+    rq.rng_multiprocessor_count = rng_policy.multiprocessor_count;
+    rq.rng_max_threads_per_multiprocessor = rng_policy.max_threads_per_multiprocessor;
     std::vector<float> out(sampling.noise.size());
     device_->check(b2d_dit_sample(device_->ctx(), &rq, out.data(), nullptr));
     return out;

@@ -129,6 +129,18 @@ std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
 
 }  // namespace engine::models::vibevoice
 
+namespace engine::sampling {
+
+// TorchCudaSamplingPolicy (include/engine/framework/sampling/torch_random.h:12-17)
+struct TorchCudaSamplingPolicy {
+    int64_t multiprocessor_count = 1;
+    int64_t max_threads_per_multiprocessor = 256;
+    bool cuda_fast_path = false;
+    int cuda_device_index = 0;
+};
+
+}  // namespace engine::sampling
+
 namespace engine::models::stable_audio {
 
 struct StableAudioConfig {
@@ -175,8 +187,9 @@ public:
     void prepare(const StableAudioSamplingState & sampling, float cfg_scale) const;
     std::vector<float> sample(const StableAudioSamplingState & sampling,
                               const StableAudioConditioningInputs & conditioning, uint64_t seed,
-                              uint64_t & rng_offset_blocks, std::string_view sampler_type, float sigma_min,
-                              float sigma_max, float rho, float cfg_scale, float apg_scale) const;
+                              uint64_t & rng_offset_blocks, const engine::sampling::TorchCudaSamplingPolicy & rng_policy,
+                              std::string_view sampler_type, float sigma_min, float sigma_max, float rho,
+                              float cfg_scale, float apg_scale) const;
 
 private:
     StableAudioConfig config_;

@@ -220,16 +220,17 @@ int test_dit(const std::string & wpath, const std::string & ipath, const std::st
     c.negative.cross_attention = f32(in, "cross_negative");
     c.has_negative = true;
     uint64_t off = 0;
-    const auto out = dit.sample(st, c, 0, off, "dpmpp-2m", f1(in, "sigma_min"), f1(in, "sigma_max"), f1(in, "rho"),
+    engine::sampling::TorchCudaSamplingPolicy pol;
+    const auto out = dit.sample(st, c, 0, off, pol, "dpmpp-2m", f1(in, "sigma_min"), f1(in, "sigma_max"), f1(in, "rho"),
                                 f1(in, "cfg_scale"), f1(in, "apg_scale"));
     const double err = rel_l2(out, f32(g, "exact_latents"));
     std::printf("dit rel-L2 vs fp32-activation oracle %.3g\n", err);
     require(err < 2e-2, "DiT latents vs oracle");
-    require_throws([&] { dit.sample(st, c, 0, off, "bogus", 0.01f, 100.f, 1.f, 7.f, 1.f); },
+    require_throws([&] { dit.sample(st, c, 0, off, pol, "bogus", 0.01f, 100.f, 1.f, 7.f, 1.f); },
                    "sampler_type is not supported");
     auto bad = c;
     bad.positive.cond_dim = 7;
-    require_throws([&] { dit.sample(st, bad, 0, off, "dpmpp-2m", 0.01f, 100.f, 1.f, 7.f, 1.f); },
+    require_throws([&] { dit.sample(st, bad, 0, off, pol, "dpmpp-2m", 0.01f, 100.f, 1.f, 7.f, 1.f); },
                    "positive conditioning shape mismatch");
     return failures;
 }

@@ -153,7 +153,9 @@ typedef struct {
     int64_t prompt_max_length;  /* 128: cross tokens = prompt_max_length + 2 */
 } b2d_dit_config;
 
-enum { B2D_SAMPLER_DPMPP_2M = 0 };
+/* FoundationRfDitRuntime::sample sampler_type values: "dpmpp-2m", "dpmpp-3m-sde", and "" / "euler" /
+ * "pingpong", which the reference routes to its v-DDIM sampler on sampling.schedule (rf_dit.cpp:461-604). */
+enum { B2D_SAMPLER_DPMPP_2M = 0, B2D_SAMPLER_DPMPP_3M_SDE = 1, B2D_SAMPLER_V_DDIM = 2 };
 
 /* One FoundationRfDitRuntime::sample request (include/engine/models/stable_audio/foundation/rf_dit.h:73-106)
  * with its StableAudioSamplingState / StableAudioConditioningInputs payloads (fp32, row-major):
@@ -172,7 +174,12 @@ typedef struct {
     const float* global_cond;
     float sigma_min, sigma_max, rho;
     float cfg_scale, apg_scale;
-    int32_t sampler;            /* B2D_SAMPLER_DPMPP_2M ("dpmpp-2m") */
+    int32_t sampler;            /* B2D_SAMPLER_* */
+    const float* schedule;      /* v-DDIM: sampling.schedule [batch, steps + 1]; otherwise unused */
+    uint64_t seed;              /* DPM++ 3M SDE noise seed */
+    uint64_t* rng_offset_blocks;            /* in/out: TensorIterator Philox offset (may be NULL: starts at 0) */
+    int64_t rng_multiprocessor_count;       /* TorchCudaSamplingPolicy (include/engine/framework/sampling/ */
+    int64_t rng_max_threads_per_multiprocessor;  /* torch_random.h:12-17); <= 0 selects 1 / 256 */
 } b2d_dit_request;
 
 /* Loads the DiT from its GGUF tensors ("model.model.*", names as load_foundation_rf_dit_weights,
@@ -211,6 +218,14 @@ enum {
 B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
                     int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);
+
+/* torch-CUDA-compatible normals on the device (src/framework/sampling/torch_random.cpp):
+ * layout 0 = generate_torch_cuda_randn(count, seed) starting at element `offset`;
+ * layout 1 = generate_torch_cuda_tensor_iterator_randn(count, seed, offset_blocks = offset, policy).
+ * bf16 != 0 rounds each value to bfloat16 like TorchRandnPrecision::BFloat16. */
+B2D_API b2d_status b2d_torch_randn(b2d_ctx* ctx, int32_t layout, uint64_t seed, uint64_t offset, int64_t count,
+                                   int64_t multiprocessor_count, int64_t max_threads_per_multiprocessor, int32_t bf16,
+                                   float* out_dev, void* stream);
 
 /* Flash attention, head_dim 64, scale 1/8: for each sequence s < nseq and head h < heads,
  * O[s, :, h] = softmax(Q[s, :, h] K[s, :, h / kv_rep]^T / 8) V[s, :, h / kv_rep]

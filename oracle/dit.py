@@ -177,6 +177,111 @@ def polyexponential_sigmas(steps: int, smin: float, smax: float, rho: float):
     return sig
 
 
+def _graph_inputs(cfg: DitConfig, inp: Dict[str, B.Tensor]):
+    Bn, T = cfg.batch, cfg.latent_tokens
+    use_cfg = cfg.cfg != 1.0
+    pos, neg = inp["cross_positive"].array(), inp["cross_negative"].array()
+    glob = inp["global"].array()
+    pmask = inp["padding_mask"].array()
+    cross = np.concatenate([pos, neg if int(inp["has_negative"].data[0]) else np.zeros_like(pos)]) if use_cfg else pos
+    globg = np.concatenate([glob, glob]) if use_cfg else glob
+    pad = np.ones((2 * Bn if use_cfg else Bn, T + 1), np.float32)
+    pad[:, 1:] = np.concatenate([pmask, pmask]) if use_cfg else pmask
+    return use_cfg, cross, globg, pad, pmask
+
+
+def _model(dit: Dit, cfg: DitConfig, xin: np.ndarray, t_per_b: np.ndarray, cross, globg, pad, pmask, use_cfg):
+    """run_dit_model with per-prompt timesteps: xin [B, C, T] -> model output [B, C, T]."""
+    Bn = cfg.batch
+    xbtc = xin.transpose(0, 2, 1)
+    xg = np.concatenate([xbtc, xbtc]) if use_cfg else xbtc
+    tg = np.concatenate([t_per_b, t_per_b]) if use_cfg else t_per_b
+    if np.all(tg == tg[0]):
+        raw = dit.forward(np.ascontiguousarray(xg), float(tg[0]), cross, globg, pad)
+    else:  # per-row timestep features: run the graph row by row
+        raw = np.concatenate([dit.forward(np.ascontiguousarray(xg[i:i + 1]), float(tg[i]), cross[i:i + 1],
+                                          globg[i:i + 1], pad[i:i + 1]) for i in range(len(tg))])
+    if not use_cfg:
+        return raw.transpose(0, 2, 1)
+    outs = [cfg_apg(raw[[b, Bn + b]], xbtc[b:b + 1], float(t_per_b[b]), 1, pmask[b:b + 1], cfg.cfg, cfg.apg)
+            for b in range(Bn)]
+    return np.concatenate(outs).transpose(0, 2, 1)
+
+
+def sample_v_ddim(dit: Dit, cfg: DitConfig, inp: Dict[str, B.Tensor]) -> np.ndarray:
+    """Graph::sample_v_ddim (rf_dit.cpp:514-604) on sampling.schedule [B, steps + 1]."""
+    use_cfg, cross, globg, pad, pmask = _graph_inputs(cfg, inp)
+    sched = inp["schedule"].array().reshape(cfg.batch, cfg.steps + 1)
+    x = inp["noise"].array().astype(np.float32).copy()
+    for step in range(cfg.steps):
+        t = sched[:, step].astype(np.float32)
+        tn = sched[:, step + 1].astype(np.float32)
+        al = np.array([f32(math.cos(float(f32(v) * PI * f32(0.5)))) for v in t], np.float32)[:, None, None]
+        sg = np.array([f32(math.sin(float(f32(v) * PI * f32(0.5)))) for v in t], np.float32)[:, None, None]
+        aln = np.array([f32(math.cos(float(f32(v) * PI * f32(0.5)))) for v in tn], np.float32)[:, None, None]
+        sgn = np.array([f32(math.sin(float(f32(v) * PI * f32(0.5)))) for v in tn], np.float32)[:, None, None]
+        mo = _model(dit, cfg, x, t, cross, globg, pad, pmask, use_cfg)
+        pred = (x * al - mo * sg).astype(np.float32)
+        if step + 1 < cfg.steps:
+            eps = (x * sg + mo * al).astype(np.float32)
+            x = (pred * aln + eps * sgn).astype(np.float32)
+        else:
+            x = pred
+    return x
+
+
+def sample_dpmpp_3m_sde(dit: Dit, cfg: DitConfig, inp: Dict[str, B.Tensor]) -> np.ndarray:
+    """Graph::sample_dpmpp_3m_sde (rf_dit.cpp:680-796); noise from the torch-CUDA TensorIterator Philox stream."""
+    from . import philox
+    use_cfg, cross, globg, pad, pmask = _graph_inputs(cfg, inp)
+    seed = int(inp["seed"].data[0])
+    sms, mt = int(inp["rng_sms"].data[0]), int(inp["rng_max_threads"].data[0])
+    offset = int(inp["rng_offset"].data[0]) if "rng_offset" in inp else 0
+    sig = polyexponential_sigmas(cfg.steps, cfg.sigma_min, cfg.sigma_max, cfg.rho)
+    x = (inp["noise"].array() * sig[0]).astype(np.float32)
+    d1 = d2 = None
+    h1 = h2 = f32(0.0)
+    for step in range(cfg.steps):
+        s, sn = sig[step], sig[step + 1]
+        c_in = f32(f32(1.0) / f32(math.sqrt(float(f32(s * s + f32(1.0))))))
+        c_skip = f32(f32(1.0) / f32(s * s + f32(1.0)))
+        c_out = f32(-s / f32(math.sqrt(float(f32(s * s + f32(1.0))))))
+        t = f32(f32(math.atan(float(s))) * f32(2.0) / PI)
+        mo = _model(dit, cfg, (x * c_in).astype(np.float32), np.full(cfg.batch, t, np.float32), cross, globg, pad,
+                    pmask, use_cfg)
+        den = (mo * c_out + x * c_skip).astype(np.float32)
+        if sn == 0.0:
+            x = den
+            break
+        h = f32(-f32(np.log(sn)) + f32(np.log(s)))
+        he = f32(h * f32(2.0))
+        x = (f32(np.exp(-he)) * x + f32(-np.expm1(-he)) * den).astype(np.float32)
+        if d2 is not None:
+            r0, r1 = f32(h1 / h), f32(h2 / h)
+            phi2 = f32(f32(np.expm1(-he)) / he + f32(1.0))
+            phi3 = f32(phi2 / he - f32(0.5))
+            a = ((den - d1) / r0).astype(np.float32)
+            b = ((d1 - d2) / r1).astype(np.float32)
+            dd1 = (a + (a - b) * r0 / f32(r0 + r1)).astype(np.float32)
+            dd2 = ((a - b) / f32(r0 + r1)).astype(np.float32)
+            x = (x + phi2 * dd1 - phi3 * dd2).astype(np.float32)
+        elif d1 is not None:
+            r = f32(h1 / h)
+            phi2 = f32(f32(np.expm1(-he)) / he + f32(1.0))
+            x = (x + phi2 * ((den - d1) / r)).astype(np.float32)
+        noise = philox.tensor_iterator_randn(x.size, seed, offset, sms, mt).reshape(x.shape)
+        offset += philox.offset_blocks(x.size, sms, mt)
+        x = (x + noise * f32(sn * f32(math.sqrt(float(f32(-np.expm1(f32(-2.0) * h))))))).astype(np.float32)
+        d2, d1 = d1, den
+        h2, h1 = h1, h
+    return x
+
+
+def sample(dit: Dit, cfg: DitConfig, inp: Dict[str, B.Tensor]) -> np.ndarray:
+    return {"dpmpp-2m": sample_dpmpp_2m, "dpmpp-3m-sde": sample_dpmpp_3m_sde, "": sample_v_ddim}[cfg.sampler](
+        dit, cfg, inp)
+
+
 def sample_dpmpp_2m(dit: Dit, cfg: DitConfig, inp: Dict[str, B.Tensor]) -> np.ndarray:
     """Graph::sample_dpmpp_2m (rf_dit.cpp:798-883) with the graph's CFG/APG. Returns latents [B, 64, T]."""
     Bn, T, C = cfg.batch, cfg.latent_tokens, cfg.io_channels

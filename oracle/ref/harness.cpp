@@ -366,6 +366,11 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     }
     const float cfg_scale = f32_scalar(in, "cfg_scale");
     const float apg_scale = f32_scalar(in, "apg_scale");
+    // sampler: 0 "dpmpp-2m", 1 "dpmpp-3m-sde", 2 "" (v-DDIM on sampling.schedule)
+    const int64_t sampler = in.count("sampler") ? i64_scalar(in, "sampler") : 0;
+    const uint64_t seed = in.count("seed") ? static_cast<uint64_t>(i64_scalar(in, "seed")) : 0;
+    if (in.count("schedule")) sampling.schedule = f32s(in, "schedule");
+    const char * sampler_name = sampler == 1 ? "dpmpp-3m-sde" : (sampler == 2 ? "" : "dpmpp-2m");
     const float sigma_min = f32_scalar(in, "sigma_min");
     const float sigma_max = f32_scalar(in, "sigma_max");
     const float rho = f32_scalar(in, "rho");
@@ -373,18 +378,52 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
     sa::foundation::FoundationRfDitRuntime dit(exec, assets, engine::assets::TensorStorageType::Native);
     engine::sampling::TorchCudaSamplingPolicy policy;
+    if (in.count("rng_sms")) policy.multiprocessor_count = i64_scalar(in, "rng_sms");
+    if (in.count("rng_max_threads")) policy.max_threads_per_multiprocessor = i64_scalar(in, "rng_max_threads");
     std::vector<float> times;
+    uint64_t final_offset = 0;
     std::vector<float> result;
     dit.prepare(sampling, cfg_scale);
     for (int r = 0; r < std::max(reps, 1); ++r) {
-        uint64_t offset = 0;
+        uint64_t offset = in.count("rng_offset") ? static_cast<uint64_t>(i64_scalar(in, "rng_offset")) : 0;
         const double t0 = now_ms();
-        result = dit.sample(sampling, cond, 0, offset, policy, "dpmpp-2m", sigma_min, sigma_max, rho, cfg_scale, apg_scale);
+        result = dit.sample(sampling, cond, seed, offset, policy, sampler_name, sigma_min, sigma_max, rho, cfg_scale,
+                            apg_scale);
         times.push_back(static_cast<float>(now_ms() - t0));
+        final_offset = offset;
     }
     Bundle out;
+    const int64_t fo = static_cast<int64_t>(final_offset);
+    out["rng_offset_out"] = raw_entry(I64, &fo, 8, {1});
     out["latents"] = f32_entry(result, {batch, c.io_channels, tokens});
     out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
+// ------------------------------------------------------------- Philox randn
+// torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
+int cmd_randn(const std::string & in_path, const std::string & out_path) {
+    const Bundle in = read_bundle(in_path);
+    const int64_t count = i64_scalar(in, "count");
+    const uint64_t seed = static_cast<uint64_t>(i64_scalar(in, "seed"));
+    const uint64_t offset = static_cast<uint64_t>(i64_scalar(in, "offset"));
+    engine::sampling::TorchCudaSamplingPolicy policy;
+    policy.multiprocessor_count = i64_scalar(in, "sms");
+    policy.max_threads_per_multiprocessor = i64_scalar(in, "max_threads");
+    const auto a = engine::sampling::generate_torch_cuda_randn(size_t(count), seed,
+                                                               engine::sampling::TorchRandnPrecision::Float32);
+    const auto b = engine::sampling::generate_torch_cuda_randn(size_t(count), seed,
+                                                               engine::sampling::TorchRandnPrecision::BFloat16);
+    const auto c = engine::sampling::generate_torch_cuda_tensor_iterator_randn(
+        size_t(count), seed, offset, policy, engine::sampling::TorchRandnPrecision::Float32);
+    const int64_t next = static_cast<int64_t>(offset + engine::sampling::torch_cuda_tensor_iterator_offset_blocks(
+                                                          uint64_t(count), policy));
+    Bundle out;
+    out["randn_f32"] = f32_entry(a, {count});
+    out["randn_bf16"] = f32_entry(b, {count});
+    out["iterator_f32"] = f32_entry(c, {count});
+    out["next_offset"] = raw_entry(I64, &next, 8, {1});
     write_bundle(out_path, out);
     return 0;
 }
@@ -433,6 +472,7 @@ int main(int argc, char ** argv) {
             return argv[i];
         };
         if (cmd == "q8") return cmd_q8(arg(2), arg(3));
+        if (cmd == "randn") return cmd_randn(arg(2), arg(3));
         if (cmd == "vvsched") return cmd_vvsched(arg(2), arg(3));
         if (cmd == "vvpredict") return cmd_vvpredict(arg(2), arg(3), arg(4), std::stoi(arg(5)));
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));

@@ -165,6 +165,11 @@ class DitConfig:
     wtype: str = BF16
     wseed: int = 0
     prompt_seeds: tuple = field(default_factory=lambda: (0,))
+    sampler: str = "dpmpp-2m"     # "dpmpp-2m", "dpmpp-3m-sde" or "" (v-DDIM on a given schedule)
+    seed: int = 42                # Philox seed of the SDE noise
+    rng_sms: int = 148            # TorchCudaSamplingPolicy of the reference caller
+    rng_max_threads: int = 2048
+    ragged_mask: bool = False
 
     @property
     def head_dim(self) -> int:
@@ -190,6 +195,12 @@ DIT_CONFIGS = {
     "tiny_q8_b2_noapg": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
                                   prompt_max_length=14, latent_tokens=48, steps=5, batch=2, apg=0.0,
                                   wtype=Q8_0, prompt_seeds=(3, 4)),
+    "tiny_bf16_vddim": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
+                                 prompt_max_length=14, latent_tokens=40, steps=5, batch=2, sampler="",
+                                 prompt_seeds=(6, 7), ragged_mask=True),
+    "tiny_f16_3msde": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
+                                prompt_max_length=14, latent_tokens=40, steps=6, batch=2, sampler="dpmpp-3m-sde",
+                                wtype=F16, prompt_seeds=(8, 9)),
     "tiny_f16_ragged": DitConfig(embed_dim=256, depth=1, num_heads=4, cond_token_dim=128, global_cond_dim=256,
                                  prompt_max_length=14, latent_tokens=37, steps=4, wtype=F16),
 }
@@ -258,6 +269,20 @@ def dit_inputs(cfg: DitConfig) -> Dict[str, B.Tensor]:
     d["cross_positive"] = B.f32(cross)
     d["cross_negative"] = B.f32(np.zeros_like(cross))
     d["global"] = B.f32(glob)
-    d["padding_mask"] = B.f32(np.ones((Bn, T), np.float32))
+    mask = np.ones((Bn, T), np.float32)
+    if cfg.ragged_mask:  # prompt b keeps its first T - 7 (b + 1) latent frames, as a shorter duration would
+        for b in range(Bn):
+            mask[b, T - 7 * (b + 1):] = 0.0
+    d["padding_mask"] = B.f32(mask)
     d["has_negative"] = B.i64(1)
+    d["sampler"] = B.i64({"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2}[cfg.sampler])
+    d["seed"] = B.i64(cfg.seed)
+    d["rng_sms"] = B.i64(cfg.rng_sms)
+    d["rng_max_threads"] = B.i64(cfg.rng_max_threads)
+    d["rng_offset"] = B.i64(0)
+    # v-DDIM schedule [B, steps + 1]: 1 -> 0 with a per-prompt warp (make_schedule, stable_audio/sampler.cpp:131-154)
+    lin = np.linspace(1.0, 0.0, cfg.steps + 1, dtype=np.float64)
+    sched = np.stack([lin ** (1.0 + 0.25 * b) for b in range(Bn)]).astype(np.float32)
+    sched[:, 0], sched[:, -1] = 1.0, 0.0
+    d["schedule"] = B.f32(sched)
     return d

@@ -30,7 +30,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_frame_f16", "one_step_q8",
                 "vv15_f16_64", "vv15_q8_1024"]
-DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps"]
+DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vddim", "tiny_f16_3msde",
+               "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps"]
 
 
 def digest(*bundles) -> np.ndarray:
@@ -92,7 +93,7 @@ def dit_golden(name: str) -> None:
     cfg = synth.DIT_CONFIGS[name]
     w, inp = synth.dit_weights(cfg), synth.dit_inputs(cfg)
     out = ref_runner.run("dit", inp, w)
-    exact = dit.sample_dpmpp_2m(dit.Dit(w, cfg, act="exact"), cfg, inp)  # fp32-activation restatement
+    exact = dit.sample(dit.Dit(w, cfg, act="exact"), cfg, inp)  # fp32-activation restatement
     B.write(os.path.join(HERE, "dit_%s.b2db" % name),
             {"latents": out["latents"], "exact_latents": B.f32(exact),
              "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})

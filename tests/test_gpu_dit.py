@@ -64,11 +64,12 @@ def run(cfg, dit, inp):
     return dit.sample(inp["noise"].array(), inp["padding_mask"].array(), inp["cross_positive"].array(),
                       inp["cross_negative"].array(), inp["global"].array(), steps=cfg.steps,
                       sigma_min=cfg.sigma_min, sigma_max=cfg.sigma_max, rho=cfg.rho, cfg_scale=cfg.cfg,
-                      apg_scale=cfg.apg)
+                      apg_scale=cfg.apg, sampler=cfg.sampler, schedule=inp["schedule"].array(), seed=cfg.seed,
+                      rng_offset=0, rng_policy=(cfg.rng_sms, cfg.rng_max_threads))
 
 
 @pytest.mark.parametrize("name", ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "sao_bf16_1x1024_2steps",
-                                  "sao_q8_1x1024_2steps"])
+                                  "sao_q8_1x1024_2steps", "tiny_bf16_vddim", "tiny_f16_3msde"])
 def test_dit_sample_matches_reference(b2d, ctx, name):
     cfg, dit = make_dit(b2d, ctx, name)
     inp = synth.dit_inputs(cfg)
@@ -85,6 +86,40 @@ def test_dit_sample_matches_reference(b2d, ctx, name):
         "rel-L2 %.3g vs exact oracle (spread %.3g)" % (err_exact, spread)
     out2 = run(cfg, dit, inp)
     assert np.array_equal(out, out2)
+    # rng_offset_blocks out-parameter: one TensorIterator draw per step with a non-zero next sigma
+    from oracle import philox
+    draws = cfg.steps - 1 if cfg.sampler == "dpmpp-3m-sde" else 0
+    n = cfg.batch * cfg.io_channels * cfg.latent_tokens
+    assert dit.rng_offset_blocks == draws * philox.offset_blocks(n, cfg.rng_sms, cfg.rng_max_threads)
+
+
+# Known answers of generate_torch_cuda_randn / the TensorIterator form
+# (tests/unittests/test_torch_random.cpp:33-100 of audio.cpp) are pinned against the oracle on CPU
+# in test_oracle.py; here the device generator must equal that oracle bit for bit.
+@pytest.mark.parametrize("layout,count,seed,offset,sms,mt,bf16", [
+    (0, 4099, 1234, 0, 1, 256, False), (0, 1000, 5678, 0, 1, 256, True),
+    (1, 65 * 64 * 3, 42, 0, 148, 2048, False), (1, 5000, 7, 13, 1, 256, False), (1, 1 << 20, 99, 5, 148, 2048, True)])
+def test_torch_randn_matches_oracle(ctx, layout, count, seed, offset, sms, mt, bf16):
+    from oracle import philox
+    out = torch.empty(count, dtype=torch.float32, device="cuda")
+    ctx.torch_randn(out.data_ptr(), count, seed, offset, layout, sms, mt, bf16,
+                    stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    if layout == 0:
+        ref = philox.torch_cuda_randn(count, seed, bf16=bf16, start=offset)
+    else:
+        ref = philox.tensor_iterator_randn(count, seed, offset, sms, mt, bf16=bf16)
+    # log / sin / cos of the device math library versus libm: a few fp32 ulp, which after bf16 rounding
+    # can flip a value that sits on a rounding boundary by one bf16 ulp (2^-7 relative)
+    if bf16:
+        diff = got != ref
+        assert diff.mean() < 1e-4
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref[diff]), 1e-30))) - 7)
+        assert (np.abs(got[diff] - ref[diff]) <= ulp).all()
+    else:
+        np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
+    assert abs(float(got.mean())) < 0.1 and abs(float(got.std()) - 1.0) < 0.1
 
 
 def test_dit_without_cfg_and_device_api(b2d, ctx):

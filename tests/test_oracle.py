@@ -76,3 +76,46 @@ def test_head_port_vs_reference(name):
     mine = V.sample_speech_latents(head, cfg, inp["positive_condition"].array(),
                                    inp["negative_condition"].array(), inp["initial_speech"].array())
     assert rel_l2(mine, g["latents"].array()) < HEAD_TOL[name]
+
+
+# Known answers of generate_torch_cuda_randn (tests/unittests/test_torch_random.cpp:33-100 of audio.cpp).
+KAT_F32_1234 = [-1.61649048, 0.56845516, -0.510224819, -0.911339402, -1.15551639, -0.22615087, -1.2891326, 1.065382,
+                -0.7166605, -0.533334374, 0.207757875, -0.979843318, 0.744693458, -0.239484429, 0.27371496,
+                0.092008315]
+KAT_F32_1234_AT = {16: -0.803610802, 17: -1.6377064, 31: -0.300402969, 32: -0.251393795, 63: -0.924830973,
+                   64: 0.799798131, 127: -0.167921364, 128: -0.322486848, 255: -1.76037288, 256: 0.534284174,
+                   299: -0.986868858}
+KAT_BF16_5678 = [-0.65625, -0.5625, 0.384765625, -0.151367188, 0.7421875, 0.244140625, 0.609375, 0.00321960449,
+                 -0.46875, 0.306640625, -0.225585938, -0.9140625, 0.7734375, 0.120117188, 0.52734375, -0.5078125]
+KAT_BF16_1234_AT = {16: -0.8046875, 17: -1.640625, 31: -0.30078125, 32: -0.251953125, 63: -0.92578125,
+                    64: 0.80078125, 127: -0.16796875, 128: -0.322265625, 255: -1.7578125, 256: 0.53515625,
+                    299: -0.98828125}
+
+
+def test_philox_randn_known_answers():
+    from oracle import philox
+    np.testing.assert_allclose(philox.torch_cuda_randn(16, 1234), KAT_F32_1234, rtol=0, atol=2e-6)
+    full = philox.torch_cuda_randn(300, 1234)
+    for i, v in KAT_F32_1234_AT.items():
+        assert abs(full[i] - v) <= 2e-6, i
+    assert np.array_equal(philox.torch_cuda_randn(16, 5678, bf16=True), np.float32(KAT_BF16_5678))
+    fb = philox.torch_cuda_randn(300, 1234, bf16=True)
+    for i, v in KAT_BF16_1234_AT.items():
+        assert fb[i] == np.float32(v), i
+    # start index slices the full stream (test_start_index_matches_full_generation_slice)
+    assert np.array_equal(philox.torch_cuda_randn(32, 1234, start=128), full[128:160])
+
+
+def test_philox_tensor_iterator_layout():
+    from oracle import philox
+    # stride = 256 * min(blocks, SMs * threads / 256); each call advances ceil(n / (4 * stride))
+    assert philox.iterator_stride(1000, 1, 256) == 256
+    assert philox.offset_blocks(1000, 1, 256) == 1
+    assert philox.offset_blocks(1025, 1, 256) == 2
+    n = 64 * 3 * 1024
+    st = philox.iterator_stride(n, 148, 2048)
+    assert st == 256 * min((n + 255) // 256, 148 * 8)
+    a = philox.tensor_iterator_randn(n, 5, 3, 148, 2048)
+    # element seq < stride with loop 0, component 0 is Philox(counter=(offset, 0, seq, 0)).x through Box-Muller
+    x, y, _, _ = philox.philox4x32_10(np.uint64(3), 0, np.arange(4, dtype=np.uint64), 0, 5)
+    assert np.array_equal(a[:4], philox.box_muller(x, y)[0])
