@@ -16,6 +16,7 @@
 
 #include "../../include/b200diff.h"
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "dit_kernels.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
@@ -717,6 +718,7 @@ b2d_status b2d_create(int device, b2d_ctx** out) {
         CK(cudaStreamCreateWithFlags(&ctx->load_stream, cudaStreamNonBlocking));
         encode_fn();
         if (const char* mt = std::getenv("B2D_ATTN_MT")) g_attn_mt = std::atoi(mt);
+        if (const char* at = std::getenv("B2D_ATTN")) g_attn_tc = std::strcmp(at, "mma") != 0;
     });
     if (s != B2D_OK) return s;
     *out = ctx.release();
@@ -886,16 +888,17 @@ b2d_status b2d_attention(b2d_ctx* ctx, int32_t bf16, const void* q, int64_t q_ro
         if (!q || !k || !v || !o || lq <= 0 || lk <= 0 || heads <= 0 || kv_rep <= 0 || nseq <= 0 ||
             heads % kv_rep)
             fail(B2D_EINVAL, "invalid attention shape");
-        if ((q_row | kv_row | q_seq | kv_seq) % 8 || (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
-                                                      reinterpret_cast<uintptr_t>(v)) % 16)
+        if ((q_row | kv_row | q_seq | kv_seq | o_row | o_seq) % 8 ||
+            (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+             reinterpret_cast<uintptr_t>(o)) % 16)
             fail(B2D_EINVAL, "attention operands need 16-byte aligned rows");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         if (bf16)
             dit_attention<__nv_bfloat16>(q, q_row, q_seq, k, v, kv_row, kv_seq, o, o_row, o_seq, lq, lk, kv_rep,
-                                         heads, nseq, st);
+                                         heads, nseq, ctx->status.as<int>(), st);
         else
             dit_attention<__half>(q, q_row, q_seq, k, v, kv_row, kv_seq, o, o_row, o_seq, lq, lk, kv_rep, heads,
-                                  nseq, st);
+                                  nseq, ctx->status.as<int>(), st);
     });
 }
 
