@@ -4,25 +4,26 @@
 // as rf_attention uses it (src/models/stable_audio/foundation/rf_dit.cpp:175-198), both the
 // self-attention (L = 1025) and the T5 cross-attention (130 keys, KV head = h / kv_rep).
 //
-// CTA (352 threads, one CTA per SM) = two 128-query tiles of one (sequence, head) sharing the
-// K/V stream:
-//   warp 0      TMA producer: Q tiles once, then 128-key K and V blocks through a 2-deep ring
-//               (3-D tensor maps [sequence][row][column]: rows past a sequence's end read 0)
-//   warps 1, 2  MMA issuers of tile 0 / tile 1 (warp 1 also owns TMEM), so the two tiles never
-//               wait on each other.  S_t = Q_t K_j^T is issued as two 64-key halves
-//               (M 128, N 64, K 64) with their own full / free barriers, so the first half of the
-//               next block is computed while the softmax still works on the second half of this
-//               one; O_t += P_t V_j  (M 128, N 64, K 128; P K-major from smem, V MN-major).  A K
-//               or V stage is released when the MMAs of every active tile that read it completed.
-//   warps 3-6   softmax of tile 0, warps 7-10 softmax of tile 1 (thread = query row = TMEM lane).
-//               Per 32-key chunk: S -> registers, p = 2^(s*scale*log2e - m) -> fp16/bf16 P (SW128
-//               K-major, double-buffered so the next P never waits for the previous P V), row sum.
-//               m is a lazily raised running max: only when a score exceeds it by more than 2^8
-//               (p > 256, still exact in fp32 / fp16 / bf16 range) is m raised to the chunk max and
-//               the row's sum, its P chunks already written for this block, and O (in TMEM) scaled
-//               down.  The epilogue applies 1/l, stages O through the dead Q tile and writes it
-//               with one TMA store (rows past the sequence are clipped).
-// TMEM (512 columns): S_0 [0,128), S_1 [128,256), O_0 [256,320), O_1 [320,384).
+// CTA (608 threads, one CTA per SM) = two 128-query tiles of one (sequence, head) sharing the
+// K/V stream.  Keys come in 128-key blocks; each block is split into two 64-key halves, and
+// half h of every block belongs to its own softmax warp set with its own running max, row sum
+// and O accumulator (flash-decoding style split of the key range, merged in the epilogue):
+//   warp 0        TMA producer: Q tiles once, then K and V blocks through a 2-deep ring
+//                 (3-D tensor maps [sequence][row][column]: rows past a sequence's end read 0)
+//   warps 1, 2    MMA issuers of tile 0 / tile 1 (warp 1 also owns TMEM):
+//                 S_{t,h} = Q_t K_{j,h}^T   (M 128, N 64, K 64) into TMEM,
+//                 O_{t,h} += P_{t,h} V_{j,h} (M 128, N 64, K 64; P K-major from smem, V MN-major);
+//                 a K / V stage is released when the MMAs of every active tile that read it completed
+//   warps 3-18    softmax, 4 warps per (tile, half); thread = query row = TMEM lane.  Per block:
+//                 S half -> registers, p = 2^(s*scale*log2e - m) -> fp16/bf16 P (SW128 K-major,
+//                 double-buffered so the next P never waits for the previous P V), row sum.  m is a
+//                 lazily raised running max: only when a score exceeds it by more than 2^8 (p > 256,
+//                 still exact in fp32 / fp16 / bf16 range) is it raised to the half's max and the
+//                 row's sum and O (in TMEM) scaled down.  Four softmax warps share each SM
+//                 sub-partition, so one warp's exponentials overlap another's bookkeeping.
+// Epilogue: m = max(m_0, m_1), O = (O_0 2^(m_0 - m) + O_1 2^(m_1 - m)) / (l_0 2^(m_0 - m) + l_1 2^(m_1 - m)),
+// staged through the dead Q tile and written with one TMA store (rows past the sequence clipped).
+// TMEM (512 columns): S_t at [128 t, 128 t + 128) (half h at +64 h), O_{t,h} at 256 + 128 t + 64 h.
 // Keys past lk get p = 0; V rows there are zero-filled by TMA.
 #pragma once
 
@@ -37,12 +38,12 @@
 namespace b2d {
 
 constexpr int kFaStages = 2;
-constexpr int kFaThreads = 352;
+constexpr int kFaThreads = 608;
 constexpr uint32_t kFaTile = 128 * 64 * 2;              // one 128 x 64 fp16/bf16 tile, 16 KB
 constexpr uint32_t kFaQ = 0;                            // two Q tiles (reused as O staging)
 constexpr uint32_t kFaK = 2 * kFaTile;                  // K ring
 constexpr uint32_t kFaV = kFaK + kFaStages * kFaTile;   // V ring
-constexpr uint32_t kFaP = kFaV + kFaStages * kFaTile;   // P[tile][buffer], 128 x 128 = two 16 KB panels
+constexpr uint32_t kFaP = kFaV + kFaStages * kFaTile;   // P[tile][buffer][half]: 128 rows x 64 keys each
 constexpr uint32_t kFaBar = kFaP + 8 * kFaTile;
 constexpr uint32_t kFaSmemBytes = kFaBar + 256 + 1024;  // + barriers + alignment slack
 constexpr float kFaRescaleLog2 = 8.0f;                  // lazy-rescale bound (log2 units)
@@ -51,6 +52,12 @@ constexpr float kFaRescaleLog2 = 8.0f;                  // lazy-rescale bound (l
 // at trace[event * 64 + block].
 #ifdef B2D_FA_TRACE
 __device__ unsigned long long g_fa_trace[32 * 64];
+__device__ int g_fa_where[32];  // last wait point per warp of CTA (0,0,0)
+#define FA_WHERE(code)                                                                                     \
+    do {                                                                                                   \
+        if (blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && (threadIdx.x & 31) == 0) \
+            g_fa_where[threadIdx.x >> 5] = (code);                                                          \
+    } while (0)
 #define FA_STAMP(ev, j)                                                                      \
     do {                                                                                     \
         if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 64)               \
@@ -60,6 +67,9 @@ __device__ unsigned long long g_fa_trace[32 * 64];
 #define FA_STAMP(ev, j) \
     do {                \
     } while (0)
+#define FA_WHERE(code) \
+    do {               \
+    } while (0)
 #endif
 
 struct FaArgs {
@@ -68,18 +78,8 @@ struct FaArgs {
     int* status;
 };
 
-// Scales the 8 packed fp16/bf16 values of one 16-byte P chunk by f.
-template <typename CT>
-__device__ __forceinline__ void fa_scale_chunk(uint8_t* p, float f) {
-    uint4 v = *reinterpret_cast<uint4*>(p);
-    uint32_t* w = &v.x;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        CT h[2];
-        *reinterpret_cast<uint32_t*>(h) = w[i];
-        w[i] = CtTraits<CT>::pack2(float(h[0]) * f, float(h[1]) * f);
-    }
-    *reinterpret_cast<uint4*>(p) = v;
+__device__ __forceinline__ float fa_max8(const float (&m)[8]) {
+    return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
 }
 
 template <typename CT>
@@ -96,9 +96,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     uint64_t* v_empty = v_full + kFaStages;    // [stage]
     uint64_t* s_full = v_empty + kFaStages;    // [tile][half]
     uint64_t* s_free = s_full + 4;             // [tile][half]
-    uint64_t* p_full = s_free + 4;             // [tile]
-    uint64_t* pv_done = p_full + 2;            // [tile][P buffer]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 4);
+    uint64_t* p_full = s_free + 4;             // [tile][half]
+    uint64_t* pv_done = p_full + 4;            // [tile][half][P buffer]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -106,6 +106,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int kvh = head / a.kv_rep;
     const int q0[2] = {int(blockIdx.x) * 256, int(blockIdx.x) * 256 + 128};
     const bool active[2] = {q0[0] < a.lq, q0[1] < a.lq};
+    // softmax warps per (tile, half) that own a valid query row; only they arrive on the
+    // softmax barriers (a warp without rows would run ahead and complete the next phase early)
+    const int vw[2] = {active[0] ? min(4, (a.lq - q0[0] + 31) >> 5) : 0,
+                       active[1] ? min(4, (a.lq - q0[1] + 31) >> 5) : 0};
     const int nb = (a.lk + 127) / 128;
 
     if (threadIdx.x == 0) {
@@ -117,17 +121,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], readers);
         }
-        // softmax arrivals come only from warps that own a valid query row (a warp without one
-        // would run ahead and complete the next phase early)
-        for (int t = 0; t < 2; ++t) {
-            const uint32_t warps = active[t] ? uint32_t(min(4, (a.lq - q0[t] + 31) >> 5)) : 1u;
+        for (int t = 0; t < 2; ++t)
             for (int h = 0; h < 2; ++h) {
+                const uint32_t w = vw[t] > 0 ? uint32_t(vw[t]) : 1u;
                 mbar_init(&s_full[t * 2 + h], 1);
-                mbar_init(&s_free[t * 2 + h], warps);
-                mbar_init(&pv_done[t * 2 + h], 1);
+                mbar_init(&s_free[t * 2 + h], w);
+                mbar_init(&p_full[t * 2 + h], w);
+                mbar_init(&pv_done[(t * 2 + h) * 2 + 0], 1);
+                mbar_init(&pv_done[(t * 2 + h) * 2 + 1], 1);
             }
-            mbar_init(&p_full[t], warps);
-        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -154,10 +156,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int j = 0; j < nb; ++j) {
                 const int s = j % kFaStages;
                 const uint32_t ph = uint32_t(j / kFaStages) & 1u;
+                FA_WHERE(1000 + j);
                 if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutProducer)) break;
                 FA_STAMP(0, j);
                 mbar_arrive_expect_tx(&k_full[s], kFaTile);
                 tma_load_3d(smem + kFaK + s * kFaTile, &tmK, &k_full[s], kvh * 64, j * 128, seq);
+                FA_WHERE(2000 + j);
                 if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutProducer)) break;
                 FA_STAMP(1, j);
                 mbar_arrive_expect_tx(&v_full[s], kFaTile);
@@ -169,18 +173,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (lane == 0 && active[t]) {
             constexpr uint32_t idS = idesc_f16(CtTraits<CT>::kFmt, 128, 64);
             constexpr uint32_t idPV = idesc_f16(CtTraits<CT>::kFmt, 128, 64) | (1u << 16);  // B (V) MN-major
-            const uint32_t dS = tmem_base + uint32_t(t * 128), dO = tmem_base + 256u + uint32_t(t * 64);
+            const uint32_t dS = tmem_base + uint32_t(t * 128), dO = tmem_base + 256u + uint32_t(t * 128);
             const uint64_t qd = smem_desc_sw128(smem + kFaQ + t * kFaTile);
             bool ok = mbar_wait(q_full, 0, abort_flag, a.status, kErrTimeoutMma);
             // S halves of block j are issued before P V of block j - 1
             for (int j = 0; ok && j <= nb; ++j) {
                 if (j < nb) {
                     const int s = j % kFaStages;
+                    FA_WHERE(3000 + j);
                     if (!(ok = mbar_wait(&k_full[s], uint32_t(j / kFaStages) & 1u, abort_flag, a.status,
                                          kErrTimeoutMma)))
                         break;
                     const uint64_t kd = smem_desc_sw128(smem + kFaK + s * kFaTile);
                     for (int h = 0; h < 2; ++h) {
+                        FA_WHERE(4000 + 100 * h + j);
                         if (j > 0 && !(ok = mbar_wait(&s_free[t * 2 + h], uint32_t(j - 1) & 1u, abort_flag,
                                                       a.status, kErrTimeoutMma)))
                             break;
@@ -198,158 +204,169 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 }
                 if (j > 0) {
                     const int jj = j - 1, s = jj % kFaStages;
+                    FA_WHERE(5000 + jj);
                     if (!(ok = mbar_wait(&v_full[s], uint32_t(jj / kFaStages) & 1u, abort_flag, a.status,
                                          kErrTimeoutMma)))
                         break;
-                    if (!(ok = mbar_wait(&p_full[t], uint32_t(jj) & 1u, abort_flag, a.status, kErrTimeoutMma)))
-                        break;
-                    tc_fence_after();
-                    FA_STAMP(4 + t, jj);
-                    const uint8_t* pt = smem + kFaP + (t * 2 + (jj & 1)) * 2 * kFaTile;
                     const uint64_t vd = smem_desc_sw128(smem + kFaV + s * kFaTile);
+                    for (int h = 0; h < 2; ++h) {
+                        FA_WHERE(6000 + 100 * h + jj);
+                        if (!(ok = mbar_wait(&p_full[t * 2 + h], uint32_t(jj) & 1u, abort_flag, a.status,
+                                             kErrTimeoutMma)))
+                            break;
+                        tc_fence_after();
+                        if (h == 0) FA_STAMP(4 + t, jj);
+                        const uint64_t pd = smem_desc_sw128(smem + kFaP + ((t * 2 + (jj & 1)) * 2 + h) * kFaTile);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        // P: K-major, two 64-key panels; V: MN-major, 16 keys = 2 x 1024 B groups
-                        const uint64_t pd = smem_desc_sw128(pt + (k >> 2) * kFaTile) + uint64_t(2 * (k & 3));
-                        mma_f16_ss(dO, pd, vd + uint64_t(128 * k), idPV, (jj | k) != 0 ? 1u : 0u);
+                        for (int k = 0; k < 4; ++k)
+                            // P: K-major 64-key panel (+32 B per 16 keys); V: MN-major, keys 64h + 16k
+                            // start (64h + 16k) rows x 128 B in
+                            mma_f16_ss(dO + uint32_t(h * 64), pd + uint64_t(2 * k),
+                                       vd + uint64_t(h * (8192 >> 4) + 128 * k), idPV, (jj | k) != 0 ? 1u : 0u);
+                        mma_commit(&pv_done[(t * 2 + h) * 2 + (jj & 1)]);
                     }
-                    mma_commit(&pv_done[t * 2 + (jj & 1)]);
+                    if (!ok) break;
                     mma_commit(&v_empty[s]);
                 }
             }
         }
     } else {
-        const int t = (warp - 3) >> 2;  // query tile of this softmax group
-        const int wq = warp & 3;        // TMEM lane quarter this warp may access
+        const int u = warp - 3;
+        const int t = u >> 3;        // query tile
+        const int h = (u >> 2) & 1;  // key half of every block owned by this warp set
+        const int wq = warp & 3;     // TMEM lane quarter this warp may access
         const int row = wq * 32 + lane;
-        const bool warp_rows = q0[t] + wq * 32 < a.lq;  // warp-uniform: any valid query row
-        if (active[t] && warp_rows) {
+        if (active[t] && wq < vw[t]) {
             const uint32_t lane_off = uint32_t(wq * 32) << 16;
-            const uint32_t tS = tmem_base + lane_off + uint32_t(t * 128);
-            const uint32_t tO = tmem_base + lane_off + 256u + uint32_t(t * 64);
+            const uint32_t tS = tmem_base + lane_off + uint32_t(t * 128 + h * 64);
+            const uint32_t tO = tmem_base + lane_off + 256u + uint32_t(t * 128 + h * 64);
             const uint32_t sw = uint32_t(row & 7);
             const float sl = a.scale_log2;
-            float m_used = 0.f, l = 0.f;  // m_used is set by the first chunk of block 0
+            uint64_t* my_s_full = &s_full[t * 2 + h];
+            uint64_t* my_s_free = &s_free[t * 2 + h];
+            uint64_t* my_p_full = &p_full[t * 2 + h];
+            uint64_t* my_pv = &pv_done[(t * 2 + h) * 2];
+            float m_used = -INFINITY, l = 0.f;
+            bool first = true;  // warp-uniform: no valid key seen yet
             bool ok = true;
             for (int j = 0; j < nb && ok; ++j) {
-                const int nvalid = min(128, a.lk - j * 128);
-                const int nchunk = (nvalid + 31) >> 5;
-                uint8_t* prow = smem + kFaP + (t * 2 + (j & 1)) * 2 * kFaTile + row * 128;
+                const int kv = min(64, a.lk - j * 128 - h * 64);  // valid keys of this half (may be <= 0)
+                uint8_t* prow = smem + kFaP + ((t * 2 + (j & 1)) * 2 + h) * kFaTile + row * 128;
                 // this P buffer was last read by P V of block j - 2
+                FA_WHERE(7000 + j);
                 if (j >= 2) {
-                    ok = mbar_wait(&pv_done[t * 2 + (j & 1)], uint32_t((j >> 1) - 1) & 1u, abort_flag, a.status,
+                    ok = mbar_wait(&my_pv[j & 1], uint32_t((j >> 1) - 1) & 1u, abort_flag, a.status,
                                    kErrTimeoutEpilogue);
                     if (!ok) break;
                 }
-                float alpha_o = 1.f;  // factor this block applies to O (product of the chunk rescales)
-                bool need_o = false;
+                FA_WHERE(8000 + j);
+                ok = mbar_wait(my_s_full, uint32_t(j) & 1u, abort_flag, a.status, kErrTimeoutEpilogue);
+                if (!ok) break;
+                tc_fence_after();
+                if (wq == 0 && lane == 0) FA_STAMP(6 + 6 * h + t, j);
+                // max over this half's valid keys, scaled to log2 units (S reloaded from TMEM)
+                auto half_max = [&]() -> float {
+                    float mx[8];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    ok = mbar_wait(&s_full[t * 2 + h], uint32_t(j) & 1u, abort_flag, a.status, kErrTimeoutEpilogue);
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (h == 0 && wq == 0 && lane == 0) FA_STAMP(6 + t, j);
-                    float x[2][32];
-                    if (warp_rows) {
-                        if (2 * h < nchunk) tmem_ld_32x32b_x32(tS + uint32_t(64 * h), x[0]);
-                        if (2 * h + 1 < nchunk) tmem_ld_32x32b_x32(tS + uint32_t(64 * h + 32), x[1]);
+                    for (int e = 0; e < 8; ++e) mx[e] = -INFINITY;
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        if (c * 32 >= kv) break;
+                        float x[32];
+                        tmem_ld_32x32b_x32(tS + uint32_t(c * 32), x);
                         tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], c * 32 + i < kv ? x[i] : -INFINITY);
                     }
-                    // the half is in registers: the next block's scores may overwrite it
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s_free[t * 2 + h]);
-                    if (!warp_rows) continue;
+                    return fa_max8(mx) * sl;
+                };
+                // p = 2^(s * scale - m) for the 64 keys, stored as this row's P (8 x 16 B chunks,
+                // 128-byte swizzle); returns the row sum, and the largest p in pmax
+                auto exp_pass = [&](float m, float& pmax) -> float {
+                    float s8[8], p8[8];
 #pragma unroll
-                    for (int cc = 0; cc < 2; ++cc) {
-                        const int c = 2 * h + cc;
-                        float (&v)[32] = x[cc];
-                        if (c < nchunk) {
-                            if (j == 0 && c == 0) {
-                                // first chunk of the row: m = its max (chunk 0 of block 0 has a valid key)
-                                float amax = -INFINITY;
+                    for (int e = 0; e < 8; ++e) s8[e] = p8[e] = 0.f;
+                    const float neg_m = -m;
 #pragma unroll
-                                for (int i = 0; i < 32; ++i) {
-                                    v[i] = i < nvalid ? v[i] * sl : -INFINITY;
-                                    amax = fmaxf(amax, v[i]);
-                                }
-                                m_used = amax;
+                    for (int c = 0; c < 2; ++c) {
+                        float x[32];
+                        if (c * 32 < kv) {
+                            tmem_ld_32x32b_x32(tS + uint32_t(c * 32), x);
+                            tmem_ld_wait();
+                            if (kv == 64) {
 #pragma unroll
-                                for (int i = 0; i < 32; ++i) v[i] -= amax;
+                                for (int i = 0; i < 32; ++i) x[i] = ex2_approx(fmaf(x[i], sl, neg_m));
                             } else {
-                                // arguments of 2^(.) with the current running max; masked keys -> -inf
-                                float amax = -INFINITY;
-                                const float neg_m = -m_used;
-                                if (nvalid == 128) {
 #pragma unroll
-                                    for (int i = 0; i < 32; ++i) {
-                                        v[i] = fmaf(v[i], sl, neg_m);
-                                        amax = fmaxf(amax, v[i]);
-                                    }
-                                } else {
-#pragma unroll
-                                    for (int i = 0; i < 32; ++i) {
-                                        v[i] = c * 32 + i < nvalid ? fmaf(v[i], sl, neg_m) : -INFINITY;
-                                        amax = fmaxf(amax, v[i]);
-                                    }
-                                }
-                                const bool exceed = amax > kFaRescaleLog2;
-                                if (__any_sync(0xffffffffu, exceed)) {
-                                    // raise m to this chunk's max: shift the arguments, scale the row's sum,
-                                    // the P chunks already written for this block and (later) O
-                                    const float shift = exceed ? amax : 0.f;
-                                    const float f = ex2_approx(-shift);
-                                    m_used += shift;
-                                    l *= f;
-                                    alpha_o *= f;
-#pragma unroll
-                                    for (int i = 0; i < 32; ++i) v[i] -= shift;
-                                    if (exceed) {
-#pragma unroll
-                                        for (int cp = 0; cp < c; ++cp)
-#pragma unroll
-                                            for (int q = 0; q < 4; ++q) {
-                                                const uint32_t ch = uint32_t(cp * 4 + q);
-                                                fa_scale_chunk<CT>(prow + (ch >> 3) * kFaTile + (((ch & 7u) ^ sw) << 4), f);
-                                            }
-                                    }
-                                    need_o = true;
-                                }
+                                for (int i = 0; i < 32; ++i)
+                                    x[i] = c * 32 + i < kv ? ex2_approx(fmaf(x[i], sl, neg_m)) : 0.f;
                             }
-                            float s8[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) s8[e] = 0.f;
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                v[i] = ex2_approx(v[i]);
-                                s8[i & 7] += v[i];
-                            }
-                            l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
                         } else {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+                            for (int i = 0; i < 32; ++i) x[i] = 0.f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            s8[i & 7] += x[i];
+                            p8[i & 7] = fmaxf(p8[i & 7], x[i]);
                         }
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
                             uint4 pk;
-                            pk.x = CtTraits<CT>::pack2(v[8 * q + 0], v[8 * q + 1]);
-                            pk.y = CtTraits<CT>::pack2(v[8 * q + 2], v[8 * q + 3]);
-                            pk.z = CtTraits<CT>::pack2(v[8 * q + 4], v[8 * q + 5]);
-                            pk.w = CtTraits<CT>::pack2(v[8 * q + 6], v[8 * q + 7]);
-                            const uint32_t ch = uint32_t(c * 4 + q);  // 16-byte chunk of the 256-byte P row
-                            *reinterpret_cast<uint4*>(prow + (ch >> 3) * kFaTile + (((ch & 7u) ^ sw) << 4)) = pk;
+                            pk.x = CtTraits<CT>::pack2(x[8 * q + 0], x[8 * q + 1]);
+                            pk.y = CtTraits<CT>::pack2(x[8 * q + 2], x[8 * q + 3]);
+                            pk.z = CtTraits<CT>::pack2(x[8 * q + 4], x[8 * q + 5]);
+                            pk.w = CtTraits<CT>::pack2(x[8 * q + 6], x[8 * q + 7]);
+                            *reinterpret_cast<uint4*>(prow + ((uint32_t(c * 4 + q) ^ sw) << 4)) = pk;
                         }
                     }
-                    if (h == 0 && wq == 0 && lane == 0) FA_STAMP(8 + t, j);
+                    pmax = fa_max8(p8);
+                    return ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+                };
+                float f_o = 1.f;  // factor O needs before this block's P V (lazy max raised)
+                bool need_o = false;
+                if (kv > 0) {
+                    if (first) {  // first keys of the row: m = their max
+                        m_used = half_max();
+                        first = false;
+                    }
+                    float pmax;
+                    float sum = exp_pass(m_used, pmax);
+                    // a p above 2^8 (argument above 8, or +inf) flags a row whose max grew
+                    const bool exceed = pmax > 256.f;
+                    if (__any_sync(0xffffffffu, exceed)) {
+                        // raise m to this half's max, redo p (overwriting P), scale the row's sum
+                        // now and O before this block's P V
+                        const float hm = half_max();
+                        const float m_new = exceed ? hm : m_used;
+                        f_o = ex2_approx(m_used - m_new);
+                        m_used = m_new;
+                        l *= f_o;
+                        need_o = true;
+                        sum = exp_pass(m_used, pmax);
+                    }
+                    l += sum;
+                } else {
+#pragma unroll
+                    for (int ch = 0; ch < 8; ++ch)
+                        *reinterpret_cast<uint4*>(prow + ((uint32_t(ch) ^ sw) << 4)) = make_uint4(0u, 0u, 0u, 0u);
                 }
-                if (!ok) break;
-                if (warp_rows) fence_proxy_async_smem();
-                if (wq == 0 && lane == 0) FA_STAMP(10 + t, j);
-                // O holds the P V sums of blocks < j at the old max: scale it once P V of block j - 1 is in
-                if (j > 0 && warp_rows && __any_sync(0xffffffffu, need_o)) {
-                    ok = mbar_wait(&pv_done[t * 2 + ((j - 1) & 1)], uint32_t((j - 1) >> 1) & 1u, abort_flag, a.status,
+                // S half consumed: the next block's scores may overwrite it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(my_s_free);
+                fence_proxy_async_smem();
+                if (wq == 0 && lane == 0) FA_STAMP(8 + 6 * h + t, j);
+                // P V of block j - 1 must be complete before P of block j is announced: it proves the
+                // MMA warp consumed the previous announcement (an mbarrier phase must not be
+                // completed twice before its waiter looks), and O is only rescaled after it
+                if (j > 0) {
+                    ok = mbar_wait(&my_pv[(j - 1) & 1], uint32_t((j - 1) >> 1) & 1u, abort_flag, a.status,
                                    kErrTimeoutEpilogue);
                     if (!ok) break;
+                }
+                // O holds this half's P V sums of blocks < j at the old max
+                if (j > 0 && __any_sync(0xffffffffu, need_o)) {
                     tc_fence_after();
                     float o[32];
 #pragma unroll
@@ -357,51 +374,67 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                         tmem_ld_32x32b_x32(tO + uint32_t(c * 32), o);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= alpha_o;
+                        for (int i = 0; i < 32; ++i) o[i] *= f_o;
                         tmem_st_32x32b_x32(tO + uint32_t(c * 32), o);
                     }
                     tmem_st_wait();
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&p_full[t]);
-                if (wq == 0 && lane == 0) FA_STAMP(12 + t, j);
+                if (lane == 0) mbar_arrive(my_p_full);
+                if (wq == 0 && lane == 0) FA_STAMP(10 + 6 * h + t, j);
             }
-            // every warp of the group reaches the named barrier below exactly once, aborted or not
+            // every warp of the tile reaches both named barriers below exactly once, aborted or not
+            FA_WHERE(9000);
             if (ok)
-                ok = mbar_wait(&pv_done[t * 2 + ((nb - 1) & 1)], uint32_t((nb - 1) >> 1) & 1u, abort_flag, a.status,
+                ok = mbar_wait(&my_pv[(nb - 1) & 1], uint32_t((nb - 1) >> 1) & 1u, abort_flag, a.status,
                                kErrTimeoutEpilogue);
-            if (ok) {
+            // (m, l) of half 1 go through its own P panel of the last block, dead once its P V is done
+            float2* ml = reinterpret_cast<float2*>(smem + kFaP + ((t * 2 + ((nb - 1) & 1)) * 2 + 1) * kFaTile) + row;
+            if (h == 1) *ml = make_float2(m_used, l);
+            const uint32_t tile_threads = 64u * uint32_t(vw[t]);
+            if (*abort_flag == 0) FA_WHERE(9100);
+            named_bar_sync(1 + t, tile_threads);
+            if (*abort_flag == 0) FA_WHERE(9200);
+            if (ok && h == 0) {
                 tc_fence_after();
+                const float2 o1 = *ml;
+                const float m = fmaxf(m_used, o1.x);
+                const float f0 = ex2_approx(m_used - m), f1 = ex2_approx(o1.x - m);
+                const float inv = 1.f / (l * f0 + o1.y * f1);
+                const float g0 = f0 * inv, g1 = f1 * inv;
                 uint8_t* orow = smem + kFaQ + t * kFaTile + row * 128;  // Q tile is dead: stage O there
-                if (warp_rows) {
-                    const float inv = 1.f / l;
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        float o[32];
-                        tmem_ld_32x32b_x32(tO + uint32_t(c * 32), o);
-                        tmem_ld_wait();
+                for (int c = 0; c < 2; ++c) {
+                    float o0[32], o1v[32];
+                    tmem_ld_32x32b_x32(tO + uint32_t(c * 32), o0);
+                    tmem_ld_32x32b_x32(tO + 64u + uint32_t(c * 32), o1v);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            uint4 v;
-                            v.x = CtTraits<CT>::pack2(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
-                            v.y = CtTraits<CT>::pack2(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
-                            v.z = CtTraits<CT>::pack2(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
-                            v.w = CtTraits<CT>::pack2(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
-                            *reinterpret_cast<uint4*>(orow + ((uint32_t(c * 4 + q) ^ sw) << 4)) = v;
-                        }
+                    for (int q = 0; q < 4; ++q) {
+                        float r[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) r[e] = o0[8 * q + e] * g0 + o1v[8 * q + e] * g1;
+                        uint4 v;
+                        v.x = CtTraits<CT>::pack2(r[0], r[1]);
+                        v.y = CtTraits<CT>::pack2(r[2], r[3]);
+                        v.z = CtTraits<CT>::pack2(r[4], r[5]);
+                        v.w = CtTraits<CT>::pack2(r[6], r[7]);
+                        *reinterpret_cast<uint4*>(orow + ((uint32_t(c * 4 + q) ^ sw) << 4)) = v;
                     }
-                    fence_proxy_async_smem();
                 }
+                fence_proxy_async_smem();
             }
-            named_bar_sync(1 + t, 32u * uint32_t(min(4, (a.lq - q0[t] + 31) >> 5)));
-            if (wq == 0 && lane == 0 && *abort_flag == 0) {
+            named_bar_sync(1 + t, tile_threads);
+            if (*abort_flag == 0) FA_WHERE(9300);
+            if (h == 0 && wq == 0 && lane == 0 && *abort_flag == 0) {
                 tma_store_3d(&tmO, smem + kFaQ + t * kFaTile, head * 64, q0[t], seq);
                 bulk_commit_group();
                 bulk_wait_read_all();
             }
         }
     }
+    if (*abort_flag == 0) FA_WHERE(9900);
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -11,7 +11,10 @@
 namespace b2d {
 
 // ~2^24 polls of try_wait (each may suspend briefly) is several seconds.
-constexpr uint32_t kSpinLimit = 1u << 24;
+#ifndef B2D_SPIN_LIMIT
+#define B2D_SPIN_LIMIT (1u << 24)
+#endif
+constexpr uint32_t kSpinLimit = B2D_SPIN_LIMIT;
 
 enum DeviceError : int {
     kErrNone = 0,
