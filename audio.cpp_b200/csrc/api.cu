@@ -137,35 +137,41 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
 // 2-SM (cta_group::2) 256 x 256 pair tiles; B operands need a 128-row TMA box.
 int g_gemm_pair = -1;  // -1 automatic, 0 off, 1 forced (B2D_GEMM_PAIR)
 
-template <int EPI, typename CT>
-void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb128, int64_t M, int64_t N, int64_t K,
+template <int BN, int EPI, typename CT>
+void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb_half, int64_t M, int64_t N, int64_t K,
                         const EpiParams& ep, int num_sms, cudaStream_t st) {
+    using S = GemmPairShape<BN>;
     static bool configured = false;
     if (!configured) {
-        CK(cudaFuncSetAttribute(gemm_tc2_kernel<EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(GemmPairShape::SMEM_BYTES)));
+        CK(cudaFuncSetAttribute(gemm_tc2_kernel<BN, EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(S::SMEM_BYTES)));
         configured = true;
     }
-    const int64_t units = ((M + 255) / 256) * (N / 256);
+    const int64_t units = ((M + 255) / 256) * (N / BN);
     if (units == 0) return;
     const int64_t pairs = units < num_sms / 2 ? units : num_sms / 2;
-    gemm_tc2_kernel<EPI, CT><<<unsigned(2 * pairs), 192, GemmPairShape::SMEM_BYTES, st>>>(ta, tb128, int(M), int(N),
-                                                                                            int(K), ep);
+    gemm_tc2_kernel<BN, EPI, CT><<<unsigned(2 * pairs), 192, S::SMEM_BYTES, st>>>(ta, tb_half, int(M), int(N), int(K),
+                                                                                  ep);
     CK(cudaGetLastError());
 }
 
+// 2-SM pair tiles of 256 x bn (bn = 256 or 192); tb_half is B's tensor map with a bn / 2-row box.
 template <typename CT>
-void launch_gemm_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb128, int64_t M, int64_t N, int64_t K,
-                      const EpiParams& ep, int num_sms, cudaStream_t st) {
-    if (N % 256) fail(B2D_EINVAL, "pair GEMM N (%lld) must be a multiple of 256", (long long)N);
+void launch_gemm_pair(int epi, const CUtensorMap& ta, const CUtensorMap& tb_half, int64_t M, int64_t N, int64_t K,
+                      const EpiParams& ep, int num_sms, cudaStream_t st, int bn = 256) {
+    if (bn != 256 && bn != 192) fail(B2D_EINVAL, "pair GEMM tile width %d (256 or 192)", bn);
+    if (N % bn) fail(B2D_EINVAL, "pair GEMM N (%lld) must be a multiple of %d", (long long)N, bn);
     if (ep.splits > 1) fail(B2D_EINVAL, "pair GEMM has no split-K");
-    switch (epi) {
-        case EPI_F32: launch_gemm_pair_t<EPI_F32, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
-        case EPI_CT: launch_gemm_pair_t<EPI_CT, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
-        case EPI_SWIGLU: launch_gemm_pair_t<EPI_SWIGLU, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
-        case EPI_RESID: launch_gemm_pair_t<EPI_RESID, CT>(ta, tb128, M, N, K, ep, num_sms, st); break;
-        default: fail(B2D_EINVAL, "unsupported pair GEMM epilogue %d", epi);
+    if (bn == 192 && epi == EPI_SWIGLU) fail(B2D_EINVAL, "SwiGLU pair tiles are 256 wide");
+#define B2D_P(BNv, EPIv)                                                              \
+    if (bn == BNv && epi == EPIv) {                                                   \
+        launch_gemm_pair_t<BNv, EPIv, CT>(ta, tb_half, M, N, K, ep, num_sms, st);     \
+        return;                                                                       \
     }
+    B2D_P(256, EPI_F32) B2D_P(256, EPI_CT) B2D_P(256, EPI_SWIGLU) B2D_P(256, EPI_RESID)
+    B2D_P(192, EPI_F32) B2D_P(192, EPI_CT) B2D_P(192, EPI_RESID)
+#undef B2D_P
+    fail(B2D_EINVAL, "unsupported pair GEMM epilogue %d", epi);
 }
 
 template <typename CT>
@@ -840,9 +846,12 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
         if (m <= 0 || n <= 0 || k <= 0) fail(B2D_EINVAL, "GEMM dimensions must be positive");
         if (epilogue == EPI_SWIGLU && bn != 256 && bn != 512) fail(B2D_EINVAL, "SwiGLU epilogue needs 256-column tiles");
         if (epilogue == EPI_RESID ? !resid_dev : !out_dev) fail(B2D_EINVAL, "GEMM output is null");
-        const bool pair = bn == 512;  // 512 selects the 2-SM 256 x 256 pair-tile kernel
+        // 512 / 384 select the 2-SM pair-tile kernel with 256 x 256 / 256 x 192 tiles
+        const bool pair = bn == 512 || bn == 384;
+        const int pair_bn = bn / 2;
         const CUtensorMap ta = make_tmap(a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128);
-        const CUtensorMap tb = make_tmap(b_dev, bf16 != 0, uint64_t(n), uint64_t(k), pair ? 128u : uint32_t(bn));
+        const CUtensorMap tb =
+            make_tmap(b_dev, bf16 != 0, uint64_t(n), uint64_t(k), pair ? uint32_t(pair_bn / 2) : uint32_t(bn));
         EpiParams ep;
         ep.out = out_dev;
         ep.ldo = ldo;
@@ -855,9 +864,9 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         if (pair) {
             if (bf16)
-                launch_gemm_pair<__nv_bfloat16>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+                launch_gemm_pair<__nv_bfloat16>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st, pair_bn);
             else
-                launch_gemm_pair<__half>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
+                launch_gemm_pair<__half>(epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st, pair_bn);
         } else if (bf16) {
             launch_gemm<__nv_bfloat16>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
         } else {

@@ -22,6 +22,20 @@
 
 namespace b2d {
 
+// Optional per-k-block clock64 trace of CTA 0's first tile for profiling builds (-DB2D_GEMM_TRACE).
+#ifdef B2D_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[4 * 256];
+#define GEMM_STAMP(ev, i)                                                                       \
+    do {                                                                                        \
+        if (blockIdx.x == 0 && u == int(blockIdx.x) && (i) < 256) g_gemm_trace[(ev) * 256 + (i)] = clock64(); \
+    } while (0)
+#else
+#define GEMM_STAMP(ev, i) \
+    do {                  \
+    } while (0)
+#endif
+
+
 enum EpiKind : int {
     EPI_F32 = 0,     // out_f32[r, n] = acc + bias[n]
     EPI_CT = 1,      // out_ct[r, n]  = ct(acc + bias[n])
@@ -257,8 +271,14 @@ __global__ void __launch_bounds__(192, 1)
                 const int kb0 = (u / num_tiles) * k_blocks;
                 const int m0 = (tile % m_tiles) * BM;
                 const int n0 = (tile / m_tiles) * BN;
-                for (int kb = kb0; kb < kb0 + k_blocks; ++kb) {
+                // Each tile starts its K walk at its own offset: CTAs that share an A row block
+                // or a B column block then fetch different K slices at any moment instead of all
+                // hitting the same L2 lines (the accumulation order is fixed per tile).
+                const int rot = ((tile % m_tiles) * 5 + (tile / m_tiles) * 3) % k_blocks;
+                for (int i = 0; i < k_blocks; ++i) {
+                    const int kb = kb0 + (rot + i < k_blocks ? rot + i : rot + i - k_blocks);
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
+                    GEMM_STAMP(0, i);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
                     tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
@@ -284,6 +304,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, ep.status, kErrTimeoutMma)) goto done;
                     tc_fence_after();
+                    GEMM_STAMP(1, kb);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     const uint64_t adesc = smem_desc_sw128(sa);
                     const uint64_t bdesc = smem_desc_sw128(sa + S::A_BYTES);
@@ -323,7 +344,9 @@ __global__ void __launch_bounds__(192, 1)
             const int rbase = m0 + quarter * 32;
             const int rows_live = M - rbase < 32 ? M - rbase : 32;
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+            if (lane == 0) GEMM_STAMP(2, quarter);
             epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, out_f32, ep, stg, lane);
+            if (lane == 0) GEMM_STAMP(3, quarter);
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             acc ^= 1;
@@ -339,18 +362,20 @@ done:
     }
 }
 
-// 2-SM variant: a cluster of 2 CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2
-// (M = 256 split across the pair's TMEM, N = 256).  Each CTA loads its own 128 rows of A and
-// its own 128 rows (half) of B, so per SM the operand traffic per FLOP is 2/3 of the
-// single-CTA 128 x 256 tile.  The leader CTA (rank 0) issues the MMAs; TMA completion of
+// 2-SM variant: a cluster of 2 CTAs computes a 256 x BN tile (BN = 256 or 192) with
+// tcgen05.mma.cta_group::2 (M = 256 split across the pair's TMEM).  Each CTA loads its own 128
+// rows of A and its own BN / 2 rows (half) of B, so per SM the operand traffic per FLOP is 2/3
+// (BN 256) or 0.73 (BN 192) of the single-CTA 128 x BN tile -- these GEMMs are bounded by the
+// L2 -> SM operand stream, not by the tensor pipe.  The leader CTA (rank 0) issues the MMAs; TMA completion of
 // both halves is counted on the leader's full barrier; commits multicast to both CTAs'
 // empty / tmem-full barriers; both epilogues release the accumulator on the leader's
 // tmem-empty barrier.  No TMA multicast is used.
+template <int BN_>
 struct GemmPairShape {
     static constexpr int BM = 128;  // rows per CTA (256 per pair)
-    static constexpr int BN = 256;  // columns per pair tile (128 rows of B per CTA)
+    static constexpr int BN = BN_;  // columns per pair tile (BN / 2 rows of B per CTA): 192 or 256
     static constexpr int BK = 64;
-    static constexpr int STAGES = 6;
+    static constexpr int STAGES = BN == 256 ? 6 : 7;
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -358,11 +383,11 @@ struct GemmPairShape {
     static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + 4 * 32 * 33 * 4;
 };
 
-template <int EPI, typename CT>
+template <int BN_, int EPI, typename CT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                     int K, EpiParams ep) {
-    using S = GemmPairShape;
+    using S = GemmPairShape<BN_>;
     constexpr int BM = S::BM, BN = S::BN, BK = S::BK, STAGES = S::STAGES;
 
     extern __shared__ uint8_t smem_raw[];
@@ -415,7 +440,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             for (int u = cluster; u < num_units; u += nclusters) {
                 const int m0 = (u % pm) * 2 * BM + int(rank) * BM;
                 const int n0 = (u / pm) * BN + int(rank) * (BN / 2);
-                for (int kb = 0; kb < k_blocks; ++kb) {
+                const int rot = ((u % pm) * 5 + (u / pm) * 3) % k_blocks;  // staggered K walk (see above)
+                for (int i = 0; i < k_blocks; ++i) {
+                    const int kb = rot + i < k_blocks ? rot + i : rot + i - k_blocks;
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
                     if (leader) mbar_arrive_expect_tx(&full[stage], 2 * S::STAGE_BYTES);
                     const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);

@@ -213,8 +213,9 @@ enum {
 };
 
 /* A [M, K] and B [N, K] are device fp16 (bf16 = 0) or bf16 (bf16 = 1) matrices.
- * K % 64 == 0, N % bn == 0, bn in {64, 128, 192, 256} (SwiGLU: 256).  bias/gate/resid may be NULL
- * where unused. */
+ * K % 64 == 0.  bn in {64, 128, 192, 256} selects a single-SM 128 x bn tile (N % bn == 0);
+ * bn = 512 / 384 select the 2-SM pair tile 256 x 256 / 256 x 192 (N % 256 / N % 192 == 0).
+ * SwiGLU: bn 256 or 512.  bias/gate/resid may be NULL where unused. */
 B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
                     int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);

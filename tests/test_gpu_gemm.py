@@ -129,3 +129,34 @@ def test_pair_gemm_all_epilogues(ctx, bf16, m, n, k):
     idx_a = torch.cat([torch.arange(i, i + 128) for i in range(0, n, 256)]).cuda()
     want_sw = torch.nn.functional.silu(ref[:, idx_a]) * ref[:, idx_a + 128]
     assert float((sw.float() - want_sw).norm() / want_sw.norm()) < (1e-2 if bf16 else 3e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("m,n,k", [(2050, 1536, 1536), (300, 576, 1024), (129, 192, 64)])
+def test_pair192_gemm_epilogues(ctx, bf16, m, n, k):
+    """The 2-SM pair kernel with 256 x 192 tiles (96 B rows per CTA), selected with bn = 384."""
+    dt = torch.bfloat16 if bf16 else torch.float16
+    g = torch.Generator(device="cuda").manual_seed(m + n + k + 7)
+    a = torch.randn(m, k, device="cuda", generator=g).to(dt)
+    b = (torch.randn(n, k, device="cuda", generator=g) * 0.05).to(dt)
+    bias = torch.randn(n, device="cuda", generator=g)
+    ref = _ref(a, b, bias)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=0, bn=384, bias=bias.data_ptr(),
+             out=out.data_ptr(), ldo=n)
+    torch.cuda.synchronize()
+    assert float((out - ref).norm() / ref.norm()) < 1e-5
+    outc = torch.zeros(m, n, device="cuda", dtype=dt)
+    ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=1, bn=384, bias=bias.data_ptr(),
+             out=outc.data_ptr(), ldo=n)
+    torch.cuda.synchronize()
+    assert float((outc.float() - ref).norm() / ref.norm()) < (1e-2 if bf16 else 2e-3)
+    x0 = torch.randn(m, n, device="cuda", generator=g)
+    gate = torch.randn(m, n, device="cuda", generator=g)
+    x = x0.clone()
+    ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=3, bn=384, bias=bias.data_ptr(),
+             resid=x.data_ptr(), ldr=n, gate=gate.data_ptr(), ldg=n)
+    torch.cuda.synchronize()
+    want = x0 + gate * ref
+    assert float((x - want).norm() / want.norm()) < 1e-5
