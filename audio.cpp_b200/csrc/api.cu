@@ -130,7 +130,22 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
     const int64_t tiles = ((M + 127) / 128) * (N / BN) * splits;
     if (tiles == 0) return;
     const int grid = int(tiles < num_sms ? tiles : num_sms);
-    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, int(M), int(N), int(K), ep);
+    // fp32 output through TMA stores when the output is a plain [M, ldo] fp32 matrix
+    CUtensorMap to{};
+    EpiParams e = ep;
+    if (EPI == EPI_F32 && S::TMA_F32_OUT && splits == 1 && !ep.seg_rows && ep.out &&
+        reinterpret_cast<uintptr_t>(ep.out) % 16 == 0 && ep.ldo % 4 == 0 && ep.ldo >= N) {
+        const cuuint64_t dims[2] = {uint64_t(N), uint64_t(M)};
+        const cuuint64_t strides[1] = {uint64_t(ep.ldo) * 4};
+        const cuuint32_t box[2] = {32, 32};
+        const cuuint32_t estr[2] = {1, 1};
+        CUresult r = encode_fn()(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ep.out, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) fail(B2D_ECUDA, "cuTensorMapEncodeTiled (fp32 output) failed (%d)", int(r));
+        e.tma_out = 1;
+    }
+    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, to, int(M), int(N), int(K), e);
     CK(cudaGetLastError());
 }
 

@@ -27,7 +27,7 @@ namespace b2d {
 __device__ unsigned long long g_gemm_trace[4 * 256];
 #define GEMM_STAMP(ev, i)                                                                       \
     do {                                                                                        \
-        if (blockIdx.x == 0 && u == int(blockIdx.x) && (i) < 256) g_gemm_trace[(ev) * 256 + (i)] = clock64(); \
+        if (blockIdx.x == 0 && (i) < 256) g_gemm_trace[(ev) * 256 + (i)] = clock64();          \
     } while (0)
 #else
 #define GEMM_STAMP(ev, i) \
@@ -64,6 +64,9 @@ struct EpiParams {
     int rope_L = 0;
     int rope_cols = 0;
     const float* vmask = nullptr;
+    // EPI_F32 through TMA stores (the kernel's tmO map: fp32 [M rows][N cols], box 32 x 32, 128B
+    // swizzle); set by the launcher when there is no split-K and no row remap.
+    int tma_out = 0;
 };
 
 template <typename CT>
@@ -100,15 +103,58 @@ struct GemmShape {
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;  // power of two
-    static constexpr size_t EPI_STAGE_BYTES = 4 * 32 * 33 * 4;  // per-warp transpose buffers
-    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + EPI_STAGE_BYTES;
+    // Epilogue staging right after the operand ring (1024-aligned): per warp either a 32 x 33 fp32
+    // transpose buffer or, for the TMA-store fp32 path, two 128B-swizzled 32 x 32 fp32 boxes.
+    static constexpr bool TMA_F32_OUT = BN != 192;  // the two 4 KB boxes per warp fit next to the ring
+    static constexpr size_t EPI_STAGE_BYTES = TMA_F32_OUT ? 4 * 2 * 4096 : 4 * 32 * 33 * 4;
+    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + EPI_STAGE_BYTES + 256 + 1024;
 };
 
 // Drains one 128-row accumulator tile (this warp's 32 TMEM lanes at `tbase`) through the epilogue.
 template <int BN, int EPI, typename CT>
 __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int rbase, int rows_live, int n0, float* out_f32,
-                                              const EpiParams& ep, float* stg, int lane) {
+                                              const EpiParams& ep, float* stg, int lane,
+                                              const CUtensorMap* tmO = nullptr) {
     constexpr int CHUNKS = EPI == EPI_SWIGLU ? 4 : BN / 32;
+    if constexpr (EPI == EPI_F32 && GemmShape<BN>::TMA_F32_OUT) {
+        if (ep.tma_out) {
+            // thread = row: its 32 columns go into a 128B-swizzled 32 x 32 box (conflict-free
+            // 16 B stores), one lane writes the box with a single TMA store (rows >= M clipped);
+            // two boxes per warp so the next chunk fills one while the other drains.
+            uint8_t* box0 = reinterpret_cast<uint8_t*>(stg);
+            const uint32_t sw = uint32_t(lane & 7);
+#pragma unroll 1
+            for (int c = 0; c < CHUNKS; ++c) {
+                float v[32];
+                tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+                tmem_ld_wait();
+                if (ep.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + n0 + c * 32 + j);
+                }
+                uint8_t* box = box0 + (c & 1) * 4096;
+                // the store issued two chunks ago read this box
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    *reinterpret_cast<float4*>(box + lane * 128 + ((uint32_t(q) ^ sw) << 4)) =
+                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                                     reinterpret_cast<uint64_t>(tmO)),
+                                 "r"(smem_u32(box)), "r"(n0 + c * 32), "r"(rbase)
+                                 : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            }
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+            return;
+        }
+    }
 #pragma unroll 1
         for (int c = 0; c < CHUNKS; ++c) {
             float v[32];
@@ -212,8 +258,8 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int rbase, int row
 
 template <int BN, int EPI, typename CT>
 __global__ void __launch_bounds__(192, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                   int K, EpiParams ep) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiParams ep) {
     using S = GemmShape<BN>;
     constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -221,7 +267,7 @@ __global__ void __launch_bounds__(192, 1)
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES + S::EPI_STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -278,7 +324,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int i = 0; i < k_blocks; ++i) {
                     const int kb = kb0 + (rot + i < k_blocks ? rot + i : rot + i - k_blocks);
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
-                    GEMM_STAMP(0, i);
+                    GEMM_STAMP(0, (u / int(gridDim.x)) * k_blocks + i);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
                     tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
@@ -304,7 +350,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, ep.status, kErrTimeoutMma)) goto done;
                     tc_fence_after();
-                    GEMM_STAMP(1, kb);
+                    GEMM_STAMP(1, (u / int(gridDim.x)) * k_blocks + kb);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     const uint64_t adesc = smem_desc_sw128(sa);
                     const uint64_t bdesc = smem_desc_sw128(sa + S::A_BYTES);
@@ -331,7 +377,8 @@ __global__ void __launch_bounds__(192, 1)
         // instruction reads/writes one contiguous 32-column row segment (coalesced, and the
         // residual read-modify-write issues all 32 rows' loads before any store instead of serialising).
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
-        float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
+        float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES +
+                                              quarter * (S::EPI_STAGE_BYTES / 4));
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
@@ -344,9 +391,9 @@ __global__ void __launch_bounds__(192, 1)
             const int rbase = m0 + quarter * 32;
             const int rows_live = M - rbase < 32 ? M - rbase : 32;
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-            if (lane == 0) GEMM_STAMP(2, quarter);
-            epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, out_f32, ep, stg, lane);
-            if (lane == 0) GEMM_STAMP(3, quarter);
+            if (lane == 0 && quarter == 0) GEMM_STAMP(2, u / int(gridDim.x));
+            epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, out_f32, ep, stg, lane, &tmO);
+            if (lane == 0 && quarter == 0) GEMM_STAMP(3, u / int(gridDim.x));
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             acc ^= 1;
