@@ -203,6 +203,8 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     from oracle import synth
     cfg = synth.DIT_CONFIGS[DIT_WORKLOAD]
     cfg = synth.DitConfig(**{**cfg.__dict__, "prompt_seeds": (rank,)})
+    if args.dit_dpm_steps:  # profiling only: shorter schedules (the reported config says so)
+        cfg = synth.DitConfig(**{**cfg.__dict__, "steps": args.dit_dpm_steps})
     w = synth.dit_weights(cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
@@ -446,6 +448,8 @@ def main():
     ap.add_argument("--workload", default="all", choices=["all", "head", "dit"],
                     help="head = VibeVoice head (headline metric); dit = also/only time the Stable Audio DiT")
     ap.add_argument("--dit-steps", type=int, default=3, help="timed DiT sampling calls (each 100 DPM++ steps)")
+    ap.add_argument("--dit-dpm-steps", type=int, default=0,
+                    help="profiling only: DPM++ steps per DiT call instead of the workload's 100")
     ap.add_argument("--dit-warmup", type=int, default=1)
     args = ap.parse_args()
     if args.impl == "reference":
