@@ -98,6 +98,8 @@ HEAD_CONFIGS = {
     "vv15_f16_64": HeadConfig(wtype=F16, frames=64),
     "vv15_q8_1024": HeadConfig(wtype=Q8_0, frames=1024),
     "vv7_q8_8192": HeadConfig(hidden=3584, wtype=Q8_0, frames=8192),
+    # C5's 7B width (hidden 3584, F = 10752, adaLN N = 50176) at 32 frames and 3 steps: parity at that shape
+    "vv7_q8_32_3steps": HeadConfig(hidden=3584, wtype=Q8_0, frames=32, steps=3, wseed=7, cseed=8, xseed=9),
     # small parity configs
     "tiny_f16": HeadConfig(hidden=256, wtype=F16, frames=8),
     "tiny_q8": HeadConfig(hidden=256, wtype=Q8_0, frames=8),
@@ -190,6 +192,8 @@ DIT_CONFIGS = {
     # full-size parity cases (BASELINE C3/C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
     "sao_bf16_1x1024_2steps": DitConfig(steps=2),
     "sao_q8_1x1024_2steps": DitConfig(wtype=Q8_0, steps=2, prompt_seeds=(5,)),
+    # C4's batch (16 prompts + CFG = 32 sequences, Q8_0, full width and depth) at 64 latent frames, 2 steps
+    "sao_q8_16x64_2steps": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16)), latent_tokens=64, steps=2),
     "tiny_bf16": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,
                            prompt_max_length=14, latent_tokens=64, steps=6),
     "tiny_q8_b2_noapg": DitConfig(embed_dim=256, depth=2, num_heads=4, cond_token_dim=128, global_cond_dim=256,

@@ -34,7 +34,7 @@ def make_head(b2d, ctx, name):
 
 
 GOLDEN_HEADS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_frame_f16", "one_step_q8",
-                "vv15_f16_64", "vv15_q8_1024"]
+                "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps"]
 
 
 @pytest.mark.parametrize("name", GOLDEN_HEADS)
