@@ -188,8 +188,10 @@ typedef struct {
 B2D_API b2d_status b2d_dit_load(b2d_ctx* ctx, const b2d_dit_config* config, const b2d_tensor_view* tensors,
                                 int32_t n_tensors);
 
-/* The whole sampling loop (Graph::sample_dpmpp_2m, rf_dit.cpp:798-883, with the in-graph CFG/APG of
- * build_cfg_model_output, :988-1028) as one captured CUDA graph.  Host buffers; returns latents
+/* The whole sampling loop as one captured CUDA graph: Graph::sample_dpmpp_2m (rf_dit.cpp:798-883),
+ * sample_dpmpp_3m_sde (:680-796, Philox noise generated on the device in the TensorIterator layout,
+ * *rng_offset_blocks advanced as the reference does) or sample_v_ddim (:514-604, on request->schedule),
+ * each with the in-graph CFG/APG of build_cfg_model_output (:988-1028).  Host buffers; returns latents
  * [batch, 64, latent_tokens] (BCT) in out_latents.  Replaces FoundationRfDitRuntime::sample. */
 B2D_API b2d_status b2d_dit_sample(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents, void* stream);
 
