@@ -507,6 +507,20 @@ HeadWorkspace& head_workspace(b2d_ctx* ctx, HeadModel& m, int64_t batch) {
 
 // One evaluation of the head on ws.noisy / ws.cp (cond_proj already applied) with
 // the time embedding row temb_row -> ws.v.  diffusion_head.cpp:495-523.
+// RMSNorm + modulate of R rows: the warp-per-row kernel up to H = 4096, the CTA-per-row one above.
+template <typename CT>
+void launch_rms_modulate(const float* x, int64_t ldx, const float* w, const float* shift, const float* scale,
+                         int64_t ldm, float eps, int64_t H, int64_t R, CT* out, int64_t ldo, cudaStream_t st) {
+    const unsigned grid = unsigned((R + 7) / 8);
+    if (H <= 2048)
+        rms_modulate_warp_kernel<CT, 16><<<grid, 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), R, out, ldo);
+    else if (H <= 4096)
+        rms_modulate_warp_kernel<CT, 32><<<grid, 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), R, out, ldo);
+    else
+        rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), out, ldo);
+    CK(cudaGetLastError());
+}
+
 template <typename CT>
 void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, cudaStream_t st) {
     const int64_t R = 2 * ws.batch, H = m.H, F = m.F, L = m.cfg.head_layers;
@@ -531,10 +545,8 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
     const float* ada = ws.ada.as<float>();
     for (int64_t l = 0; l < L; ++l) {
         const float* shift = ada + 3 * H * l;
-        rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(ws.x.as<float>(), H, m.norms.as<float>() + l * H,
-                                                                  shift, shift + H, m.NADA, m.cfg.rms_norm_eps,
-                                                                  int(H), ws.h.as<CT>(), H);
-        CK(cudaGetLastError());
+        launch_rms_modulate<CT>(ws.x.as<float>(), H, m.norms.as<float>() + l * H, shift, shift + H, m.NADA,
+                                m.cfg.rms_norm_eps, H, R, ws.h.as<CT>(), H, st);
         ep = EpiParams{};
         ep.status = status;
         ep.out = ws.ffn.p;
@@ -556,9 +568,8 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
             launch_gemm<CT>(256, EPI_RESID, ws.tm_ffn, m.tm_down256[size_t(l)], R, H, F, ep, sms, st);
     }
     const float* fshift = ada + 3 * H * L;
-    rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(ws.x.as<float>(), H, nullptr, fshift, fshift + H,
-                                                              m.NADA, m.cfg.rms_norm_eps, int(H), ws.h.as<CT>(), H);
-    CK(cudaGetLastError());
+    launch_rms_modulate<CT>(ws.x.as<float>(), H, nullptr, fshift, fshift + H, m.NADA, m.cfg.rms_norm_eps, H, R,
+                            ws.h.as<CT>(), H, st);
     ep = EpiParams{};
     ep.status = status;
     ep.out = ws.vpart.p;

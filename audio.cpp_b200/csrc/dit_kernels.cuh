@@ -67,6 +67,53 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const float* __restrict_
     }
 }
 
+// Same LayerNorm, one warp per row with the row in registers and shuffle-only reductions
+// (d <= 128 * MAXV); 8 rows per 256-thread CTA.
+template <typename CT, int MAXV>
+__global__ void __launch_bounds__(256) layernorm_warp_kernel(const float* __restrict__ x, int d, int64_t rows,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ beta, float eps,
+                                                             CT* __restrict__ out) {
+    const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int n4 = d / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * d);
+    float4 v[MAXV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        v[i] = idx < n4 ? x4[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
+    const float mean = warp_sum(s) / float(d);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        if (lane + 32 * i < n4) {
+            const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, e = v[i].w - mean;
+            q += a * a + b * b + c * c + e * e;
+        }
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / float(d) + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const float4* b4 = reinterpret_cast<const float4*>(beta);
+    uint2* o2 = reinterpret_cast<uint2*>(out + row * d);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < n4) {
+            const float4 gg = __ldg(g4 + idx), bb = __ldg(b4 + idx);
+            const float a = (v[i].x - mean) * rstd * gg.x + bb.x;
+            const float b = (v[i].y - mean) * rstd * gg.y + bb.y;
+            const float c = (v[i].z - mean) * rstd * gg.z + bb.z;
+            const float e = (v[i].w - mean) * rstd * gg.w + bb.w;
+            o2[idx] = make_uint2(CtTraits<CT>::pack2(a, b), CtTraits<CT>::pack2(c, e));
+        }
+    }
+}
+
 // Global-token rows: h[seq, 0, :] = gpre[seq, :] + temb[step, seq % B, :]   (rf_dit.cpp:545-552);
 // temb holds one row per (step, prompt) since v-DDIM gives every prompt its own timestep.
 __global__ void dit_global_row_kernel(float* __restrict__ h, int64_t seq_rows, const float* __restrict__ gpre,

@@ -122,6 +122,47 @@ __global__ void __launch_bounds__(THREADS) rms_modulate_kernel(const float* __re
     }
 }
 
+// Same computation, one warp per row with the row held in registers (x read once, reductions by
+// shuffles only): rows of H <= 128 * MAXV floats; 8 rows per 256-thread CTA.
+template <typename CT, int MAXV>
+__global__ void __launch_bounds__(256) rms_modulate_warp_kernel(const float* __restrict__ x, int64_t ldx,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ shift,
+                                                                const float* __restrict__ scale, int64_t ldm, float eps,
+                                                                int H, int64_t rows, CT* __restrict__ out, int64_t ldo) {
+    const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int n4 = H / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * ldx);
+    float4 v[MAXV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        v[i] = idx < n4 ? x4[idx] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / float(H) + eps);
+    const float4* s4 = reinterpret_cast<const float4*>(shift + row * ldm);
+    const float4* c4 = reinterpret_cast<const float4*>(scale + row * ldm);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    uint2* o2 = reinterpret_cast<uint2*>(out + row * ldo);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < n4) {
+            const float4 sh = s4[idx], sc = c4[idx];
+            const float4 ww = w ? __ldg(w4 + idx) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float a = v[i].x * inv * ww.x * (1.f + sc.x) + sh.x;
+            const float b = v[i].y * inv * ww.y * (1.f + sc.y) + sh.y;
+            const float c = v[i].z * inv * ww.z * (1.f + sc.z) + sh.z;
+            const float d = v[i].w * inv * ww.w * (1.f + sc.w) + sh.w;
+            o2[idx] = make_uint2(CtTraits<CT>::pack2(a, b), CtTraits<CT>::pack2(c, d));
+        }
+    }
+}
+
 // sc[r, :] = ct(silu(cp[r, :] + temb[:]))   (SiluModule on c = cond_proj + t_emb)
 template <typename CT>
 __global__ void silu_cond_kernel(const float* __restrict__ cp, const float* __restrict__ temb, int64_t rows, int H,
