@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn"]
+            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout"]
 
 
 class B2DError(RuntimeError):
@@ -100,6 +100,7 @@ def lib() -> C.CDLL:
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
         L.b2d_attention.argtypes = [P, I32, P, I64, I64, P, P, I64, I64, P, I64, I64, I32, I32, I32, I32, I32, P]
+        L.b2d_selftest_wait_timeout.argtypes = [P, C.c_uint32, P]
         L.b2d_torch_randn.argtypes = [P, I32, C.c_uint64, C.c_uint64, I64, I64, I64, I32, P, P]
         L.b2d_dit_load.argtypes = [P, C.POINTER(DitConfig), C.POINTER(TensorView), I32]
         L.b2d_dit_sample.argtypes = [P, C.POINTER(DitRequest), P, P]
@@ -164,6 +165,10 @@ class Context:
     def q8_0_dequantize(self, q8_dev: int, rows: int, k: int, out_dev: int, stream: int = 0) -> None:
         self.check(lib().b2d_q8_0_dequantize(self._h, C.c_void_p(q8_dev), rows, k, C.c_void_p(out_dev),
                                              C.c_void_p(stream)))
+
+    def selftest_wait_timeout(self, polls: int, stream: int = 0) -> None:
+        """Runs a kernel whose bounded wait must expire; raises B2DError(B2D_ETIMEOUT)."""
+        self.check(lib().b2d_selftest_wait_timeout(self._h, polls, C.c_void_p(stream)))
 
     def torch_randn(self, out_dev: int, count: int, seed: int, offset: int = 0, layout: int = 0, sms: int = 1,
                     max_threads: int = 256, bf16: bool = False, stream: int = 0) -> None:

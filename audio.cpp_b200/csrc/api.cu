@@ -772,6 +772,33 @@ void b2d_destroy(b2d_ctx* ctx) {
 
 const char* b2d_last_error(const b2d_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
 
+namespace {
+// One thread waits on an mbarrier that nothing ever arrives on, through the same bounded wait the
+// kernels use (with `polls` as its limit instead of kSpinLimit): the wait gives up, records the
+// timeout code in the status word and the kernel returns.
+__global__ void selftest_wait_kernel(uint32_t polls, int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, kErrTimeoutMma, polls);
+}
+}  // namespace
+
+b2d_status b2d_selftest_wait_timeout(b2d_ctx* ctx, uint32_t polls, void* stream) {
+    return guarded(ctx, [&] {
+        if (polls == 0 || polls > (1u << 24)) fail(B2D_EINVAL, "polls must be in [1, 2^24]");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        selftest_wait_kernel<<<1, 32, 0, st>>>(polls, ctx->status.as<int>());
+        CK(cudaGetLastError());
+        check_status_word(ctx, st);
+    });
+}
+
 b2d_status b2d_sync(b2d_ctx* ctx, void* stream) {
     return guarded(ctx, [&] { check_status_word(ctx, static_cast<cudaStream_t>(stream)); });
 }

@@ -60,8 +60,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase with the given parity; on timeout or when another role
 // already aborted (*abort != 0) it records `code` and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
-                                          int code) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+                                          int code, uint32_t limit = kSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 1023u) == 1023u && *abort) return false;
     }

@@ -240,6 +240,13 @@ B2D_API b2d_status b2d_attention(b2d_ctx* ctx, int32_t bf16, const void* q, int6
                                  int64_t o_row, int64_t o_seq, int32_t lq, int32_t lk, int32_t heads, int32_t kv_rep,
                                  int32_t nseq, void* stream);
 
+/* ------------------------------------------------------------- diagnostics */
+/* Failure-path self-test: launches one kernel whose bounded device-side wait (the same wait every
+ * kernel of the library uses, with `polls` in [1, 2^24] as its limit) can never succeed, so it gives up
+ * and the call returns B2D_ETIMEOUT with its message.  No GPU fault is involved: the context, its
+ * stream and its status word stay usable for the next call.  No counterpart in the reference. */
+B2D_API b2d_status b2d_selftest_wait_timeout(b2d_ctx* ctx, uint32_t polls, void* stream);
+
 /* ------------------------------------------------- allocation-free variant */
 /* No counterpart in the reference: an addition for callers that cannot
  * allocate device memory -- hosts that only pass the library buffers they
