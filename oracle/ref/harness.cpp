@@ -11,6 +11,7 @@
 //   vvpredict <weights> <in> <out> <thr>   one VibeVoiceDiffusionHeadWeightsRuntime::predict
 //   vv <weights> <in> <out> <thr> <reps>   sample_vibevoice_speech_latents (whole step loop)
 //   dit <weights> <in> <out> <thr> <reps> FoundationRfDitRuntime::sample
+//   sa3 <weights> <in> <out> <thr> <reps> StableAudioRfDitRuntime::sample (Stable Audio 3 DiT)
 //
 // Reference entry points exercised (paths inside audio.cpp):
 //   include/engine/models/vibevoice/diffusion_sampler.h:23  sample_vibevoice_speech_latents
@@ -23,6 +24,7 @@
 #include "engine/framework/core/execution_context.h"
 #include "engine/framework/sampling/torch_random.h"
 #include "engine/models/stable_audio/foundation/rf_dit.h"
+#include "engine/models/stable_audio/rf_dit.h"
 #include "engine/models/vibevoice/diffusion_head.h"
 #include "engine/models/vibevoice/diffusion_sampler.h"
 #include "engine/models/vibevoice/scheduler.h"
@@ -401,6 +403,87 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     return 0;
 }
 
+// ------------------------------------------------------ Stable Audio 3 DiT
+// StableAudioRfDitRuntime::sample (src/models/stable_audio/rf_dit.cpp:586-694): rectified-flow DiT with
+// memory tokens, local-add conditioning, qk-RMSNorm, optional differential attention, 6-way adaLN,
+// APG-CFG when cfg_scale != 1, and the pingpong (Philox noise) or euler sampler on sampling.schedule.
+int cmd_sa3(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+    namespace sa = engine::models::stable_audio;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<sa::StableAudioAssets>();
+    auto & c = assets->config;
+    c.io_channels = i64_scalar(in, "io_channels");
+    c.embed_dim = i64_scalar(in, "embed_dim");
+    c.depth = i64_scalar(in, "depth");
+    c.num_heads = i64_scalar(in, "num_heads");
+    c.cond_dim = i64_scalar(in, "cond_dim");
+    c.cond_token_dim = c.cond_dim;
+    c.global_cond_dim = i64_scalar(in, "global_cond_dim");
+    c.local_add_cond_dim = i64_scalar(in, "local_add_cond_dim");
+    c.num_memory_tokens = i64_scalar(in, "num_memory_tokens");
+    c.differential_attention = i64_scalar(in, "differential") != 0;
+    c.prompt_max_length = i64_scalar(in, "prompt_max_length");
+    c.stable_audio_open_v1 = false;
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
+
+    const int64_t batch = i64_scalar(in, "batch");
+    const int64_t tokens = i64_scalar(in, "latent_tokens");
+    const int64_t steps = i64_scalar(in, "steps");
+    sa::StableAudioSamplingState sampling;
+    sampling.batch = batch;
+    sampling.latent_sample_size = tokens;
+    sampling.channels = c.io_channels;
+    sampling.schedule_points = steps + 1;
+    sampling.schedule = f32s(in, "schedule");
+    sampling.padding_mask = f32s(in, "padding_mask");
+    sampling.noise = f32s(in, "noise");
+    sampling.local_add_conditioning = f32s(in, "local_add");
+
+    sa::StableAudioConditioningInputs cond;
+    const int64_t cross_tokens = c.prompt_max_length + 1;
+    cond.positive.batch = batch;
+    cond.positive.cross_tokens = cross_tokens;
+    cond.positive.cond_dim = c.cond_dim;
+    cond.positive.cross_attention = f32s(in, "cross_positive");
+    cond.positive.global = f32s(in, "global");
+    cond.has_negative = i64_scalar(in, "has_negative") != 0;
+    if (cond.has_negative) {
+        cond.negative = cond.positive;
+        cond.negative.cross_attention = f32s(in, "cross_negative");
+        const auto m = f32s(in, "negative_mask");
+        cond.negative.cross_attention_mask.assign(m.size(), 0);
+        for (size_t i = 0; i < m.size(); ++i) cond.negative.cross_attention_mask[i] = m[i] != 0.0F ? 1 : 0;
+    }
+    const float cfg_scale = f32_scalar(in, "cfg_scale");
+    const float apg_scale = f32_scalar(in, "apg_scale");
+    // sampler: 0 "pingpong", 1 "euler"
+    const char * sampler_name = i64_scalar(in, "sampler") == 1 ? "euler" : "pingpong";
+    const uint64_t seed = static_cast<uint64_t>(i64_scalar(in, "seed"));
+
+    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    sa::StableAudioRfDitRuntime dit(exec, assets, engine::assets::TensorStorageType::Native);
+    engine::sampling::TorchCudaSamplingPolicy policy;
+    policy.multiprocessor_count = i64_scalar(in, "rng_sms");
+    policy.max_threads_per_multiprocessor = i64_scalar(in, "rng_max_threads");
+    std::vector<float> times, result;
+    uint64_t final_offset = 0;
+    dit.prepare(sampling, cfg_scale);
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        uint64_t offset = static_cast<uint64_t>(i64_scalar(in, "rng_offset"));
+        const double t0 = now_ms();
+        result = dit.sample(sampling, cond, seed, offset, policy, sampler_name, cfg_scale, apg_scale);
+        times.push_back(static_cast<float>(now_ms() - t0));
+        final_offset = offset;
+    }
+    Bundle out;
+    const int64_t fo = static_cast<int64_t>(final_offset);
+    out["rng_offset_out"] = raw_entry(I64, &fo, 8, {1});
+    out["latents"] = f32_entry(result, {batch, c.io_channels, tokens});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
 // ------------------------------------------------------------- Philox randn
 // torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
 int cmd_randn(const std::string & in_path, const std::string & out_path) {
@@ -477,6 +560,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vvpredict") return cmd_vvpredict(arg(2), arg(3), arg(4), std::stoi(arg(5)));
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         std::fprintf(stderr, "unknown command %s\n", cmd.c_str());
         return 2;
     } catch (const std::exception & e) {

@@ -290,3 +290,148 @@ def dit_inputs(cfg: DitConfig) -> Dict[str, B.Tensor]:
     sched[:, 0], sched[:, -1] = 1.0, 0.0
     d["schedule"] = B.f32(sched)
     return d
+
+
+# ------------------------------------------------------------------ Stable Audio 3 DiT
+@dataclass
+class Sa3Config:
+    """StableAudioConfig fields of the SA3 rectified-flow DiT (include/engine/models/stable_audio/assets.h:14-84)
+    plus the sampling request (StableAudioRfDitRuntime::sample, src/models/stable_audio/rf_dit.cpp:586-694)."""
+    embed_dim: int = 256
+    depth: int = 2
+    num_heads: int = 4
+    cond_dim: int = 128
+    global_cond_dim: int = 64
+    local_add_cond_dim: int = 32
+    num_memory_tokens: int = 4
+    differential: bool = False
+    io_channels: int = 64
+    prompt_max_length: int = 14       # cross tokens = prompt_max_length + 1
+    latent_tokens: int = 40
+    batch: int = 1
+    steps: int = 4
+    cfg: float = 7.0
+    apg: float = 1.0
+    sampler: str = "pingpong"         # "pingpong" (Philox noise each step) or "euler"
+    wtype: str = F32
+    wseed: int = 3
+    prompt_seeds: tuple = field(default_factory=lambda: (0,))
+    seed: int = 7
+    rng_sms: int = 148
+    rng_max_threads: int = 2048
+    ragged_mask: bool = False
+
+    @property
+    def head_dim(self) -> int:
+        return self.embed_dim // self.num_heads
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        d = {k: B.i64(getattr(self, k)) for k in (
+            "io_channels", "embed_dim", "depth", "num_heads", "cond_dim", "global_cond_dim", "local_add_cond_dim",
+            "num_memory_tokens", "prompt_max_length", "latent_tokens", "batch", "steps", "seed", "rng_sms",
+            "rng_max_threads")}
+        d["differential"] = B.i64(int(self.differential))
+        d["sampler"] = B.i64({"pingpong": 0, "euler": 1}[self.sampler])
+        d["cfg_scale"] = B.f32(self.cfg)
+        d["apg_scale"] = B.f32(self.apg)
+        d["rng_offset"] = B.i64(0)
+        return d
+
+
+SA3_CONFIGS = {
+    "sa3_tiny_f32": Sa3Config(),
+    "sa3_tiny_f32_diff_b2": Sa3Config(differential=True, batch=2, prompt_seeds=(1, 2), ragged_mask=True),
+    "sa3_tiny_f32_euler_nocfg": Sa3Config(sampler="euler", cfg=1.0, prompt_seeds=(3,)),
+    "sa3_tiny_bf16_diff": Sa3Config(differential=True, wtype=BF16, prompt_seeds=(4,), steps=5),
+}
+
+SP = "model.model."
+
+
+def sa3_weights(cfg: Sa3Config) -> Dict[str, B.Tensor]:
+    """Tensor names and shapes of load_stable_audio_rf_dit_weights (rf_dit.cpp:386-585)."""
+    rng = np.random.default_rng(cfg.wseed)
+    d, C, hd = cfg.embed_dim, cfg.io_channels, cfg.head_dim
+    w: Dict[str, B.Tensor] = {}
+
+    def lin(name, out, inp, bias=False, conv=False, std=0.02):
+        shape = (out, inp, 1) if conv else (out, inp)
+        wtype = F32 if (conv and cfg.wtype == Q8_0) else cfg.wtype
+        w[SP + name + ".weight"] = encode_weight(_normal(rng, shape, std), wtype)
+        if bias:
+            w[SP + name + ".bias"] = B.f32(_normal(rng, (out,), 0.02))
+
+    def vec(name, n, base=0.0, std=0.02):
+        w[SP + name] = B.f32(base + _normal(rng, (n,), std))
+
+    lin("to_cond_embed.0", d, cfg.cond_dim)
+    lin("to_cond_embed.2", d, d)
+    lin("to_global_embed.0", d, cfg.global_cond_dim)
+    lin("to_global_embed.2", d, d)
+    lin("to_timestep_embed.0", d, 256, bias=True)
+    lin("to_timestep_embed.2", d, d, bias=True)
+    lin("preprocess_conv", C, C, conv=True)
+    lin("postprocess_conv", C, C, conv=True)
+    lin("transformer.project_in", d, C)
+    lin("transformer.project_out", C, d)
+    w[SP + "transformer.memory_tokens"] = B.f32(_normal(rng, (cfg.num_memory_tokens, d)))
+    lin("transformer.global_cond_embedder.0", d, d, bias=True)
+    lin("transformer.global_cond_embedder.2", 6 * d, d, bias=True)
+    for i in range(cfg.depth):
+        p = "transformer.layers.%d." % i
+        for n in ("pre_norm", "cross_attend_norm", "ff_norm"):
+            vec(p + n + ".gamma", d, 1.0)
+        lin(p + "self_attn.to_qkv", d * (5 if cfg.differential else 3), d)
+        lin(p + "self_attn.to_out", d, d)
+        lin(p + "cross_attn.to_q", d * (2 if cfg.differential else 1), d)
+        lin(p + "cross_attn.to_kv", d * (3 if cfg.differential else 2), d)
+        lin(p + "cross_attn.to_out", d, d)
+        for a in ("self_attn", "cross_attn"):
+            vec(p + a + ".q_norm.gamma", hd, 1.0, 0.1)
+            vec(p + a + ".k_norm.gamma", hd, 1.0, 0.1)
+        lin(p + "ff.ff.0.proj", 8 * d, d, bias=True)
+        lin(p + "ff.ff.2", d, 4 * d, bias=True)
+        lin(p + "to_local_embed.0", d, cfg.local_add_cond_dim, bias=True)
+        lin(p + "to_local_embed.2", d, d, bias=True)
+        vec(p + "to_scale_shift_gate", 6 * d, 0.0, 0.1)
+    return w
+
+
+def sa3_inputs(cfg: Sa3Config) -> Dict[str, B.Tensor]:
+    """Per prompt: noise [64, T], T5-like states [P + 1, cond_dim], global [global_cond_dim], local-add
+    features [T, local_add_cond_dim]; the negative prompt keeps every other token (its mask) and zeros the rest;
+    the rectified-flow schedule runs 1 -> 0 with a per-prompt warp."""
+    Bn, T, C = cfg.batch, cfg.latent_tokens, cfg.io_channels
+    P1 = cfg.prompt_max_length + 1
+    noise = np.zeros((Bn, C, T), np.float32)
+    cross = np.zeros((Bn, P1, cfg.cond_dim), np.float32)
+    cneg = np.zeros_like(cross)
+    glob = np.zeros((Bn, cfg.global_cond_dim), np.float32)
+    local = np.zeros((Bn, T, cfg.local_add_cond_dim), np.float32)
+    for b, s in enumerate(cfg.prompt_seeds[:Bn]):
+        rng = np.random.default_rng(2000 + s)
+        noise[b] = _normal(rng, (C, T))
+        cross[b] = _normal(rng, (P1, cfg.cond_dim))
+        cneg[b] = _normal(rng, (P1, cfg.cond_dim))
+        glob[b] = _normal(rng, (cfg.global_cond_dim,))
+        local[b] = _normal(rng, (T, cfg.local_add_cond_dim))
+    nmask = np.zeros((Bn, P1), np.float32)
+    nmask[:, ::2] = 1.0
+    d = cfg.scalars()
+    d["noise"] = B.f32(noise)
+    d["cross_positive"] = B.f32(cross)
+    d["cross_negative"] = B.f32(cneg)
+    d["negative_mask"] = B.f32(nmask)
+    d["has_negative"] = B.i64(1)
+    d["global"] = B.f32(glob)
+    d["local_add"] = B.f32(local)
+    mask = np.ones((Bn, T), np.float32)
+    if cfg.ragged_mask:
+        for b in range(Bn):
+            mask[b, T - 5 * (b + 1):] = 0.0
+    d["padding_mask"] = B.f32(mask)
+    lin = np.linspace(1.0, 0.0, cfg.steps + 1, dtype=np.float64)
+    sched = np.stack([lin ** (1.0 + 0.3 * b) for b in range(Bn)]).astype(np.float32)
+    sched[:, 0], sched[:, -1] = 1.0, 0.0
+    d["schedule"] = B.f32(sched)
+    return d

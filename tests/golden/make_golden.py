@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import dit, ref_runner, synth, vibevoice  # noqa: E402
+from oracle import dit, ref_runner, sa3, synth, vibevoice  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -32,6 +32,7 @@ HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_fram
                 "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps"]
 DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vddim", "tiny_f16_3msde",
                "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps"]
+SA3_GOLDENS = list(synth.SA3_CONFIGS)
 
 
 def digest(*bundles) -> np.ndarray:
@@ -100,8 +101,21 @@ def dit_golden(name: str) -> None:
     print("dit", name, "ok", out["latents"].dims)
 
 
+def sa3_golden(name: str) -> None:
+    """Stable Audio 3 DiT (StableAudioRfDitRuntime::sample) on a tiny seeded configuration."""
+    cfg = synth.SA3_CONFIGS[name]
+    w, inp = synth.sa3_weights(cfg), synth.sa3_inputs(cfg)
+    out = ref_runner.run("sa3", inp, w)
+    exact = sa3.sample(sa3.Sa3Dit(w, cfg, act="exact"), cfg, inp)
+    B.write(os.path.join(HERE, "%s.b2db" % name),
+            {"latents": out["latents"], "exact_latents": B.f32(exact), "rng_offset_out": out["rng_offset_out"],
+             "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("sa3", name, "ok", out["latents"].dims)
+
+
 def main(argv) -> None:
-    names = argv or ["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS]
+    names = argv or (["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS] +
+                     ["sa3:" + n for n in SA3_GOLDENS])
     for n in names:
         if n == "q8":
             q8_golden()
@@ -111,6 +125,8 @@ def main(argv) -> None:
             head_golden(n[5:])
         elif n.startswith("dit:"):
             dit_golden(n[4:])
+        elif n.startswith("sa3:"):
+            sa3_golden(n[4:])
         else:
             raise SystemExit("unknown fixture " + n)
 
