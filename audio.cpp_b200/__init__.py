@@ -29,7 +29,8 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout"]
+            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
+            "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device"]
 
 
 class B2DError(RuntimeError):
@@ -69,6 +70,24 @@ class DitRequest(C.Structure):
                 ("rng_multiprocessor_count", C.c_int64), ("rng_max_threads_per_multiprocessor", C.c_int64)]
 
 
+class Sa3Config(C.Structure):
+    _fields_ = [("embed_dim", C.c_int64), ("depth", C.c_int64), ("num_heads", C.c_int64), ("cond_dim", C.c_int64),
+                ("global_cond_dim", C.c_int64), ("local_add_cond_dim", C.c_int64), ("num_memory_tokens", C.c_int64),
+                ("io_channels", C.c_int64), ("prompt_max_length", C.c_int64), ("differential_attention", C.c_int32)]
+
+
+class Sa3Request(C.Structure):
+    _fields_ = [("batch", C.c_int64), ("latent_tokens", C.c_int64), ("schedule_points", C.c_int64),
+                ("noise", C.c_void_p), ("padding_mask", C.c_void_p), ("schedule", C.c_void_p),
+                ("cross_positive", C.c_void_p), ("cross_negative", C.c_void_p), ("negative_mask", C.c_void_p),
+                ("global_cond", C.c_void_p), ("local_add", C.c_void_p), ("cfg_scale", C.c_float),
+                ("apg_scale", C.c_float), ("sampler", C.c_int32), ("seed", C.c_uint64),
+                ("rng_offset_blocks", C.POINTER(C.c_uint64)), ("rng_multiprocessor_count", C.c_int64),
+                ("rng_max_threads_per_multiprocessor", C.c_int64)]
+
+
+SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
+
 SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
 
 
@@ -105,6 +124,9 @@ def lib() -> C.CDLL:
         L.b2d_dit_load.argtypes = [P, C.POINTER(DitConfig), C.POINTER(TensorView), I32]
         L.b2d_dit_sample.argtypes = [P, C.POINTER(DitRequest), P, P]
         L.b2d_dit_sample_device.argtypes = [P, C.POINTER(DitRequest), P, P]
+        L.b2d_sa3_load.argtypes = [P, C.POINTER(Sa3Config), C.POINTER(TensorView), I32]
+        L.b2d_sa3_sample.argtypes = [P, C.POINTER(Sa3Request), P, P]
+        L.b2d_sa3_sample_device.argtypes = [P, C.POINTER(Sa3Request), P, P]
         _lib = L
     return _lib
 
@@ -262,6 +284,60 @@ class StableAudioDiT:
         rq = self._request(noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
                            sigma_max, rho, cfg_scale, apg_scale, sampler, schedule, seed, rng_offset, rng_policy)
         self.ctx.check(lib().b2d_dit_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
+                                                   C.c_void_p(stream)))
+        return out
+
+
+class StableAudio3DiT:
+    """StableAudioRfDitRuntime (include/engine/models/stable_audio/rf_dit.h:78-100) on a B200 context: the
+    Stable Audio 3 rectified-flow DiT with memory tokens, local-add conditioning and optional differential
+    attention.  ``weights``: (name, ggml_type, dims, payload) with the GGUF names ``model.model.*``."""
+
+    def __init__(self, ctx: Context, embed_dim: int, depth: int, num_heads: int, cond_dim: int,
+                 global_cond_dim: int, local_add_cond_dim: int, num_memory_tokens: int, prompt_max_length: int,
+                 differential_attention: bool = False, io_channels: int = 64, weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = Sa3Config(embed_dim, depth, num_heads, cond_dim, global_cond_dim, local_add_cond_dim,
+                             num_memory_tokens, io_channels, prompt_max_length, int(bool(differential_attention)))
+        self._offset = C.c_uint64(0)
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_sa3_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    @property
+    def rng_offset_blocks(self) -> int:
+        """TensorIterator Philox offset after the last call (the reference's rng_offset_blocks out-parameter)."""
+        return int(self._offset.value)
+
+    def _request(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
+                 local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy):
+        b, _, t = noise.shape
+        self._offset = C.c_uint64(rng_offset)
+        opt = lambda a: _ptr(a) if a is not None else None  # noqa: E731
+        return Sa3Request(b, t, schedule.shape[-1], _ptr(noise), _ptr(padding_mask), _ptr(schedule),
+                          _ptr(cross_positive), opt(cross_negative), opt(negative_mask), _ptr(global_cond),
+                          _ptr(local_add), cfg_scale, apg_scale, SA3_SAMPLERS.get(sampler, -1), seed,
+                          C.pointer(self._offset), rng_policy[0], rng_policy[1])
+
+    def sample(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
+               local_add, cfg_scale=7.0, apg_scale=1.0, sampler="pingpong", seed=0, rng_offset=0,
+               rng_policy=(1, 256), out=None, stream: int = 0):
+        """Host arrays (numpy / pinned torch) -> latents [B, 64, T]."""
+        arrs = [np.ascontiguousarray(a, np.float32) if isinstance(a, np.ndarray) else a
+                for a in (noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
+                          local_add)]
+        rq = self._request(*arrs, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy)
+        if out is None:
+            out = np.empty(arrs[0].shape, np.float32)
+        self.ctx.check(lib().b2d_sa3_sample(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)), C.c_void_p(stream)))
+        return out
+
+    def sample_device(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask,
+                      global_cond, local_add, out, cfg_scale=7.0, apg_scale=1.0, sampler="pingpong", seed=0,
+                      rng_offset=0, rng_policy=(1, 256), stream: int = 0):
+        """Device tensors (torch CUDA) -> out (device), asynchronous on `stream`."""
+        rq = self._request(noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
+                           local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy)
+        self.ctx.check(lib().b2d_sa3_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
                                                    C.c_void_p(stream)))
         return out
 

@@ -18,6 +18,7 @@
 #include "attention.cuh"
 #include "attention_tc.cuh"
 #include "dit_kernels.cuh"
+#include "sa3_kernels.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -313,6 +314,7 @@ struct HeadWorkspace {
 };
 
 struct DitModel;
+struct Sa3Model;
 
 struct HeadModel {
     b2d_vv_head_config cfg{};
@@ -335,6 +337,7 @@ struct b2d_ctx {
     cudaStream_t load_stream = nullptr;
     std::unique_ptr<HeadModel> head;
     std::unique_ptr<DitModel> dit;
+    std::unique_ptr<Sa3Model> sa3;
 };
 
 namespace {
@@ -723,6 +726,7 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 }
 
 #include "dit_runtime.inc"
+#include "sa3_runtime.inc"
 
 }  // namespace
 
@@ -764,6 +768,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         cudaDeviceSynchronize();
         ctx->head.reset();
         ctx->dit.reset();
+        ctx->sa3.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -1019,6 +1024,65 @@ b2d_status b2d_dit_sample(b2d_ctx* ctx, const b2d_dit_request* request, float* o
 
 b2d_status b2d_dit_sample_device(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents, void* stream) {
     return dit_sample_common(ctx, request, out_latents, stream, false);
+}
+
+b2d_status b2d_sa3_load(b2d_ctx* ctx, const b2d_sa3_config* config, const b2d_tensor_view* tensors,
+                        int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "Stable Audio RF DiT runtime requires assets");
+        const b2d_sa3_config& c = *config;
+        if (c.num_heads <= 0 || c.embed_dim % c.num_heads != 0)
+            fail(B2D_EINVAL, "Stable Audio RF DiT head dimensions are invalid");
+        if (c.embed_dim / c.num_heads != 64) fail(B2D_EINVAL, "head_dim must be 64 on this path");
+        if (c.io_channels != 64) fail(B2D_EINVAL, "io_channels must be 64 on this path");
+        if (c.embed_dim % 128 || c.embed_dim > 4096 || c.cond_dim <= 0 || c.cond_dim % 64 || c.global_cond_dim <= 0 ||
+            c.global_cond_dim % 64 || c.local_add_cond_dim <= 0 || c.num_memory_tokens <= 0 || c.depth <= 0 ||
+            c.prompt_max_length < 0)
+            fail(B2D_EINVAL, "embed_dim must be a multiple of 128 (<= 4096), cond_dim and global_cond_dim of 64");
+        auto m = std::make_unique<Sa3Model>();
+        m->cfg = c;
+        m->d = c.embed_dim;
+        m->heads = c.num_heads;
+        m->cd = c.cond_dim;
+        m->gd = c.global_cond_dim;
+        m->la = c.local_add_cond_dim;
+        m->lak = (c.local_add_cond_dim + 63) / 64 * 64;
+        m->M = c.num_memory_tokens;
+        m->P1 = c.prompt_max_length + 1;
+        m->F = 4 * c.embed_dim;
+        m->nq = c.differential_attention ? 5 : 3;
+        m->nqc = c.differential_attention ? 2 : 1;
+        m->nkv = c.differential_attention ? 3 : 2;
+        const b2d_tensor_view* probe =
+            find_tensor(tensors, n_tensors, "model.model.transformer.layers.0.self_attn.to_qkv.weight");
+        m->bf16 = probe && probe->ggml_type == B2D_TYPE_BF16;
+        ctx->sa3.reset();
+        if (m->bf16)
+            sa3_load_t<__nv_bfloat16>(ctx, *m, tensors, n_tensors);
+        else
+            sa3_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->sa3 = std::move(m);
+    });
+}
+
+static b2d_status sa3_sample_common(b2d_ctx* ctx, const b2d_sa3_request* rq, float* out, void* stream, bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->sa3) fail(B2D_ESTATE, "Stable Audio RF DiT weights are not loaded");
+        if (!rq || !out) fail(B2D_EINVAL, "Stable Audio RF DiT request is null");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (ctx->sa3->bf16)
+            sa3_sample<__nv_bfloat16>(ctx, *rq, out, st, host);
+        else
+            sa3_sample<__half>(ctx, *rq, out, st, host);
+    });
+}
+
+b2d_status b2d_sa3_sample(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents, void* stream) {
+    return sa3_sample_common(ctx, request, out_latents, stream, true);
+}
+
+b2d_status b2d_sa3_sample_device(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents, void* stream) {
+    return sa3_sample_common(ctx, request, out_latents, stream, false);
 }
 
 }  // extern "C"

@@ -51,6 +51,7 @@ struct EpiParams {
     int64_t ldr = 0;
     const float* gate = nullptr;
     int64_t ldg = 0;
+    int gate_rows = 0;          // EPI_RESID: gate row = r / gate_rows (one gate row per sequence); 0: row r
     int* status = nullptr;
     int splits = 1;             // split-K factor (EPI_F32 only): split s writes out + s * split_stride
     int64_t split_stride = 0;
@@ -230,7 +231,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int rbase, int row
                         const int64_t row = rbase + r0 + i;
                         const bool ok = r0 + i < rows_live;
                         rv[i] = ok ? R[row * ep.ldr + col] : 0.f;
-                        gv[i] = (ok && G) ? G[row * ep.ldg + col] : 1.f;
+                        gv[i] = (ok && G) ? G[(ep.gate_rows ? row / ep.gate_rows : row) * ep.ldg + col] : 1.f;
                     }
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {

@@ -199,6 +199,70 @@ B2D_API b2d_status b2d_dit_sample(b2d_ctx* ctx, const b2d_dit_request* request, 
 B2D_API b2d_status b2d_dit_sample_device(b2d_ctx* ctx, const b2d_dit_request* request, float* out_latents,
                                          void* stream);
 
+/* ------------------------------------------ Stable Audio 3 rectified-flow DiT */
+/* Mirrors the StableAudioConfig fields the SA3 DiT uses (include/engine/models/stable_audio/assets.h:14-84).
+ * head_dim = embed_dim / num_heads must be 64, embed_dim a multiple of 128, cond_dim and
+ * global_cond_dim multiples of 64. */
+typedef struct {
+    int64_t embed_dim;
+    int64_t depth;
+    int64_t num_heads;
+    int64_t cond_dim;            /* T5 hidden width of the cross tokens */
+    int64_t global_cond_dim;
+    int64_t local_add_cond_dim;  /* local-add features per latent token (> 0) */
+    int64_t num_memory_tokens;   /* > 0 */
+    int64_t io_channels;         /* must be 64 */
+    int64_t prompt_max_length;   /* cross tokens = prompt_max_length + 1 */
+    int32_t differential_attention;
+} b2d_sa3_config;
+
+/* StableAudioRfDitRuntime::sample sampler_type values ("" selects pingpong, rf_dit.cpp:596-599). */
+enum { B2D_SA3_PINGPONG = 0, B2D_SA3_EULER = 1 };
+
+/* One StableAudioRfDitRuntime::sample request (include/engine/models/stable_audio/rf_dit.h:78-100) with
+ * its StableAudioSamplingState / StableAudioConditioningInputs payloads (fp32, row-major):
+ *   noise [batch, 64, latent_tokens] (BCT), padding_mask [batch, latent_tokens],
+ *   schedule [batch, schedule_points] (sigma per step, 1 -> 0),
+ *   cross_positive / cross_negative [batch, prompt_max_length + 1, cond_dim] (negative NULL: zeros),
+ *   negative_mask [batch, prompt_max_length + 1] (NULL: keep every negative token),
+ *   global_cond [batch, global_cond_dim], local_add [batch, latent_tokens, local_add_cond_dim].
+ * CFG runs when cfg_scale != 1 (graph batch 2 * batch, APG-CFG with apg_scale). */
+typedef struct {
+    int64_t batch;
+    int64_t latent_tokens;
+    int64_t schedule_points;
+    const float* noise;
+    const float* padding_mask;
+    const float* schedule;
+    const float* cross_positive;
+    const float* cross_negative;
+    const float* negative_mask;
+    const float* global_cond;
+    const float* local_add;
+    float cfg_scale, apg_scale;
+    int32_t sampler;            /* B2D_SA3_* */
+    uint64_t seed;              /* pingpong noise seed */
+    uint64_t* rng_offset_blocks;            /* in/out: TensorIterator Philox offset (may be NULL: starts at 0) */
+    int64_t rng_multiprocessor_count;       /* TorchCudaSamplingPolicy; <= 0 selects 1 */
+    int64_t rng_max_threads_per_multiprocessor;  /* <= 0 selects 256 */
+} b2d_sa3_request;
+
+/* Loads the SA3 DiT from its GGUF tensors ("model.model.*", names as load_stable_audio_rf_dit_weights,
+ * src/models/stable_audio/rf_dit.cpp:386-585).  Replaces the weight load of StableAudioRfDitRuntime's
+ * constructor. */
+B2D_API b2d_status b2d_sa3_load(b2d_ctx* ctx, const b2d_sa3_config* config, const b2d_tensor_view* tensors,
+                                int32_t n_tensors);
+
+/* The whole sampling loop as one captured CUDA graph: the pingpong sampler (Philox noise generated on the
+ * device in the TensorIterator layout, *rng_offset_blocks advanced once per step as the reference does) or
+ * euler, with the in-graph APG-CFG of build_cfg_model_output (rf_dit.cpp:834-873).  Host buffers; returns
+ * latents [batch, 64, latent_tokens] (BCT).  Replaces StableAudioRfDitRuntime::sample (rf_dit.cpp:586-694). */
+B2D_API b2d_status b2d_sa3_sample(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents, void* stream);
+
+/* Same with every pointer of the request (schedule included) and out_latents in device memory. */
+B2D_API b2d_status b2d_sa3_sample_device(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents,
+                                         void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
