@@ -260,6 +260,71 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     return res
 
 
+SA3_WORKLOAD = "sa3_bench_bf16"
+
+
+def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
+    """Stable Audio 3 DiT (the first row after the head and the SAO DiT): BF16, 1 prompt + CFG (2 sequences)
+    x (64 memory + 2584 latent) tokens, 8 pingpong steps, CFG 7, APG 1.  Per rank its own prompt (weak
+    scaling).  Metric: sequence-steps/s over all ranks."""
+    from oracle import synth
+    cfg = synth.SA3_CONFIGS[SA3_WORKLOAD]
+    cfg = synth.Sa3Config(**{**cfg.__dict__, "prompt_seeds": (rank,)})
+    w = synth.sa3_weights(cfg)
+    gt = {0: 0, 1: 1, 3: 8, 2: 30}
+    model = b2d.StableAudio3DiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_dim, cfg.global_cond_dim,
+                                cfg.local_add_cond_dim, cfg.num_memory_tokens, cfg.prompt_max_length,
+                                cfg.differential, cfg.io_channels,
+                                weights=[(n, gt[t.dtype], t.dims, t.data) for n, t in w.items()])
+    if rank != 0 or args.no_cpu_baseline:
+        del w
+    inp = synth.sa3_inputs(cfg)
+    keys = ("noise", "padding_mask", "schedule", "cross_positive", "cross_negative", "negative_mask", "global",
+            "local_add")
+    dev = [torch.from_numpy(inp[k].array().copy()).cuda() for k in keys]
+    host = [torch.from_numpy(inp[k].array().copy()).pin_memory() for k in keys]
+    out_dev = torch.empty_like(dev[0])
+    out_host = torch.empty(dev[0].shape).pin_memory()
+    st = torch.cuda.current_stream()
+    kw = dict(cfg_scale=cfg.cfg, apg_scale=cfg.apg, sampler=cfg.sampler, seed=cfg.seed,
+              rng_policy=(cfg.rng_sms, cfg.rng_max_threads), stream=st.cuda_stream)
+    calls, warm = max(1, min(args.steps, 5)), max(3, min(args.warmup, 3))
+    ms = timed(lambda: model.sample_device(*dev, out_dev, **kw), calls, warm)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(lambda: model.sample(*host, out=out_host, **kw), calls, 1)
+    seq_steps = 2 * cfg.batch * cfg.steps * world
+    L1 = cfg.num_memory_tokens + cfg.latent_tokens
+    d = cfg.embed_dim
+    # per sequence-step: projections 2 L1 d (3d + d + d + d + 8d + 4d) + attention 4 L1 (L1 + P1) d; local-add and
+    # the cross K/V are step-invariant and computed once per call
+    fl = 2 * L1 * d * 18 * d + 4 * L1 * (L1 + cfg.prompt_max_length + 1) * d
+    res = {"metric": "denoise sequence-steps/sec (SA3 DiT)", "value": round(seq_steps / (ms / 1e3), 2),
+           "unit": "seq-steps/s", "ms_per_call": round(ms, 2), "timed_calls": calls, "warmup_calls": warm,
+           "config": {"workload": SA3_WORKLOAD,
+                      "model": "Stable-Audio-3-layout DiT at SAO-1.0 transformer size (random-init)",
+                      "weights": cfg.wtype, "sequences_per_rank": 2 * cfg.batch, "tokens": L1,
+                      "steps": cfg.steps, "sampler": cfg.sampler, "cfg_scale": cfg.cfg, "apg_scale": cfg.apg,
+                      "differential_attention": cfg.differential, "n_gpus": world},
+           "dtype": "bf16 tensor-core operands, fp32 accumulate",
+           "e2e": {"value": round(seq_steps / (ms_e2e / 1e3), 2), "unit": "seq-steps/s",
+                   "h2d_bytes_per_step": sum(t.numel() * 4 for t in host), "d2h_bytes_per_step": out_host.numel() * 4,
+                   "api": "b2d_sa3_sample (host buffers, pinned)"},
+           "gpu_launches_per_call": 18 + 5 * cfg.depth + cfg.steps * (7 + 14 * cfg.depth),
+           "whole_call_tflops": round(seq_steps / world * cfg.depth * fl / (ms / 1e3) / 1e12, 1)}
+    assert np.isfinite(out_host.numpy()).all()
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle import ref_runner
+        if ref_runner.available():
+            c1 = synth.Sa3Config(**{**cfg.__dict__, "steps": 1})
+            o = ref_runner.run("sa3", synth.sa3_inputs(c1), w, reps=1)
+            cms = float(o["wall_ms"].data[0])
+            res["cpu_baseline"] = {"value": round(2 * cfg.batch / (cms / 1e3), 4), "unit": "seq-steps/s",
+                                   "cores": os.cpu_count(), "kind": "reference",
+                                   "sample": "1 pingpong step of the 2-sequence SA3 workload, audio.cpp ggml CPU (%s)"
+                                             % ref_runner.variant()}
+    return res
+
+
 def make_timer(torch, args, world, st):
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
 
@@ -293,7 +358,7 @@ def make_timer(torch, args, world, st):
 
 
 def bench_dit_only(args, torch, b2d, world, rank, local):
-    """--workload dit: time only the DiT (used for DiT profiling); prints the DiT result as the line."""
+    """--workload dit / sa3: time only that DiT (used for profiling); prints its result as the line."""
     ctx = b2d.Context(local)
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -301,7 +366,11 @@ def bench_dit_only(args, torch, b2d, world, rank, local):
         peaks = {}
     st = torch.cuda.current_stream()
     with ClockSampler(local) as clk:
-        res = bench_dit(args, torch, b2d, ctx, world, rank, make_timer(torch, args, world, st), peaks)
+        timer = make_timer(torch, args, world, st)
+        if args.workload == "sa3":
+            res = bench_sa3(args, torch, b2d, ctx, world, rank, timer)
+        else:
+            res = bench_dit(args, torch, b2d, ctx, world, rank, timer, peaks)
     if rank == 0:
         res.update({"n_gpus": world, "steps": res["timed_calls"], "warmup": res["warmup_calls"],
                     "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -322,7 +391,7 @@ def bench_ours(args):
     b2d = load_package()
     from oracle import synth  # seeded synthetic weights/inputs (no checkpoints here)
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
-    if args.workload == "dit":
+    if args.workload in ("dit", "sa3"):
         return bench_dit_only(args, torch, b2d, world, rank, local)
     w = synth.head_weights(cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
@@ -408,6 +477,9 @@ def bench_ours(args):
     dit_res = None
     if args.workload in ("all", "dit"):
         dit_res = bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks)
+    sa3_res = None
+    if args.workload == "all":
+        sa3_res = bench_sa3(args, torch, b2d, ctx, world, rank, timed)
     if rank == 0:
         roof = gemm_roofline(b2d, ctx, torch, cfg, peaks)
         flops_call = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
@@ -432,6 +504,8 @@ def bench_ours(args):
                                               "1 warm-up + 1 timed call" % (frames, variant)}
         if dit_res is not None:
             line["dit"] = dit_res
+        if sa3_res is not None:
+            line["sa3"] = sa3_res
         print(json.dumps(line))
     ctx.close()
     if world > 1:
@@ -445,8 +519,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="all", choices=["all", "head", "dit"],
-                    help="head = VibeVoice head (headline metric); dit = also/only time the Stable Audio DiT")
+    ap.add_argument("--workload", default="all", choices=["all", "head", "dit", "sa3"],
+                    help="all = head line with the DiT and SA3 results attached; head = VibeVoice head only; "
+                         "dit / sa3 = only that DiT")
     ap.add_argument("--dit-steps", type=int, default=3, help="timed DiT sampling calls (each 100 DPM++ steps)")
     ap.add_argument("--dit-dpm-steps", type=int, default=0,
                     help="profiling only: DPM++ steps per DiT call instead of the workload's 100")

@@ -343,6 +343,22 @@ SA3_CONFIGS = {
     "sa3_tiny_f32_diff_b2": Sa3Config(differential=True, batch=2, prompt_seeds=(1, 2), ragged_mask=True),
     "sa3_tiny_f32_euler_nocfg": Sa3Config(sampler="euler", cfg=1.0, prompt_seeds=(3,)),
     "sa3_tiny_bf16_diff": Sa3Config(differential=True, wtype=BF16, prompt_seeds=(4,), steps=5),
+    # several attention / GEMM tiles per sequence, a local-add width that is not a multiple of 64
+    "sa3_mid_bf16_diff_b2": Sa3Config(embed_dim=512, num_heads=8, cond_dim=256, global_cond_dim=128,
+                                      local_add_cond_dim=40, num_memory_tokens=8, prompt_max_length=30,
+                                      latent_tokens=300, batch=2, differential=True, wtype=BF16, prompt_seeds=(5, 6),
+                                      ragged_mask=True),
+    # bench workload: the reference tree does not publish the SA3 transformer dimensions (they come from
+    # the model package's JSON); this uses the SAO 1.0 transformer size with SA3's conditioning layout,
+    # 120 s of latents at the SAO latent rate, the documented defaults (8 pingpong steps, CFG 7, APG 1)
+    "sa3_bench_bf16": Sa3Config(embed_dim=1536, depth=24, num_heads=24, cond_dim=768, global_cond_dim=768,
+                                local_add_cond_dim=64, num_memory_tokens=64, prompt_max_length=128,
+                                latent_tokens=2584, steps=8, wtype=BF16, prompt_seeds=(0,)),
+    # 128-wide GEMM tiles (3d, d not multiples of 256), Q8_0 weights, euler with partial APG
+    "sa3_mid_q8_euler": Sa3Config(embed_dim=384, num_heads=6, cond_dim=192, global_cond_dim=64,
+                                  local_add_cond_dim=32, num_memory_tokens=16, prompt_max_length=20,
+                                  latent_tokens=200, cfg=4.5, apg=0.5, sampler="euler", wtype=Q8_0,
+                                  prompt_seeds=(7,)),
 }
 
 SP = "model.model."

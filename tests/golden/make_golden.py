@@ -32,7 +32,7 @@ HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_fram
                 "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps"]
 DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vddim", "tiny_f16_3msde",
                "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps"]
-SA3_GOLDENS = list(synth.SA3_CONFIGS)
+SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
 
 
 def digest(*bundles) -> np.ndarray:

@@ -42,7 +42,7 @@ def run(cfg, model, inp, **kw):
 
 
 @pytest.mark.parametrize("name", ["sa3_tiny_f32", "sa3_tiny_f32_diff_b2", "sa3_tiny_f32_euler_nocfg",
-                                  "sa3_tiny_bf16_diff"])
+                                  "sa3_tiny_bf16_diff", "sa3_mid_bf16_diff_b2", "sa3_mid_q8_euler"])
 def test_sa3_sample_matches_reference(b2d, ctx, name):
     cfg, model = make(b2d, ctx, name)
     inp = synth.sa3_inputs(cfg)

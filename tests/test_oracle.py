@@ -122,7 +122,7 @@ def test_philox_tensor_iterator_layout():
 
 
 @pytest.mark.parametrize("name", ["sa3_tiny_f32", "sa3_tiny_f32_diff_b2", "sa3_tiny_f32_euler_nocfg",
-                                  "sa3_tiny_bf16_diff"])
+                                  "sa3_tiny_bf16_diff", "sa3_mid_bf16_diff_b2", "sa3_mid_q8_euler"])
 def test_sa3_port_vs_reference(name):
     """The Stable Audio 3 DiT restatement (oracle/sa3.py) against StableAudioRfDitRuntime::sample run by the
     reference's own CPU build: with fp32 weights the arithmetic is the same up to summation order (1e-5); with
