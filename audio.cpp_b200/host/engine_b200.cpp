@@ -166,6 +166,87 @@ std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
 
 }  // namespace engine::models::vibevoice
 
+namespace engine::models::stable_audio {
+
+StableAudioRfDitRuntime::StableAudioRfDitRuntime(const StableAudioConfig & config,
+                                                 const std::vector<engine::b200::RawTensor> & tensors, int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    const auto views = engine::b200::views_of(tensors);
+    const b2d_sa3_config c{config.embed_dim,          config.depth,
+                           config.num_heads,          config.cond_dim,
+                           config.global_cond_dim,    config.local_add_cond_dim,
+                           config.num_memory_tokens,  config.io_channels,
+                           config.prompt_max_length,  config.differential_attention ? 1 : 0};
+    device_->check(b2d_sa3_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+void StableAudioRfDitRuntime::prepare(const StableAudioSamplingState & sampling, float) const {
+    if (sampling.batch <= 0 || sampling.latent_sample_size <= 0)
+        throw std::runtime_error("Stable Audio RF DiT graph requires positive batch and latent length");
+}
+
+// Validation and messages as Graph::sample / validate_inputs / make_*_conditioning
+// (src/models/stable_audio/rf_dit.cpp:586-622, 868-946); the whole sampler runs on the GPU (b2d_sa3_sample).
+std::vector<float> StableAudioRfDitRuntime::sample(const StableAudioSamplingState & sampling,
+                                                   const StableAudioConditioningInputs & conditioning, uint64_t seed,
+                                                   uint64_t & rng_offset_blocks,
+                                                   const engine::sampling::TorchCudaSamplingPolicy & rng_policy,
+                                                   std::string_view sampler_type, float cfg_scale,
+                                                   float apg_scale) const {
+    prepare(sampling, cfg_scale);
+    const int64_t B = sampling.batch, T = sampling.latent_sample_size, P1 = config_.prompt_max_length + 1;
+    if (static_cast<int64_t>(sampling.noise.size()) != B * config_.io_channels * T ||
+        static_cast<int64_t>(sampling.padding_mask.size()) != B * T)
+        throw std::runtime_error("Stable Audio RF DiT graph shape mismatch");
+    if (sampling.channels != config_.io_channels) throw std::runtime_error("Stable Audio RF DiT channel count mismatch");
+    if (conditioning.positive.batch != B || conditioning.positive.cross_tokens != P1 ||
+        conditioning.positive.cond_dim != config_.cond_dim ||
+        static_cast<int64_t>(conditioning.positive.global.size()) != B * config_.global_cond_dim)
+        throw std::runtime_error("Stable Audio RF DiT positive conditioning shape mismatch");
+    if (conditioning.has_negative &&
+        (conditioning.negative.batch != B || conditioning.negative.cross_tokens != P1 ||
+         conditioning.negative.cond_dim != config_.cond_dim))
+        throw std::runtime_error("Stable Audio RF DiT negative conditioning shape mismatch");
+    const bool pingpong = sampler_type.empty() || sampler_type == "pingpong";
+    if (!pingpong && sampler_type != "euler")
+        throw std::runtime_error("Stable Audio sampler_type must be pingpong or euler");
+    if (static_cast<int64_t>(sampling.local_add_conditioning.size()) != B * T * config_.local_add_cond_dim)
+        throw std::runtime_error("Stable Audio RF DiT local conditioning shape mismatch");
+    if (sampling.schedule_points <= 1 || static_cast<int64_t>(sampling.schedule.size()) != B * sampling.schedule_points)
+        throw std::runtime_error("Stable Audio RF DiT schedule shape mismatch");
+    // the negative prompt's token mask as the C ABI's float mask (make_cross_conditioning keeps tokens with mask != 0)
+    std::vector<float> nmask;
+    if (conditioning.has_negative) {
+        nmask.assign(static_cast<size_t>(B * P1), 1.0F);
+        for (size_t i = 0; i < nmask.size() && i < conditioning.negative.cross_attention_mask.size(); ++i)
+            nmask[i] = conditioning.negative.cross_attention_mask[i] != 0 ? 1.0F : 0.0F;
+    }
+    b2d_sa3_request rq{};
+    rq.batch = B;
+    rq.latent_tokens = T;
+    rq.schedule_points = sampling.schedule_points;
+    rq.noise = sampling.noise.data();
+    rq.padding_mask = sampling.padding_mask.data();
+    rq.schedule = sampling.schedule.data();
+    rq.cross_positive = conditioning.positive.cross_attention.data();
+    rq.cross_negative = conditioning.has_negative ? conditioning.negative.cross_attention.data() : nullptr;
+    rq.negative_mask = conditioning.has_negative ? nmask.data() : nullptr;
+    rq.global_cond = conditioning.positive.global.data();
+    rq.local_add = sampling.local_add_conditioning.data();
+    rq.cfg_scale = cfg_scale;
+    rq.apg_scale = apg_scale;
+    rq.sampler = pingpong ? B2D_SA3_PINGPONG : B2D_SA3_EULER;
+    rq.seed = seed;
+    rq.rng_offset_blocks = &rng_offset_blocks;
+    rq.rng_multiprocessor_count = rng_policy.multiprocessor_count;
+    rq.rng_max_threads_per_multiprocessor = rng_policy.max_threads_per_multiprocessor;
+    std::vector<float> out(sampling.noise.size());
+    device_->check(b2d_sa3_sample(device_->ctx(), &rq, out.data(), nullptr));
+    return out;
+}
+
+}  // namespace engine::models::stable_audio
+
 namespace engine::models::stable_audio::foundation {
 
 FoundationRfDitRuntime::FoundationRfDitRuntime(const StableAudioConfig & config,

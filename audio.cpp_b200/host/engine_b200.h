@@ -7,6 +7,7 @@
 //   engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime include/engine/models/vibevoice/diffusion_head.h:58-97
 //   engine::models::vibevoice::sample_vibevoice_speech_latents       include/engine/models/vibevoice/diffusion_sampler.h:23-26
 //   engine::models::stable_audio::foundation::FoundationRfDitRuntime include/engine/models/stable_audio/foundation/rf_dit.h:73-106
+//   engine::models::stable_audio::StableAudioRfDitRuntime            include/engine/models/stable_audio/rf_dit.h:78-100
 #pragma once
 
 #include <cstdint>
@@ -151,6 +152,11 @@ struct StableAudioConfig {
     int64_t num_heads = 24;
     int64_t cond_token_dim = 768;
     int64_t global_cond_dim = 1536;
+    // Stable Audio 3 fields (include/engine/models/stable_audio/assets.h:14-84)
+    int64_t cond_dim = 0;
+    int64_t local_add_cond_dim = 0;
+    int64_t num_memory_tokens = 0;
+    bool differential_attention = false;
 };
 
 struct StableAudioSamplingState {
@@ -162,6 +168,7 @@ struct StableAudioSamplingState {
     std::vector<float> schedule;
     std::vector<float> padding_mask;
     std::vector<float> noise;
+    std::vector<float> local_add_conditioning;
 };
 
 struct StableAudioConditionedInput {
@@ -169,6 +176,7 @@ struct StableAudioConditionedInput {
     int64_t cross_tokens = 0;
     int64_t cond_dim = 0;
     std::vector<float> cross_attention;
+    std::vector<uint8_t> cross_attention_mask;
     std::vector<float> global;
 };
 
@@ -176,6 +184,23 @@ struct StableAudioConditioningInputs {
     StableAudioConditionedInput positive;
     StableAudioConditionedInput negative;
     bool has_negative = false;
+};
+
+// Stable Audio 3 rectified-flow DiT: pingpong / euler samplers with APG-CFG, the whole loop on the GPU
+// (b2d_sa3_sample).
+class StableAudioRfDitRuntime {
+public:
+    StableAudioRfDitRuntime(const StableAudioConfig & config, const std::vector<engine::b200::RawTensor> & tensors,
+                            int device);
+    void prepare(const StableAudioSamplingState & sampling, float cfg_scale) const;
+    std::vector<float> sample(const StableAudioSamplingState & sampling,
+                              const StableAudioConditioningInputs & conditioning, uint64_t seed,
+                              uint64_t & rng_offset_blocks, const engine::sampling::TorchCudaSamplingPolicy & rng_policy,
+                              std::string_view sampler_type, float cfg_scale, float apg_scale) const;
+
+private:
+    StableAudioConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
 };
 
 namespace foundation {

@@ -4,6 +4,7 @@
 //   test_engine sched <golden dir>                          scheduler vs reference vectors (no GPU)
 //   test_engine head  <weights> <inputs> <golden>           sample_vibevoice_speech_latents on the GPU
 //   test_engine dit   <weights> <inputs> <golden>           FoundationRfDitRuntime::sample on the GPU
+//   test_engine sa3   <weights> <inputs> <golden>           StableAudioRfDitRuntime::sample on the GPU
 // Bundles are B2DB files (see oracle/bundle.py): weights by tensor name, inputs and goldens by key.
 #include "engine_b200.h"
 
@@ -215,7 +216,7 @@ int test_dit(const std::string & wpath, const std::string & ipath, const std::st
     st.noise = f32(in, "noise");
     st.padding_mask = f32(in, "padding_mask");
     sa::StableAudioConditioningInputs c;
-    c.positive = {st.batch, cfg.prompt_max_length + 2, cfg.cond_token_dim, f32(in, "cross_positive"), f32(in, "global")};
+    c.positive = {st.batch, cfg.prompt_max_length + 2, cfg.cond_token_dim, f32(in, "cross_positive"), {}, f32(in, "global")};
     c.negative = c.positive;
     c.negative.cross_attention = f32(in, "cross_negative");
     c.has_negative = true;
@@ -235,6 +236,58 @@ int test_dit(const std::string & wpath, const std::string & ipath, const std::st
     return failures;
 }
 
+int test_sa3(const std::string & wpath, const std::string & ipath, const std::string & gpath) {
+    namespace sa = engine::models::stable_audio;
+    const Bundle in = read_bundle(ipath), g = read_bundle(gpath);
+    sa::StableAudioConfig cfg;
+    cfg.embed_dim = i64(in, "embed_dim");
+    cfg.depth = i64(in, "depth");
+    cfg.num_heads = i64(in, "num_heads");
+    cfg.cond_dim = i64(in, "cond_dim");
+    cfg.global_cond_dim = i64(in, "global_cond_dim");
+    cfg.local_add_cond_dim = i64(in, "local_add_cond_dim");
+    cfg.num_memory_tokens = i64(in, "num_memory_tokens");
+    cfg.prompt_max_length = i64(in, "prompt_max_length");
+    cfg.differential_attention = i64(in, "differential") != 0;
+    sa::StableAudioRfDitRuntime dit(cfg, tensors_of(read_bundle(wpath)), 0);
+    sa::StableAudioSamplingState st;
+    st.batch = i64(in, "batch");
+    st.latent_sample_size = i64(in, "latent_tokens");
+    st.channels = 64;
+    st.schedule_points = i64(in, "steps") + 1;
+    st.schedule = f32(in, "schedule");
+    st.noise = f32(in, "noise");
+    st.padding_mask = f32(in, "padding_mask");
+    st.local_add_conditioning = f32(in, "local_add");
+    const int64_t P1 = cfg.prompt_max_length + 1;
+    sa::StableAudioConditioningInputs c;
+    c.positive = {st.batch, P1, cfg.cond_dim, f32(in, "cross_positive"), {}, f32(in, "global")};
+    c.negative = c.positive;
+    c.negative.cross_attention = f32(in, "cross_negative");
+    for (const float m : f32(in, "negative_mask")) c.negative.cross_attention_mask.push_back(m != 0.0F ? 1 : 0);
+    c.has_negative = true;
+    uint64_t off = 0;
+    engine::sampling::TorchCudaSamplingPolicy pol;
+    pol.multiprocessor_count = i64(in, "rng_sms");
+    pol.max_threads_per_multiprocessor = i64(in, "rng_max_threads");
+    const auto out = dit.sample(st, c, uint64_t(i64(in, "seed")), off, pol, i64(in, "sampler") == 0 ? "pingpong" : "euler",
+                                f1(in, "cfg_scale"), f1(in, "apg_scale"));
+    const double err = rel_l2(out, f32(g, "latents"));
+    std::printf("sa3 rel-L2 vs the reference %.3g\n", err);
+    require(err < 2e-2, "SA3 latents vs reference");
+    require(int64_t(off) == i64(g, "rng_offset_out"), "rng_offset_blocks out-parameter");
+    require_throws([&] { dit.sample(st, c, 0, off, pol, "dpmpp-2m", 7.f, 1.f); },
+                   "sampler_type must be pingpong or euler");
+    auto bad = st;
+    bad.local_add_conditioning.pop_back();
+    require_throws([&] { dit.sample(bad, c, 0, off, pol, "pingpong", 7.f, 1.f); }, "local conditioning shape mismatch");
+    auto badc = c;
+    badc.positive.cond_dim = 7;
+    require_throws([&] { dit.sample(st, badc, 0, off, pol, "pingpong", 7.f, 1.f); },
+                   "positive conditioning shape mismatch");
+    return failures;
+}
+
 }  // namespace
 
 int main(int argc, char ** argv) {
@@ -242,7 +295,8 @@ int main(int argc, char ** argv) {
         if (argc >= 3 && std::string(argv[1]) == "sched") return test_sched(argv[2]) ? 1 : 0;
         if (argc >= 5 && std::string(argv[1]) == "head") return test_head(argv[2], argv[3], argv[4]) ? 1 : 0;
         if (argc >= 5 && std::string(argv[1]) == "dit") return test_dit(argv[2], argv[3], argv[4]) ? 1 : 0;
-        std::fprintf(stderr, "usage: %s sched <dir> | head|dit <weights> <inputs> <golden>\n", argv[0]);
+        if (argc >= 5 && std::string(argv[1]) == "sa3") return test_sa3(argv[2], argv[3], argv[4]) ? 1 : 0;
+        std::fprintf(stderr, "usage: %s sched <dir> | head|dit|sa3 <weights> <inputs> <golden>\n", argv[0]);
         return 2;
     } catch (const std::exception & e) {
         std::fprintf(stderr, "FAILED with exception: %s\n", e.what());

@@ -1,5 +1,5 @@
 """Runs the C++ tests of the audio.cpp-facing classes (audio.cpp_b200/host/test_engine.cpp):
-the scheduler against the reference vectors on CPU, and the head / DiT runtimes on the GPU."""
+the scheduler against the reference vectors on CPU, and the head / DiT / SA3 runtimes on the GPU."""
 import os
 import subprocess
 
@@ -39,3 +39,12 @@ def test_cpp_dit_runtime(tmp_path):
     B.write(str(tmp_path / "w.b2db"), synth.dit_weights(cfg))
     B.write(str(tmp_path / "in.b2db"), synth.dit_inputs(cfg))
     print(_run("dit", str(tmp_path / "w.b2db"), str(tmp_path / "in.b2db"), os.path.join(GOLDEN, "dit_tiny_bf16.b2db")))
+
+
+@pytest.mark.gpu
+def test_cpp_sa3_runtime(tmp_path):
+    cfg = synth.SA3_CONFIGS["sa3_tiny_f32_diff_b2"]
+    B.write(str(tmp_path / "w.b2db"), synth.sa3_weights(cfg))
+    B.write(str(tmp_path / "in.b2db"), synth.sa3_inputs(cfg))
+    print(_run("sa3", str(tmp_path / "w.b2db"), str(tmp_path / "in.b2db"),
+               os.path.join(GOLDEN, "sa3_tiny_f32_diff_b2.b2db")))
