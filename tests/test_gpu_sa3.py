@@ -76,3 +76,25 @@ def test_sa3_device_api_and_errors(b2d, ctx):
     assert np.array_equal(out.cpu().numpy(), host)
     with pytest.raises(b2d.B2DError, match="pingpong or euler"):
         model.sample(*[inp[k].array() for k in keys], sampler="bogus")
+
+
+def test_sa3_no_negative_prompt_and_rng_offset(b2d, ctx):
+    """cross_negative = NULL (the unconditional half sees zeros, make_cross_conditioning with has_negative false)
+    and a non-zero starting Philox offset, against the fp32-activation restatement run on the same request."""
+    from oracle import bundle as B
+    from oracle import sa3
+    cfg, model = make(b2d, ctx, "sa3_tiny_f32")
+    inp = dict(synth.sa3_inputs(cfg))
+    inp["has_negative"] = B.i64(0)
+    inp["rng_offset"] = B.i64(37)
+    exact = sa3.sample(sa3.Sa3Dit(synth.sa3_weights(cfg), cfg, act="exact"), cfg, inp)
+    a = {k: inp[k].array() for k in ("noise", "padding_mask", "schedule", "cross_positive", "global", "local_add")}
+    out = model.sample(a["noise"], a["padding_mask"], a["schedule"], a["cross_positive"], None, None, a["global"],
+                       a["local_add"], cfg_scale=cfg.cfg, apg_scale=cfg.apg, sampler=cfg.sampler, seed=cfg.seed,
+                       rng_offset=37, rng_policy=(cfg.rng_sms, cfg.rng_max_threads))
+    err = rel_l2(out, exact)
+    print("no negative, offset 37: vs exact %.3g" % err)
+    assert err < 2e-3, err
+    from oracle import philox
+    n = cfg.batch * cfg.io_channels * cfg.latent_tokens
+    assert model.rng_offset_blocks == 37 + cfg.steps * philox.offset_blocks(n, cfg.rng_sms, cfg.rng_max_threads)
