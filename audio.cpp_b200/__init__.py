@@ -67,7 +67,8 @@ class DitRequest(C.Structure):
                 ("global_cond", C.c_void_p), ("sigma_min", C.c_float), ("sigma_max", C.c_float), ("rho", C.c_float),
                 ("cfg_scale", C.c_float), ("apg_scale", C.c_float), ("sampler", C.c_int32), ("schedule", C.c_void_p),
                 ("seed", C.c_uint64), ("rng_offset_blocks", C.POINTER(C.c_uint64)),
-                ("rng_multiprocessor_count", C.c_int64), ("rng_max_threads_per_multiprocessor", C.c_int64)]
+                ("rng_multiprocessor_count", C.c_int64), ("rng_max_threads_per_multiprocessor", C.c_int64),
+                ("rng_batch_total", C.c_int64), ("rng_batch_first", C.c_int64)]
 
 
 class Sa3Config(C.Structure):
@@ -83,7 +84,8 @@ class Sa3Request(C.Structure):
                 ("global_cond", C.c_void_p), ("local_add", C.c_void_p), ("cfg_scale", C.c_float),
                 ("apg_scale", C.c_float), ("sampler", C.c_int32), ("seed", C.c_uint64),
                 ("rng_offset_blocks", C.POINTER(C.c_uint64)), ("rng_multiprocessor_count", C.c_int64),
-                ("rng_max_threads_per_multiprocessor", C.c_int64)]
+                ("rng_max_threads_per_multiprocessor", C.c_int64), ("rng_batch_total", C.c_int64),
+                ("rng_batch_first", C.c_int64)]
 
 
 SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
@@ -251,14 +253,14 @@ class StableAudioDiT:
 
     def _request(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
                  sigma_max, rho, cfg_scale, apg_scale, sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0,
-                 rng_policy=(1, 256)):
+                 rng_policy=(1, 256), rng_batch=(0, 0)):
         b, _, t = noise.shape
         self._offset = C.c_uint64(rng_offset)
         return DitRequest(b, t, steps, _ptr(noise), _ptr(padding_mask), _ptr(cross_positive),
                           _ptr(cross_negative) if cross_negative is not None else None, _ptr(global_cond),
                           sigma_min, sigma_max, rho, cfg_scale, apg_scale, SAMPLERS[sampler],
                           _ptr(schedule) if schedule is not None else None, seed, C.pointer(self._offset),
-                          rng_policy[0], rng_policy[1])
+                          rng_policy[0], rng_policy[1], rng_batch[1], rng_batch[0])
 
     @property
     def rng_offset_blocks(self) -> int:
@@ -267,12 +269,13 @@ class StableAudioDiT:
 
     def sample(self, noise, padding_mask, cross_positive, cross_negative, global_cond, steps=100, sigma_min=0.01,
                sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, out=None, stream: int = 0,
-               sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256)):
-        """Host arrays (numpy / pinned torch) -> latents [B, 64, T]."""
+               sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256), rng_batch=(0, 0)):
+        """Host arrays (numpy / pinned torch) -> latents [B, 64, T].  rng_batch = (first prompt, prompts in the
+        whole batch) when this call is one data-parallel shard of a batched request (noise as the batched call)."""
         arrs = [np.ascontiguousarray(a, np.float32) if isinstance(a, np.ndarray) else a
                 for a in (noise, padding_mask, cross_positive, cross_negative, global_cond, schedule)]
         rq = self._request(*arrs[:5], steps, sigma_min, sigma_max, rho, cfg_scale, apg_scale, sampler, arrs[5], seed,
-                           rng_offset, rng_policy)
+                           rng_offset, rng_policy, rng_batch)
         if out is None:
             out = np.empty(arrs[0].shape, np.float32)
         self.ctx.check(lib().b2d_dit_sample(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)), C.c_void_p(stream)))
@@ -280,9 +283,10 @@ class StableAudioDiT:
 
     def sample_device(self, noise, padding_mask, cross_positive, cross_negative, global_cond, out, steps=100,
                       sigma_min=0.01, sigma_max=100.0, rho=1.0, cfg_scale=7.0, apg_scale=1.0, stream: int = 0,
-                      sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256)):
+                      sampler="dpmpp-2m", schedule=None, seed=0, rng_offset=0, rng_policy=(1, 256), rng_batch=(0, 0)):
         rq = self._request(noise, padding_mask, cross_positive, cross_negative, global_cond, steps, sigma_min,
-                           sigma_max, rho, cfg_scale, apg_scale, sampler, schedule, seed, rng_offset, rng_policy)
+                           sigma_max, rho, cfg_scale, apg_scale, sampler, schedule, seed, rng_offset, rng_policy,
+                           rng_batch)
         self.ctx.check(lib().b2d_dit_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
                                                    C.c_void_p(stream)))
         return out
@@ -309,23 +313,24 @@ class StableAudio3DiT:
         return int(self._offset.value)
 
     def _request(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
-                 local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy):
+                 local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy, rng_batch=(0, 0)):
         b, _, t = noise.shape
         self._offset = C.c_uint64(rng_offset)
         opt = lambda a: _ptr(a) if a is not None else None  # noqa: E731
         return Sa3Request(b, t, schedule.shape[-1], _ptr(noise), _ptr(padding_mask), _ptr(schedule),
                           _ptr(cross_positive), opt(cross_negative), opt(negative_mask), _ptr(global_cond),
                           _ptr(local_add), cfg_scale, apg_scale, SA3_SAMPLERS.get(sampler, -1), seed,
-                          C.pointer(self._offset), rng_policy[0], rng_policy[1])
+                          C.pointer(self._offset), rng_policy[0], rng_policy[1], rng_batch[1], rng_batch[0])
 
     def sample(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
                local_add, cfg_scale=7.0, apg_scale=1.0, sampler="pingpong", seed=0, rng_offset=0,
-               rng_policy=(1, 256), out=None, stream: int = 0):
-        """Host arrays (numpy / pinned torch) -> latents [B, 64, T]."""
+               rng_policy=(1, 256), out=None, stream: int = 0, rng_batch=(0, 0)):
+        """Host arrays (numpy / pinned torch) -> latents [B, 64, T].  rng_batch = (first prompt, prompts in the
+        whole batch) when this call is one data-parallel shard of a batched request (noise as the batched call)."""
         arrs = [np.ascontiguousarray(a, np.float32) if isinstance(a, np.ndarray) else a
                 for a in (noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
                           local_add)]
-        rq = self._request(*arrs, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy)
+        rq = self._request(*arrs, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy, rng_batch)
         if out is None:
             out = np.empty(arrs[0].shape, np.float32)
         self.ctx.check(lib().b2d_sa3_sample(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)), C.c_void_p(stream)))
@@ -333,10 +338,10 @@ class StableAudio3DiT:
 
     def sample_device(self, noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask,
                       global_cond, local_add, out, cfg_scale=7.0, apg_scale=1.0, sampler="pingpong", seed=0,
-                      rng_offset=0, rng_policy=(1, 256), stream: int = 0):
+                      rng_offset=0, rng_policy=(1, 256), stream: int = 0, rng_batch=(0, 0)):
         """Device tensors (torch CUDA) -> out (device), asynchronous on `stream`."""
         rq = self._request(noise, padding_mask, schedule, cross_positive, cross_negative, negative_mask, global_cond,
-                           local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy)
+                           local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy, rng_batch)
         self.ctx.check(lib().b2d_sa3_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
                                                    C.c_void_p(stream)))
         return out

@@ -153,6 +153,7 @@ struct DitStepCoef {
     int first_step;
     int hist;                    // 3M: previous denoised outputs available (0, 1, 2)
     unsigned long long seed, rng_offset, rng_stride;  // 3M noise: TensorIterator Philox stream of this step
+    unsigned long long rng_elem0;                      // first element of this request within the batched draw
 };
 
 // Per (step, prompt): alpha / sigma = cos / sin(t pi / 2) of this and the next timestep.
@@ -312,7 +313,7 @@ __global__ void dit_update_kernel(const float* __restrict__ part, int splits, in
                 } else if (k.hist == 1) {
                     nx += k.phi2 * ((denoised - hist_p1[i]) / k.r0);
                 }
-                nx += torch_iterator_randn_at(k.seed, k.rng_offset, k.rng_stride, uint64_t(i)) * k.noise_scale;
+                nx += torch_iterator_randn_at(k.seed, k.rng_offset, k.rng_stride, uint64_t(i) + k.rng_elem0) * k.noise_scale;
             }
             hist_cur[i] = denoised;
         }

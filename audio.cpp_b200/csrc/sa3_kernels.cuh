@@ -237,6 +237,7 @@ struct Sa3StepCoef {
     int sampler;     // 0 pingpong, 1 euler
     int final_step;
     unsigned long long seed, rng_offset, rng_stride;  // pingpong noise: TensorIterator Philox stream
+    unsigned long long rng_elem0;                      // first element of this request within the batched draw
 };
 struct Sa3BatchCoef {
     float sigma, next_sigma, dt;  // next_sigma = sigma + dt, dt = schedule[s + 1] - schedule[s] (fp32)
@@ -333,7 +334,7 @@ __global__ void sa3_update_kernel(const float* __restrict__ part, int splits, in
         if (k.sampler == 0) {
             const float den = xv - kb.sigma * v;
             nx = (1.0f - kb.next_sigma) * den +
-                 kb.next_sigma * torch_iterator_randn_at(k.seed, k.rng_offset, k.rng_stride, uint64_t(i));
+                 kb.next_sigma * torch_iterator_randn_at(k.seed, k.rng_offset, k.rng_stride, uint64_t(i) + k.rng_elem0);
         } else {
             nx = xv + kb.dt * v;
         }

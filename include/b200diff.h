@@ -180,6 +180,11 @@ typedef struct {
     uint64_t* rng_offset_blocks;            /* in/out: TensorIterator Philox offset (may be NULL: starts at 0) */
     int64_t rng_multiprocessor_count;       /* TorchCudaSamplingPolicy (include/engine/framework/sampling/ */
     int64_t rng_max_threads_per_multiprocessor;  /* torch_random.h:12-17); <= 0 selects 1 / 256 */
+    /* No counterpart in the reference (0, 0 = the request is the whole batch): this request holds prompts
+     * [rng_batch_first, rng_batch_first + batch) of a batch of rng_batch_total prompts and draws its slice of
+     * that batched call's noise, so data-parallel shards reproduce the single batched call. */
+    int64_t rng_batch_total;
+    int64_t rng_batch_first;
 } b2d_dit_request;
 
 /* Loads the DiT from its GGUF tensors ("model.model.*", names as load_foundation_rf_dit_weights,
@@ -245,6 +250,8 @@ typedef struct {
     uint64_t* rng_offset_blocks;            /* in/out: TensorIterator Philox offset (may be NULL: starts at 0) */
     int64_t rng_multiprocessor_count;       /* TorchCudaSamplingPolicy; <= 0 selects 1 */
     int64_t rng_max_threads_per_multiprocessor;  /* <= 0 selects 256 */
+    int64_t rng_batch_total;    /* as in b2d_dit_request (0, 0 = the request is the whole batch) */
+    int64_t rng_batch_first;
 } b2d_sa3_request;
 
 /* Loads the SA3 DiT from its GGUF tensors ("model.model.*", names as load_stable_audio_rf_dit_weights,

@@ -141,3 +141,25 @@ def test_dit_without_cfg_and_device_api(b2d, ctx):
     torch.cuda.synchronize()
     ctx.sync()
     assert np.array_equal(out.cpu().numpy(), host)
+
+
+def test_dit_prompt_shards_reproduce_the_batched_3m_sde_call(b2d, ctx):
+    """Data-parallel shards of one batched DPM++ 3M SDE request (rng_batch = (first, total)) draw their slices
+    of the batched call's TensorIterator noise and reproduce its latents (up to GEMM accumulation order)."""
+    cfg, dit = make_dit(b2d, ctx, "tiny_f16_3msde")
+    inp = synth.dit_inputs(cfg)
+    keys = ("noise", "padding_mask", "cross_positive", "cross_negative", "global")
+    full = {k: inp[k].array() for k in keys}
+    kw = dict(steps=cfg.steps, sigma_min=cfg.sigma_min, sigma_max=cfg.sigma_max, rho=cfg.rho, cfg_scale=cfg.cfg,
+              apg_scale=cfg.apg, sampler=cfg.sampler, seed=cfg.seed, rng_policy=(cfg.rng_sms, cfg.rng_max_threads))
+    batched = dit.sample(*[full[k] for k in keys], **kw)
+    off = dit.rng_offset_blocks
+    parts = []
+    for b in range(cfg.batch):
+        parts.append(dit.sample(*[full[k][b:b + 1] for k in keys], rng_batch=(b, cfg.batch), **kw))
+        assert dit.rng_offset_blocks == off
+    err = rel_l2(np.concatenate(parts), batched)
+    print("shards vs batched %.3g" % err)
+    assert err < 1e-4, err
+    with pytest.raises(b2d.B2DError, match="outside a batch"):
+        dit.sample(*[full[k][1:2] for k in keys], rng_batch=(2, cfg.batch), **kw)

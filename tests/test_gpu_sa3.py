@@ -98,3 +98,30 @@ def test_sa3_no_negative_prompt_and_rng_offset(b2d, ctx):
     from oracle import philox
     n = cfg.batch * cfg.io_channels * cfg.latent_tokens
     assert model.rng_offset_blocks == 37 + cfg.steps * philox.offset_blocks(n, cfg.rng_sms, cfg.rng_max_threads)
+
+
+def test_sa3_prompt_shards_reproduce_the_batched_call(b2d, ctx):
+    """Data-parallel shards of one batched pingpong request (one prompt each, rng_batch = (first, total)) draw
+    their slices of the batched call's TensorIterator noise and reproduce its latents (up to GEMM accumulation
+    order), and the batched call itself matches the reference."""
+    cfg, model = make(b2d, ctx, "sa3_tiny_f32_diff_b2")
+    inp = synth.sa3_inputs(cfg)
+    keys = ("noise", "padding_mask", "schedule", "cross_positive", "cross_negative", "negative_mask", "global",
+            "local_add")
+    full = {k: inp[k].array() for k in keys}
+    kw = dict(cfg_scale=cfg.cfg, apg_scale=cfg.apg, sampler=cfg.sampler, seed=cfg.seed,
+              rng_policy=(cfg.rng_sms, cfg.rng_max_threads))
+    batched = model.sample(*[full[k] for k in keys], **kw)
+    offset_batched = model.rng_offset_blocks
+    parts = []
+    for b in range(cfg.batch):
+        parts.append(model.sample(*[full[k][b:b + 1] for k in keys], rng_batch=(b, cfg.batch), **kw))
+        assert model.rng_offset_blocks == offset_batched
+    sharded = np.concatenate(parts)
+    err = rel_l2(sharded, batched)
+    print("shards vs batched %.3g" % err)
+    assert err < 1e-4, err
+    assert rel_l2(batched, golden("sa3_tiny_f32_diff_b2")["latents"].array()) < 2e-2
+    # without the batch slice each one-prompt call draws its own (different) noise stream
+    alone = model.sample(*[full[k][1:2] for k in keys], **kw)
+    assert rel_l2(alone, batched[1:2]) > 1e-2
