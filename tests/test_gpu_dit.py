@@ -160,6 +160,6 @@ def test_dit_prompt_shards_reproduce_the_batched_3m_sde_call(b2d, ctx):
         assert dit.rng_offset_blocks == off
     err = rel_l2(np.concatenate(parts), batched)
     print("shards vs batched %.3g" % err)
-    assert err < 1e-4, err
+    assert err < 1e-3, err
     with pytest.raises(b2d.B2DError, match="outside a batch"):
         dit.sample(*[full[k][1:2] for k in keys], rng_batch=(2, cfg.batch), **kw)

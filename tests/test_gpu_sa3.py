@@ -120,7 +120,7 @@ def test_sa3_prompt_shards_reproduce_the_batched_call(b2d, ctx):
     sharded = np.concatenate(parts)
     err = rel_l2(sharded, batched)
     print("shards vs batched %.3g" % err)
-    assert err < 1e-4, err
+    assert err < 1e-3, err
     assert rel_l2(batched, golden("sa3_tiny_f32_diff_b2")["latents"].array()) < 2e-2
     # without the batch slice each one-prompt call draws its own (different) noise stream
     alone = model.sample(*[full[k][1:2] for k in keys], **kw)
