@@ -23,6 +23,7 @@
 #include "engine/framework/assets/tensor_source.h"
 #include "engine/framework/core/execution_context.h"
 #include "engine/framework/sampling/torch_random.h"
+#include "engine/models/stable_audio/foundation/oobleck_autoencoder.h"
 #include "engine/models/stable_audio/foundation/rf_dit.h"
 #include "engine/models/stable_audio/rf_dit.h"
 #include "engine/models/vibevoice/diffusion_head.h"
@@ -484,6 +485,47 @@ int cmd_sa3(const std::string & w, const std::string & in_path, const std::strin
     return 0;
 }
 
+// ------------------------------------------------------ Oobleck VAE decode
+// OobleckAutoencoderRuntime::decode (src/models/stable_audio/foundation/oobleck_autoencoder.cpp:600-705):
+// weight-normalised in-conv, decoder blocks (snake, transposed-conv upsampling, crop, three dilated
+// residual units), final snake and out-conv; latents [B, latent_dim, T] -> audio [B, frames, channels].
+int cmd_oobleck(const std::string & w, const std::string & in_path, const std::string & out_path, int threads,
+                int reps) {
+    namespace sf = engine::models::stable_audio::foundation;
+    namespace sa = engine::models::stable_audio;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<sa::StableAudioAssets>();
+    auto & c = assets->config;
+    c.latent_dim = i64_scalar(in, "latent_dim");
+    c.audio_channels = static_cast<int>(i64_scalar(in, "audio_channels"));
+    c.sample_rate = 44100;
+    c.same_channels = i64_scalar(in, "channels");
+    c.same_c_mults = i64s(in, "c_mults");
+    c.same_strides = i64s(in, "strides");
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
+    const int64_t batch = i64_scalar(in, "batch");
+    const int64_t tokens = i64_scalar(in, "latent_tokens");
+    const auto latents = f32s(in, "latents");
+    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    sf::OobleckAutoencoderRuntime vae(exec, assets, engine::assets::TensorStorageType::Native);
+    vae.prepare_decode(batch, tokens);
+    std::vector<float> times, audio;
+    int64_t frames = 0;
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        const double t0 = now_ms();
+        const auto out = vae.decode(latents, batch, tokens);
+        times.push_back(static_cast<float>(now_ms() - t0));
+        audio.clear();
+        for (const auto & a : out) audio.insert(audio.end(), a.samples.begin(), a.samples.end());
+        frames = static_cast<int64_t>(out.front().samples.size()) / c.audio_channels;
+    }
+    Bundle out;
+    out["audio"] = f32_entry(audio, {batch, frames, static_cast<int64_t>(c.audio_channels)});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
 // ------------------------------------------------------------- Philox randn
 // torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
 int cmd_randn(const std::string & in_path, const std::string & out_path) {
@@ -561,6 +603,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "oobleck") return cmd_oobleck(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         std::fprintf(stderr, "unknown command %s\n", cmd.c_str());
         return 2;
     } catch (const std::exception & e) {

@@ -451,3 +451,98 @@ def sa3_inputs(cfg: Sa3Config) -> Dict[str, B.Tensor]:
     sched[:, 0], sched[:, -1] = 1.0, 0.0
     d["schedule"] = B.f32(sched)
     return d
+
+
+@dataclass
+class OobleckConfig:
+    """StableAudioConfig fields of the Oobleck VAE decoder (include/engine/models/stable_audio/assets.h:14-84:
+    latent_dim, same_channels, same_c_mults, same_strides, audio_channels) and the decode request."""
+    latent_dim: int = 64
+    channels: int = 64
+    c_mults: tuple = (1, 2, 4)
+    strides: tuple = (2, 4, 2)
+    audio_channels: int = 2
+    batch: int = 1
+    latent_tokens: int = 32
+    wseed: int = 11
+    seed: int = 12
+
+    def decoder_channels(self):
+        return [self.channels * m for m in (1,) + tuple(self.c_mults)]
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        d = {k: B.i64(getattr(self, k)) for k in ("latent_dim", "channels", "audio_channels", "batch",
+                                                    "latent_tokens")}
+        d["c_mults"] = B.i64(np.array(self.c_mults, np.int64))
+        d["strides"] = B.i64(np.array(self.strides, np.int64))
+        return d
+
+
+OOBLECK_CONFIGS = {
+    "oobleck_tiny": OobleckConfig(),
+    "oobleck_tiny_b2_odd": OobleckConfig(c_mults=(1, 2), strides=(3, 5), batch=2, latent_tokens=21, wseed=13,
+                                         seed=14),
+}
+
+OP = "pretransform.model.decoder.layers."
+
+
+def oobleck_weights(cfg: OobleckConfig) -> Dict[str, B.Tensor]:
+    """Tensor names and shapes of load_oobleck_autoencoder_weights' decoder half
+    (src/models/stable_audio/foundation/oobleck_autoencoder.cpp:334-420): weight-normalised convs stored as
+    weight_v / weight_g (+ bias), snake alpha / beta stored as logarithms."""
+    rng = np.random.default_rng(cfg.wseed)
+    ch = cfg.decoder_channels()
+    w: Dict[str, B.Tensor] = {}
+
+    def conv(prefix, shape, gain, bias=True):
+        w[prefix + ".weight_v"] = B.f32(_normal(rng, shape))
+        w[prefix + ".weight_g"] = B.f32((gain * (0.75 + 0.5 * rng.random((shape[0], 1, 1)))).astype(np.float32))
+        if bias:
+            w[prefix + ".bias"] = B.f32(_normal(rng, (shape[0],), 0.02))
+
+    def snake(prefix, c):
+        w[prefix + ".alpha"] = B.f32(_normal(rng, (c,), 0.2))
+        w[prefix + ".beta"] = B.f32(_normal(rng, (c,), 0.2))
+
+    conv(OP + "0", (ch[-1], cfg.latent_dim, 7), 1.0)
+    n = len(cfg.strides)
+    for block in range(n, 0, -1):
+        p = OP + str(n - block + 1) + ".layers."
+        cin, cout, s = ch[block], ch[block - 1], cfg.strides[block - 1]
+        snake(p + "0", cin)
+        # ConvTranspose1d weight [in, out, 2 s], weight_g per input channel, bias per output channel
+        w[p + "1.weight_v"] = B.f32(_normal(rng, (cin, cout, 2 * s)))
+        w[p + "1.weight_g"] = B.f32((0.75 + 0.5 * rng.random((cin, 1, 1))).astype(np.float32))
+        w[p + "1.bias"] = B.f32(_normal(rng, (cout,), 0.02))
+        for r in (2, 3, 4):
+            q = p + str(r) + ".layers."
+            snake(q + "0", cout)
+            conv(q + "1", (cout, cout, 7), 0.4)
+            snake(q + "2", cout)
+            conv(q + "3", (cout, cout, 1), 0.4)
+    snake(OP + str(n + 1), ch[0])
+    conv(OP + str(n + 2), (cfg.audio_channels, ch[0], 7), 1.0, bias=False)
+    # the encoder half, which the reference's loader also requires (decode does not use it)
+    E = "pretransform.model.encoder.layers."
+    conv(E + "0", (ch[0], cfg.audio_channels, 7), 1.0)
+    for block in range(n):
+        p = E + str(block + 1) + ".layers."
+        for r in range(3):
+            q = p + str(r) + ".layers."
+            snake(q + "0", ch[block])
+            conv(q + "1", (ch[block], ch[block], 7), 0.4)
+            snake(q + "2", ch[block])
+            conv(q + "3", (ch[block], ch[block], 1), 0.4)
+        snake(p + "3", ch[block])
+        conv(p + "4", (ch[block + 1], ch[block], 2 * cfg.strides[block]), 1.0)
+    snake(E + str(n + 1), ch[-1])
+    conv(E + str(n + 2), (2 * cfg.latent_dim, ch[-1], 3), 1.0)
+    return w
+
+
+def oobleck_inputs(cfg: OobleckConfig) -> Dict[str, B.Tensor]:
+    """Latents [B, latent_dim, T] ~ N(0, 1)."""
+    d = cfg.scalars()
+    d["latents"] = B.f32(_normal(np.random.default_rng(cfg.seed), (cfg.batch, cfg.latent_dim, cfg.latent_tokens)))
+    return d

@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import dit, ref_runner, sa3, synth, vibevoice  # noqa: E402
+from oracle import dit, oobleck, ref_runner, sa3, synth, vibevoice  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -33,6 +33,7 @@ HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_fram
 DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vddim", "tiny_f16_3msde",
                "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps"]
 SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
+OOBLECK_GOLDENS = [n for n in synth.OOBLECK_CONFIGS if "bench" not in n]
 
 
 def digest(*bundles) -> np.ndarray:
@@ -113,9 +114,19 @@ def sa3_golden(name: str) -> None:
     print("sa3", name, "ok", out["latents"].dims)
 
 
+def oobleck_golden(name: str) -> None:
+    """Stable Audio Oobleck VAE decode (OobleckAutoencoderRuntime::decode) on a tiny seeded configuration."""
+    cfg = synth.OOBLECK_CONFIGS[name]
+    w, inp = synth.oobleck_weights(cfg), synth.oobleck_inputs(cfg)
+    out = ref_runner.run("oobleck", inp, w)
+    B.write(os.path.join(HERE, "%s.b2db" % name),
+            {"audio": out["audio"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("oobleck", name, "ok", out["audio"].dims)
+
+
 def main(argv) -> None:
     names = argv or (["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS] +
-                     ["sa3:" + n for n in SA3_GOLDENS])
+                     ["sa3:" + n for n in SA3_GOLDENS] + ["oobleck:" + n for n in OOBLECK_GOLDENS])
     for n in names:
         if n == "q8":
             q8_golden()
@@ -127,6 +138,8 @@ def main(argv) -> None:
             dit_golden(n[4:])
         elif n.startswith("sa3:"):
             sa3_golden(n[4:])
+        elif n.startswith("oobleck:"):
+            oobleck_golden(n[8:])
         else:
             raise SystemExit("unknown fixture " + n)
 

@@ -146,3 +146,19 @@ def test_sa3_port_vs_reference(name):
     draws = cfg.steps if cfg.sampler == "pingpong" else 0
     n = cfg.batch * cfg.io_channels * cfg.latent_tokens
     assert int(g["rng_offset_out"].data[0]) == draws * philox.offset_blocks(n, cfg.rng_sms, cfg.rng_max_threads)
+
+
+@pytest.mark.parametrize("name", ["oobleck_tiny", "oobleck_tiny_b2_odd"])
+def test_oobleck_port_vs_reference(name):
+    """The Oobleck VAE decoder restatement (oracle/oobleck.py) against OobleckAutoencoderRuntime::decode run by the
+    reference's own CPU build (fp32 weights: same arithmetic up to summation order)."""
+    from oracle import oobleck, synth
+    cfg = synth.OOBLECK_CONFIGS[name]
+    w, inp = synth.oobleck_weights(cfg), synth.oobleck_inputs(cfg)
+    g = golden(name)
+    assert np.array_equal(digest(w, inp), g["input_sha256"].data), "synthetic generator drifted"
+    ref = g["audio"].array()
+    mine = oobleck.OobleckDecoder(w, cfg).decode(inp["latents"].array())
+    assert mine.shape == ref.shape
+    err = float(np.linalg.norm(mine - ref) / np.linalg.norm(ref))
+    assert err < 1e-5, err
