@@ -30,7 +30,8 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
             "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
-            "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device"]
+            "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
+            "b2d_oobleck_decode_device"]
 
 
 class B2DError(RuntimeError):
@@ -88,6 +89,11 @@ class Sa3Request(C.Structure):
                 ("rng_batch_first", C.c_int64)]
 
 
+class OobleckConfig(C.Structure):
+    _fields_ = [("latent_dim", C.c_int64), ("channels", C.c_int64), ("audio_channels", C.c_int64),
+                ("n_blocks", C.c_int32), ("c_mults", C.c_int64 * 8), ("strides", C.c_int64 * 8)]
+
+
 SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
 
 SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
@@ -129,6 +135,9 @@ def lib() -> C.CDLL:
         L.b2d_sa3_load.argtypes = [P, C.POINTER(Sa3Config), C.POINTER(TensorView), I32]
         L.b2d_sa3_sample.argtypes = [P, C.POINTER(Sa3Request), P, P]
         L.b2d_sa3_sample_device.argtypes = [P, C.POINTER(Sa3Request), P, P]
+        L.b2d_oobleck_load.argtypes = [P, C.POINTER(OobleckConfig), C.POINTER(TensorView), I32]
+        L.b2d_oobleck_decode.argtypes = [P, P, I64, I64, P, P]
+        L.b2d_oobleck_decode_device.argtypes = [P, P, I64, I64, P, P]
         _lib = L
     return _lib
 
@@ -344,6 +353,40 @@ class StableAudio3DiT:
                            local_add, cfg_scale, apg_scale, sampler, seed, rng_offset, rng_policy, rng_batch)
         self.ctx.check(lib().b2d_sa3_sample_device(self.ctx.handle, C.byref(rq), C.c_void_p(_ptr(out)),
                                                    C.c_void_p(stream)))
+        return out
+
+
+class OobleckDecoder:
+    """OobleckAutoencoderRuntime's decode half (include/engine/models/stable_audio/foundation/oobleck_autoencoder.h:
+    71-96) on a B200 context.  ``weights``: (name, ggml_type, dims, payload) with the names
+    ``pretransform.model.decoder.layers.*``."""
+
+    def __init__(self, ctx: Context, latent_dim: int, channels: int, c_mults, strides, audio_channels: int = 2,
+                 weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = OobleckConfig(latent_dim, channels, audio_channels, len(strides))
+        for i, (m, s) in enumerate(zip(c_mults, strides)):
+            self.cfg.c_mults[i] = m
+            self.cfg.strides[i] = s
+        self.hop = int(np.prod(strides))
+        self.audio_channels = audio_channels
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_oobleck_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    def decode(self, latents, out=None, stream: int = 0):
+        """Host latents [B, latent_dim, T] -> audio [B, T x hop, audio_channels]."""
+        latents = np.ascontiguousarray(latents, np.float32) if isinstance(latents, np.ndarray) else latents
+        b, _, t = latents.shape
+        if out is None:
+            out = np.empty((b, t * self.hop, self.audio_channels), np.float32)
+        self.ctx.check(lib().b2d_oobleck_decode(self.ctx.handle, _ptr(latents), b, t, _ptr(out), C.c_void_p(stream)))
+        return out
+
+    def decode_device(self, latents, out, stream: int = 0):
+        """Device latents -> device audio, asynchronous on `stream`."""
+        b, _, t = latents.shape
+        self.ctx.check(lib().b2d_oobleck_decode_device(self.ctx.handle, _ptr(latents), b, t, _ptr(out),
+                                                       C.c_void_p(stream)))
         return out
 
 

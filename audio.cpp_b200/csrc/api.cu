@@ -19,6 +19,7 @@
 #include "attention_tc.cuh"
 #include "dit_kernels.cuh"
 #include "sa3_kernels.cuh"
+#include "conv_tc.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -315,6 +316,7 @@ struct HeadWorkspace {
 
 struct DitModel;
 struct Sa3Model;
+struct OobModel;
 
 struct HeadModel {
     b2d_vv_head_config cfg{};
@@ -338,6 +340,7 @@ struct b2d_ctx {
     std::unique_ptr<HeadModel> head;
     std::unique_ptr<DitModel> dit;
     std::unique_ptr<Sa3Model> sa3;
+    std::unique_ptr<OobModel> oob;
 };
 
 namespace {
@@ -727,6 +730,7 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 
 #include "dit_runtime.inc"
 #include "sa3_runtime.inc"
+#include "oobleck_runtime.inc"
 
 }  // namespace
 
@@ -769,6 +773,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         ctx->head.reset();
         ctx->dit.reset();
         ctx->sa3.reset();
+        ctx->oob.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -1083,6 +1088,43 @@ b2d_status b2d_sa3_sample(b2d_ctx* ctx, const b2d_sa3_request* request, float* o
 
 b2d_status b2d_sa3_sample_device(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents, void* stream) {
     return sa3_sample_common(ctx, request, out_latents, stream, false);
+}
+
+b2d_status b2d_oobleck_load(b2d_ctx* ctx, const b2d_oobleck_config* config, const b2d_tensor_view* tensors,
+                            int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0))
+            fail(B2D_EINVAL, "Stable Audio Foundation Oobleck runtime requires assets");
+        const b2d_oobleck_config& c = *config;
+        if (c.n_blocks <= 0 || c.n_blocks > 8 || c.channels <= 0 || c.latent_dim <= 0 || c.latent_dim % 64 ||
+            c.audio_channels <= 0 || c.audio_channels > 64)
+            fail(B2D_EINVAL, "Oobleck config: latent_dim must be a multiple of 64, 1..8 blocks, 1..64 audio channels");
+        for (int i = 0; i < c.n_blocks; ++i)
+            if (c.c_mults[i] <= 0 || c.strides[i] <= 0) fail(B2D_EINVAL, "Oobleck config: c_mults / strides must be positive");
+        auto m = std::make_unique<OobModel>();
+        m->cfg = c;
+        ctx->oob.reset();
+        oob_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->oob = std::move(m);
+    });
+}
+
+static b2d_status oob_decode_common(b2d_ctx* ctx, const float* latents, int64_t batch, int64_t latent_tokens,
+                                    float* audio, void* stream, bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->oob) fail(B2D_ESTATE, "Stable Audio Foundation Oobleck weights are not loaded");
+        oob_decode<__half>(ctx, latents, batch, latent_tokens, audio, static_cast<cudaStream_t>(stream), host);
+    });
+}
+
+b2d_status b2d_oobleck_decode(b2d_ctx* ctx, const float* latents, int64_t batch, int64_t latent_tokens, float* audio,
+                              void* stream) {
+    return oob_decode_common(ctx, latents, batch, latent_tokens, audio, stream, true);
+}
+
+b2d_status b2d_oobleck_decode_device(b2d_ctx* ctx, const float* latents, int64_t batch, int64_t latent_tokens,
+                                     float* audio, void* stream) {
+    return oob_decode_common(ctx, latents, batch, latent_tokens, audio, stream, false);
 }
 
 }  // extern "C"

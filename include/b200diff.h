@@ -270,6 +270,34 @@ B2D_API b2d_status b2d_sa3_sample(b2d_ctx* ctx, const b2d_sa3_request* request, 
 B2D_API b2d_status b2d_sa3_sample_device(b2d_ctx* ctx, const b2d_sa3_request* request, float* out_latents,
                                          void* stream);
 
+/* --------------------------------------------- Stable Audio Oobleck VAE decode */
+/* The StableAudioConfig fields of the Oobleck decoder (include/engine/models/stable_audio/assets.h:14-84):
+ * decoder channels = channels x (1, c_mults[0..n_blocks)), all multiples of 64; latent_dim a multiple of 64. */
+typedef struct {
+    int64_t latent_dim;      /* 64 */
+    int64_t channels;        /* same_channels: 128 */
+    int64_t audio_channels;  /* 2 */
+    int32_t n_blocks;        /* len(same_strides) <= 8 */
+    int64_t c_mults[8];      /* same_c_mults: 1, 2, 4, 8, 16 */
+    int64_t strides[8];      /* same_strides: 2, 4, 4, 8, 8 */
+} b2d_oobleck_config;
+
+/* Loads the decoder half of load_oobleck_autoencoder_weights (src/models/stable_audio/foundation/
+ * oobleck_autoencoder.cpp:334-420): "pretransform.model.decoder.layers.*" weight_v / weight_g / bias and snake
+ * alpha / beta, weight norm folded on the host as the reference does. */
+B2D_API b2d_status b2d_oobleck_load(b2d_ctx* ctx, const b2d_oobleck_config* config, const b2d_tensor_view* tensors,
+                                    int32_t n_tensors);
+
+/* OobleckAutoencoderRuntime::decode (oobleck_autoencoder.cpp:600-705, 764-770): latents [batch, latent_dim,
+ * latent_tokens] (fp32, host) -> audio [batch, frames, audio_channels] (interleaved, as AudioBuffer::samples),
+ * frames = latent_tokens x prod(strides).  Every conv runs as an implicit GEMM on the tensor cores. */
+B2D_API b2d_status b2d_oobleck_decode(b2d_ctx* ctx, const float* latents, int64_t batch, int64_t latent_tokens,
+                                      float* audio, void* stream);
+
+/* Same with device pointers; asynchronous on `stream`. */
+B2D_API b2d_status b2d_oobleck_decode_device(b2d_ctx* ctx, const float* latents, int64_t batch,
+                                             int64_t latent_tokens, float* audio, void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
