@@ -325,6 +325,66 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
     return res
 
 
+OOBLECK_WORKLOAD = "oobleck_bench_sao_1x1024"
+
+
+def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
+    """Oobleck VAE decode at the SAO-1.0 shape: 1024 latents -> 2,097,152 stereo frames per rank (weak scaling).
+    Metric: decoded audio frames/s over all ranks."""
+    from oracle import synth
+    cfg = synth.OOBLECK_CONFIGS[OOBLECK_WORKLOAD]
+    w = synth.oobleck_weights(cfg)
+    dec = b2d.OobleckDecoder(ctx, cfg.latent_dim, cfg.channels, cfg.c_mults, cfg.strides, cfg.audio_channels,
+                             weights=[(n, 0, t.dims, t.data) for n, t in w.items()])
+    lat = synth.oobleck_inputs(synth.OobleckConfig(**{**cfg.__dict__, "seed": cfg.seed + rank}))["latents"].array()
+    frames = cfg.latent_tokens * int(np.prod(cfg.strides))
+    d_lat = torch.from_numpy(lat.copy()).cuda()
+    d_out = torch.empty((cfg.batch, frames, cfg.audio_channels), dtype=torch.float32, device="cuda")
+    h_lat = torch.from_numpy(lat.copy()).pin_memory()
+    h_out = torch.empty((cfg.batch, frames, cfg.audio_channels)).pin_memory()
+    st = torch.cuda.current_stream()
+    calls, warm = max(1, min(args.steps, 5)), 3
+    ms = timed(lambda: dec.decode_device(d_lat, d_out, stream=st.cuda_stream), calls, warm)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(lambda: dec.decode(h_lat, out=h_out, stream=st.cuda_stream), calls, 1)
+    # algorithmic FLOPs: 2 x output rows x Cout x taps x Cin per conv (transposed conv: 2 taps x s phases)
+    ch = [cfg.channels * m for m in (1,) + tuple(cfg.c_mults)]
+    L, fl = cfg.latent_tokens, 2.0 * cfg.latent_tokens * ch[-1] * 7 * cfg.latent_dim
+    for blk in range(len(cfg.strides), 0, -1):
+        s, cin, cout = cfg.strides[blk - 1], ch[blk], ch[blk - 1]
+        fl += 2.0 * L * s * cout * 2 * cin
+        L *= s
+        fl += 3 * (2.0 * L * cout * 7 * cout + 2.0 * L * cout * cout)
+    fl += 2.0 * L * cfg.audio_channels * 7 * ch[0]
+    fl *= cfg.batch
+    total = frames * cfg.batch * world
+    res = {"metric": "decoded audio frames/sec (Oobleck VAE)", "value": round(total / (ms / 1e3), 1),
+           "unit": "frames/s", "ms_per_call": round(ms, 3), "timed_calls": calls, "warmup_calls": warm,
+           "realtime_factor_44k1": round(total / (ms / 1e3) / 44100.0, 1),
+           "config": {"workload": OOBLECK_WORKLOAD, "model": "Stable-Audio-Open-1.0-shaped Oobleck decoder (random-init)",
+                      "latent_tokens": cfg.latent_tokens, "frames": frames, "channels": ch, "strides": cfg.strides,
+                      "n_gpus": world},
+           "dtype": "fp16 tensor-core operands, fp32 accumulate and residual stream",
+           "e2e": {"value": round(total / (ms_e2e / 1e3), 1), "unit": "frames/s",
+                   "h2d_bytes_per_step": h_lat.numel() * 4, "d2h_bytes_per_step": h_out.numel() * 4,
+                   "api": "b2d_oobleck_decode (host buffers, pinned)"},
+           "gpu_launches_per_call": 4 + 7 * len(cfg.strides),
+           "whole_call_tflops": round(fl / (ms / 1e3) / 1e12, 1)}
+    assert np.isfinite(h_out.numpy()).all()
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle import ref_runner
+        if ref_runner.available():
+            c1 = synth.OobleckConfig(**{**cfg.__dict__, "latent_tokens": 16})
+            o = ref_runner.run("oobleck", synth.oobleck_inputs(c1), w, reps=1)
+            cms = float(o["wall_ms"].data[0])
+            f1 = 16 * int(np.prod(cfg.strides))
+            res["cpu_baseline"] = {"value": round(f1 / (cms / 1e3), 1), "unit": "frames/s",
+                                   "cores": os.cpu_count(), "kind": "reference",
+                                   "sample": "16 of the 1024 latents (%d frames), audio.cpp ggml CPU (%s)"
+                                             % (f1, ref_runner.variant())}
+    return res
+
+
 def make_timer(torch, args, world, st):
     flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
 
@@ -369,6 +429,8 @@ def bench_dit_only(args, torch, b2d, world, rank, local):
         timer = make_timer(torch, args, world, st)
         if args.workload == "sa3":
             res = bench_sa3(args, torch, b2d, ctx, world, rank, timer)
+        elif args.workload == "oobleck":
+            res = bench_oobleck(args, torch, b2d, ctx, world, rank, timer)
         else:
             res = bench_dit(args, torch, b2d, ctx, world, rank, timer, peaks)
     if rank == 0:
@@ -391,7 +453,7 @@ def bench_ours(args):
     b2d = load_package()
     from oracle import synth  # seeded synthetic weights/inputs (no checkpoints here)
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
-    if args.workload in ("dit", "sa3"):
+    if args.workload in ("dit", "sa3", "oobleck"):
         return bench_dit_only(args, torch, b2d, world, rank, local)
     w = synth.head_weights(cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
@@ -477,9 +539,10 @@ def bench_ours(args):
     dit_res = None
     if args.workload in ("all", "dit"):
         dit_res = bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks)
-    sa3_res = None
+    sa3_res = oob_res = None
     if args.workload == "all":
         sa3_res = bench_sa3(args, torch, b2d, ctx, world, rank, timed)
+        oob_res = bench_oobleck(args, torch, b2d, ctx, world, rank, timed)
     if rank == 0:
         roof = gemm_roofline(b2d, ctx, torch, cfg, peaks)
         flops_call = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
@@ -506,6 +569,8 @@ def bench_ours(args):
             line["dit"] = dit_res
         if sa3_res is not None:
             line["sa3"] = sa3_res
+        if oob_res is not None:
+            line["oobleck"] = oob_res
         print(json.dumps(line))
     ctx.close()
     if world > 1:
@@ -519,9 +584,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="all", choices=["all", "head", "dit", "sa3"],
+    ap.add_argument("--workload", default="all", choices=["all", "head", "dit", "sa3", "oobleck"],
                     help="all = head line with the DiT and SA3 results attached; head = VibeVoice head only; "
-                         "dit / sa3 = only that DiT")
+                         "dit / sa3 / oobleck = only that path")
     ap.add_argument("--dit-steps", type=int, default=3, help="timed DiT sampling calls (each 100 DPM++ steps)")
     ap.add_argument("--dit-dpm-steps", type=int, default=0,
                     help="profiling only: DPM++ steps per DiT call instead of the workload's 100")

@@ -482,6 +482,10 @@ OOBLECK_CONFIGS = {
     "oobleck_tiny": OobleckConfig(),
     "oobleck_tiny_b2_odd": OobleckConfig(c_mults=(1, 2), strides=(3, 5), batch=2, latent_tokens=21, wseed=13,
                                          seed=14),
+    # bench: the Stable Audio Open 1.0 VAE shape (channels 128, c_mults 1 2 4 8 16, strides 2 4 4 8 8 -> 2048x
+    # upsampling), one 1024-latent generation (47.5 s of 44.1 kHz stereo)
+    "oobleck_bench_sao_1x1024": OobleckConfig(channels=128, c_mults=(1, 2, 4, 8, 16), strides=(2, 4, 4, 8, 8),
+                                              latent_tokens=1024, wseed=15, seed=16),
 }
 
 OP = "pretransform.model.decoder.layers."
