@@ -44,8 +44,11 @@ struct ConvParams {
     int* status;
 };
 
+// The sine goes to the SFU (__sinf): the epilogues evaluate one per output element (about 3 G per
+// SAO-shape decode), and the full-range sinf made them the critical path; the SFU result's absolute
+// error (a few 1e-6 for the |alpha x| of a decoder) is far below the fp16 rounding of the operands.
 __device__ __forceinline__ float snake_f(float x, float a, float ib) {
-    const float s = sinf(x * a);
+    const float s = __sinf(x * a);
     return x + s * s * ib;
 }
 
