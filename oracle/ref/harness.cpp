@@ -29,6 +29,7 @@
 #include "engine/models/vibevoice/diffusion_head.h"
 #include "engine/models/vibevoice/diffusion_sampler.h"
 #include "engine/models/vibevoice/scheduler.h"
+#include "engine/models/vibevoice/tokenizer_audio.h"
 
 #include "engine/framework/io/yaml.h"
 
@@ -526,6 +527,64 @@ int cmd_oobleck(const std::string & w, const std::string & in_path, const std::s
     return 0;
 }
 
+// ----------------------------------------------- VibeVoice acoustic decode
+// VibeVoiceTokenizerWeightsRuntime::decode_acoustic (src/models/vibevoice/tokenizer_audio.cpp:1855-1878): the
+// causal sigma-VAE decoder (stem conv, transposed-conv upsampling, ConvNeXt-style blocks with depthwise mixer and
+// GELU FFN, head conv); latents [frames, vae_dim] -> mono samples.  The loader also reads the acoustic and
+// semantic encoders, which the synthetic bundle carries.
+std::string yaml_free_depths(const std::vector<int64_t> & d) {
+    std::string out;
+    for (size_t i = 0; i < d.size(); ++i) out += (i ? "-" : "") + std::to_string(d[i]);
+    return out;
+}
+
+engine::models::vibevoice::VibeVoiceTokenizerConfig tok_config(const Bundle & in, const std::string & p) {
+    engine::models::vibevoice::VibeVoiceTokenizerConfig c;
+    c.channels = 1;
+    c.causal = true;
+    c.vae_dim = i64_scalar(in, p + "vae_dim");
+    c.mixer_layer = "depthwise_conv";
+    c.conv_norm = "none";
+    c.pad_mode = "constant";
+    c.disable_last_norm = i64_scalar(in, p + "disable_last_norm") != 0;
+    c.layernorm = "RMSNorm";
+    c.layernorm_eps = f32_scalar(in, p + "eps");
+    c.layernorm_elementwise_affine = true;
+    c.conv_bias = true;
+    c.layer_scale_init_value = 1.0e-6F;
+    c.encoder_n_filters = i64_scalar(in, p + "n_filters");
+    c.encoder_ratios = i64s(in, p + "ratios");
+    c.encoder_depths = yaml_free_depths(i64s(in, p + "depths"));
+    c.decoder_n_filters = c.encoder_n_filters;
+    c.decoder_ratios = c.encoder_ratios;
+    return c;
+}
+
+int cmd_vvdec(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+    namespace vv = engine::models::vibevoice;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<vv::VibeVoiceAssets>();
+    assets->config.acoustic_tokenizer = tok_config(in, "acoustic_");
+    assets->config.semantic_tokenizer = tok_config(in, "semantic_");
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
+    vv::VibeVoiceTokenizerWeightsRuntime rt(assets, engine::core::BackendType::Cpu, 0, threads);
+    vv::VibeVoiceTokenizerLatents lat;
+    lat.values = f32s(in, "latents");
+    lat.dim = assets->config.acoustic_tokenizer.vae_dim;
+    lat.frames = static_cast<int64_t>(lat.values.size()) / lat.dim;
+    std::vector<float> times, samples;
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        const double t0 = now_ms();
+        samples = rt.decode_acoustic(lat).samples;
+        times.push_back(static_cast<float>(now_ms() - t0));
+    }
+    Bundle out;
+    out["samples"] = f32_entry(samples, {static_cast<int64_t>(samples.size())});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
 // ------------------------------------------------------------- Philox randn
 // torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
 int cmd_randn(const std::string & in_path, const std::string & out_path) {
@@ -603,6 +662,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "vvdec") return cmd_vvdec(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "oobleck") return cmd_oobleck(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         std::fprintf(stderr, "unknown command %s\n", cmd.c_str());
         return 2;

@@ -550,3 +550,104 @@ def oobleck_inputs(cfg: OobleckConfig) -> Dict[str, B.Tensor]:
     d = cfg.scalars()
     d["latents"] = B.f32(_normal(np.random.default_rng(cfg.seed), (cfg.batch, cfg.latent_dim, cfg.latent_tokens)))
     return d
+
+
+@dataclass
+class VVDecConfig:
+    """VibeVoiceTokenizerConfig fields of the acoustic sigma-VAE (include/engine/models/vibevoice/assets.h:15-37):
+    decoder channels n_filters << (D - 1 - stage), decoder depths = reversed encoder depths, decoder ratios =
+    encoder ratios; plus the small semantic encoder the tokenizer loader also reads."""
+    vae_dim: int = 64
+    n_filters: int = 64
+    ratios: tuple = (2, 3)
+    depths: tuple = (1, 1, 2)          # encoder depths; the decoder runs them reversed
+    disable_last_norm: bool = True
+    eps: float = 1e-5
+    frames: int = 24
+    semantic_vae_dim: int = 32
+    wseed: int = 21
+    seed: int = 22
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        d = {}
+        for p, vd, nf, ratios, depths, dln in (("acoustic_", self.vae_dim, self.n_filters, self.ratios, self.depths,
+                                                 self.disable_last_norm),
+                                                ("semantic_", self.semantic_vae_dim, 32, (2,), (1, 1), True)):
+            d[p + "vae_dim"] = B.i64(vd)
+            d[p + "n_filters"] = B.i64(nf)
+            d[p + "ratios"] = B.i64(np.array(ratios, np.int64))
+            d[p + "depths"] = B.i64(np.array(depths, np.int64))
+            d[p + "disable_last_norm"] = B.i64(int(dln))
+            d[p + "eps"] = B.f32(self.eps)
+        return d
+
+
+VVDEC_CONFIGS = {
+    "vvdec_tiny": VVDecConfig(),
+    "vvdec_tiny_norm": VVDecConfig(ratios=(4, 2), depths=(2, 1, 1), disable_last_norm=False, frames=17, wseed=23,
+                                   seed=24),
+}
+
+
+def _tok_block(w, rng, p, c):
+    w[p + ".norm.weight"] = B.f32(1.0 + _normal(rng, (c,), 0.1))
+    w[p + ".mixer.conv.conv.conv.weight"] = B.f32(_normal(rng, (c, 1, 7), 0.3))
+    w[p + ".mixer.conv.conv.conv.bias"] = B.f32(_normal(rng, (c,), 0.02))
+    w[p + ".gamma"] = B.f32(_normal(rng, (c,), 0.3))
+    w[p + ".ffn_norm.weight"] = B.f32(1.0 + _normal(rng, (c,), 0.1))
+    w[p + ".ffn.linear1.weight"] = B.f32(_normal(rng, (4 * c, c), 1.0 / np.sqrt(c)))
+    w[p + ".ffn.linear1.bias"] = B.f32(_normal(rng, (4 * c,), 0.02))
+    w[p + ".ffn.linear2.weight"] = B.f32(_normal(rng, (c, 4 * c), 1.0 / np.sqrt(4 * c)))
+    w[p + ".ffn.linear2.bias"] = B.f32(_normal(rng, (c,), 0.02))
+    w[p + ".ffn_gamma"] = B.f32(_normal(rng, (c,), 0.3))
+
+
+def _tok_conv(w, rng, p, shape):
+    w[p + ".weight"] = B.f32(_normal(rng, shape, 1.0 / np.sqrt(shape[1] * shape[2]) if shape[1] > 1 else 0.3))
+    w[p + ".bias"] = B.f32(_normal(rng, (shape[0],), 0.02))
+
+
+def _tok_encoder(w, rng, prefix, vae_dim, nf, ratios, depths, last_norm):
+    rr = list(reversed(ratios))
+    _tok_conv(w, rng, prefix + ".downsample_layers.0.0.conv.conv", (nf, 1, 7))
+    for i, r in enumerate(rr):
+        _tok_conv(w, rng, prefix + ".downsample_layers.%d.0.conv.conv" % (i + 1), (nf << (i + 1), nf << i, 2 * r))
+    for s, dep in enumerate(depths):
+        for b in range(dep):
+            _tok_block(w, rng, prefix + ".stages.%d.%d" % (s, b), nf << s)
+    if last_norm:
+        w[prefix + ".norm.weight"] = B.f32(1.0 + _normal(rng, (nf << (len(depths) - 1),), 0.1))
+    _tok_conv(w, rng, prefix + ".head.conv.conv", (vae_dim, nf << (len(depths) - 1), 7))
+
+
+def vvdec_weights(cfg: VVDecConfig) -> Dict[str, B.Tensor]:
+    """Tensor names and shapes of load_vibevoice_tokenizer_weights (src/models/vibevoice/tokenizer_audio.cpp:
+    214-388, 1507-1542): acoustic encoder + decoder and semantic encoder, f32."""
+    rng = np.random.default_rng(cfg.wseed)
+    w: Dict[str, B.Tensor] = {}
+    D = len(cfg.depths)
+    dd = list(reversed(cfg.depths))
+    P = "model.acoustic_tokenizer.decoder"
+    _tok_conv(w, rng, P + ".upsample_layers.0.0.conv.conv", (cfg.n_filters << (D - 1), cfg.vae_dim, 7))
+    for i, r in enumerate(cfg.ratios):
+        cin, cout = cfg.n_filters << (D - 1 - i), cfg.n_filters << (D - 2 - i)
+        w[P + ".upsample_layers.%d.0.convtr.convtr.weight" % (i + 1)] = B.f32(
+            _normal(rng, (cin, cout, 2 * r), 1.0 / np.sqrt(cin * 2)))
+        w[P + ".upsample_layers.%d.0.convtr.convtr.bias" % (i + 1)] = B.f32(_normal(rng, (cout,), 0.02))
+    for s, dep in enumerate(dd):
+        for b in range(dep):
+            _tok_block(w, rng, P + ".stages.%d.%d" % (s, b), cfg.n_filters << (D - 1 - s))
+    if not cfg.disable_last_norm:
+        w[P + ".norm.weight"] = B.f32(1.0 + _normal(rng, (cfg.n_filters,), 0.1))
+    _tok_conv(w, rng, P + ".head.conv.conv", (1, cfg.n_filters, 7))
+    _tok_encoder(w, rng, "model.acoustic_tokenizer.encoder", cfg.vae_dim, cfg.n_filters, cfg.ratios, cfg.depths,
+                 not cfg.disable_last_norm)
+    _tok_encoder(w, rng, "model.semantic_tokenizer.encoder", cfg.semantic_vae_dim, 32, (2,), (1, 1), False)
+    return w
+
+
+def vvdec_inputs(cfg: VVDecConfig) -> Dict[str, B.Tensor]:
+    """Acoustic latents [frames, vae_dim] ~ N(0, 1) (VibeVoiceTokenizerLatents.values, time-major)."""
+    d = cfg.scalars()
+    d["latents"] = B.f32(_normal(np.random.default_rng(cfg.seed), (cfg.frames, cfg.vae_dim)))
+    return d

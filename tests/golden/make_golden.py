@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import dit, oobleck, ref_runner, sa3, synth, vibevoice  # noqa: E402
+from oracle import dit, oobleck, ref_runner, sa3, synth, vibevoice, vvdec  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -34,6 +34,7 @@ DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vd
                "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps"]
 SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
 OOBLECK_GOLDENS = [n for n in synth.OOBLECK_CONFIGS if "bench" not in n]
+VVDEC_GOLDENS = [n for n in synth.VVDEC_CONFIGS if "bench" not in n]
 
 
 def digest(*bundles) -> np.ndarray:
@@ -124,9 +125,20 @@ def oobleck_golden(name: str) -> None:
     print("oobleck", name, "ok", out["audio"].dims)
 
 
+def vvdec_golden(name: str) -> None:
+    """VibeVoice acoustic sigma-VAE decode (VibeVoiceTokenizerWeightsRuntime::decode_acoustic), tiny config."""
+    cfg = synth.VVDEC_CONFIGS[name]
+    w, inp = synth.vvdec_weights(cfg), synth.vvdec_inputs(cfg)
+    out = ref_runner.run("vvdec", inp, w)
+    B.write(os.path.join(HERE, "%s.b2db" % name),
+            {"samples": out["samples"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("vvdec", name, "ok", out["samples"].dims)
+
+
 def main(argv) -> None:
     names = argv or (["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS] +
-                     ["sa3:" + n for n in SA3_GOLDENS] + ["oobleck:" + n for n in OOBLECK_GOLDENS])
+                     ["sa3:" + n for n in SA3_GOLDENS] + ["oobleck:" + n for n in OOBLECK_GOLDENS] +
+                     ["vvdec:" + n for n in VVDEC_GOLDENS])
     for n in names:
         if n == "q8":
             q8_golden()
@@ -140,6 +152,8 @@ def main(argv) -> None:
             sa3_golden(n[4:])
         elif n.startswith("oobleck:"):
             oobleck_golden(n[8:])
+        elif n.startswith("vvdec:"):
+            vvdec_golden(n[6:])
         else:
             raise SystemExit("unknown fixture " + n)
 

@@ -162,3 +162,19 @@ def test_oobleck_port_vs_reference(name):
     assert mine.shape == ref.shape
     err = float(np.linalg.norm(mine - ref) / np.linalg.norm(ref))
     assert err < 1e-5, err
+
+
+@pytest.mark.parametrize("name", ["vvdec_tiny", "vvdec_tiny_norm"])
+def test_vvdec_port_vs_reference(name):
+    """The VibeVoice acoustic decoder restatement (oracle/vvdec.py) against
+    VibeVoiceTokenizerWeightsRuntime::decode_acoustic run by the reference's own CPU build (fp32 weights)."""
+    from oracle import synth, vvdec
+    cfg = synth.VVDEC_CONFIGS[name]
+    w, inp = synth.vvdec_weights(cfg), synth.vvdec_inputs(cfg)
+    g = golden(name)
+    assert np.array_equal(digest(w, inp), g["input_sha256"].data), "synthetic generator drifted"
+    ref = g["samples"].array()
+    mine = vvdec.AcousticDecoder(w, cfg).decode(inp["latents"].array())
+    assert mine.shape == ref.shape
+    err = float(np.linalg.norm(mine - ref) / np.linalg.norm(ref))
+    assert err < 1e-5, err
