@@ -31,7 +31,7 @@ EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_vers
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
             "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
-            "b2d_oobleck_decode_device"]
+            "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device"]
 
 
 class B2DError(RuntimeError):
@@ -94,6 +94,12 @@ class OobleckConfig(C.Structure):
                 ("n_blocks", C.c_int32), ("c_mults", C.c_int64 * 8), ("strides", C.c_int64 * 8)]
 
 
+class VvdecConfig(C.Structure):
+    _fields_ = [("vae_dim", C.c_int64), ("n_filters", C.c_int64), ("n_stages", C.c_int32),
+                ("ratios", C.c_int64 * 8), ("depths", C.c_int64 * 8), ("disable_last_norm", C.c_int32),
+                ("eps", C.c_float)]
+
+
 SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
 
 SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
@@ -138,6 +144,9 @@ def lib() -> C.CDLL:
         L.b2d_oobleck_load.argtypes = [P, C.POINTER(OobleckConfig), C.POINTER(TensorView), I32]
         L.b2d_oobleck_decode.argtypes = [P, P, I64, I64, P, P]
         L.b2d_oobleck_decode_device.argtypes = [P, P, I64, I64, P, P]
+        L.b2d_vvdec_load.argtypes = [P, C.POINTER(VvdecConfig), C.POINTER(TensorView), I32]
+        L.b2d_vvdec_decode.argtypes = [P, P, I64, P, P]
+        L.b2d_vvdec_decode_device.argtypes = [P, P, I64, P, P]
         _lib = L
     return _lib
 
@@ -387,6 +396,40 @@ class OobleckDecoder:
         b, _, t = latents.shape
         self.ctx.check(lib().b2d_oobleck_decode_device(self.ctx.handle, _ptr(latents), b, t, _ptr(out),
                                                        C.c_void_p(stream)))
+        return out
+
+
+class VibeVoiceAcousticDecoder:
+    """VibeVoiceTokenizerWeightsRuntime::decode_acoustic (include/engine/models/vibevoice/tokenizer_audio.h:94-140)
+    on a B200 context.  ``weights``: (name, ggml_type, dims, payload) with the names
+    ``model.acoustic_tokenizer.decoder.*``; ``depths`` in encoder order, ``ratios`` = decoder_ratios."""
+
+    def __init__(self, ctx: Context, vae_dim: int, n_filters: int, ratios, depths, disable_last_norm: bool = True,
+                 eps: float = 1e-5, weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = VvdecConfig(vae_dim, n_filters, len(depths))
+        for i, r in enumerate(ratios):
+            self.cfg.ratios[i] = r
+        for i, d in enumerate(depths):
+            self.cfg.depths[i] = d
+        self.cfg.disable_last_norm = int(bool(disable_last_norm))
+        self.cfg.eps = eps
+        self.hop = int(np.prod(ratios))
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_vvdec_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    def decode(self, latents, out=None, stream: int = 0):
+        """Host latents [frames, vae_dim] -> mono samples [frames x hop]."""
+        latents = np.ascontiguousarray(latents, np.float32) if isinstance(latents, np.ndarray) else latents
+        frames = latents.shape[0]
+        if out is None:
+            out = np.empty(frames * self.hop, np.float32)
+        self.ctx.check(lib().b2d_vvdec_decode(self.ctx.handle, _ptr(latents), frames, _ptr(out), C.c_void_p(stream)))
+        return out
+
+    def decode_device(self, latents, out, stream: int = 0):
+        self.ctx.check(lib().b2d_vvdec_decode_device(self.ctx.handle, _ptr(latents), latents.shape[0], _ptr(out),
+                                                     C.c_void_p(stream)))
         return out
 
 

@@ -317,6 +317,7 @@ struct HeadWorkspace {
 struct DitModel;
 struct Sa3Model;
 struct OobModel;
+struct VdModel;
 
 struct HeadModel {
     b2d_vv_head_config cfg{};
@@ -341,6 +342,7 @@ struct b2d_ctx {
     std::unique_ptr<DitModel> dit;
     std::unique_ptr<Sa3Model> sa3;
     std::unique_ptr<OobModel> oob;
+    std::unique_ptr<VdModel> vvdec;
 };
 
 namespace {
@@ -731,6 +733,7 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 #include "dit_runtime.inc"
 #include "sa3_runtime.inc"
 #include "oobleck_runtime.inc"
+#include "vvdec_runtime.inc"
 
 }  // namespace
 
@@ -774,6 +777,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         ctx->dit.reset();
         ctx->sa3.reset();
         ctx->oob.reset();
+        ctx->vvdec.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -1125,6 +1129,42 @@ b2d_status b2d_oobleck_decode(b2d_ctx* ctx, const float* latents, int64_t batch,
 b2d_status b2d_oobleck_decode_device(b2d_ctx* ctx, const float* latents, int64_t batch, int64_t latent_tokens,
                                      float* audio, void* stream) {
     return oob_decode_common(ctx, latents, batch, latent_tokens, audio, stream, false);
+}
+
+b2d_status b2d_vvdec_load(b2d_ctx* ctx, const b2d_vvdec_config* config, const b2d_tensor_view* tensors,
+                          int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "VibeVoice tokenizer weights runtime requires assets");
+        const b2d_vvdec_config& c = *config;
+        if (c.n_stages < 1 || c.n_stages > 8 || c.vae_dim <= 0 || c.vae_dim % 64 || c.n_filters <= 0 ||
+            c.n_filters % 64)
+            fail(B2D_EINVAL, "tokenizer decoder config: 1..8 stages, vae_dim and n_filters multiples of 64");
+        for (int i = 0; i < c.n_stages; ++i)
+            if (c.depths[i] <= 0 || (i + 1 < c.n_stages && c.ratios[i] <= 0))
+                fail(B2D_EINVAL, "tokenizer decoder config: depths / ratios must be positive");
+        auto m = std::make_unique<VdModel>();
+        m->cfg = c;
+        ctx->vvdec.reset();
+        vd_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->vvdec = std::move(m);
+    });
+}
+
+static b2d_status vd_decode_common(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples, void* stream,
+                                   bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->vvdec) fail(B2D_ESTATE, "VibeVoice acoustic decoder weights are not loaded");
+        vd_decode<__half>(ctx, latents, frames, samples, static_cast<cudaStream_t>(stream), host);
+    });
+}
+
+b2d_status b2d_vvdec_decode(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples, void* stream) {
+    return vd_decode_common(ctx, latents, frames, samples, stream, true);
+}
+
+b2d_status b2d_vvdec_decode_device(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples,
+                                   void* stream) {
+    return vd_decode_common(ctx, latents, frames, samples, stream, false);
 }
 
 }  // extern "C"

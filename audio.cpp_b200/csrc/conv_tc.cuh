@@ -23,6 +23,7 @@ enum ConvMode : int {
     kConvSnakeCt = 1,   // out_ct[row, n] = ct(snake(acc + bias[n]))
     kConvResid = 2,     // v = acc + bias[n] (+ out_f32 when accumulate); out_f32 = v; out_ct = ct(snake(v)) if given
     kConvUpsample = 3,  // transposed conv: column n = (phase, o); row q -> time q s + phase - crop; then as kConvResid
+    kConvGeluCt = 4,    // out_ct[row, n] = ct(gelu_erf(acc + bias[n]))
 };
 
 struct ConvParams {
@@ -41,6 +42,7 @@ struct ConvParams {
     const float* snake_ib;     // 1 / (exp(beta) + 1e-9)
     int stride, crop, cout;    // kConvUpsample
     int64_t out_rows_seq;      // kConvUpsample: output rows per sequence (input rows x stride)
+    const float* scale;        // kConvResid: per-column factor on (acc + bias) before the accumulate (or null)
     int* status;
 };
 
@@ -191,7 +193,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] += __ldg(cp.bias + ocol0 + j);
                 }
-                if (cp.mode != kConvSnakeCt) {
+                if (cp.mode == kConvResid && cp.scale) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] *= __ldg(cp.scale + ocol0 + j);
+                }
+                if (cp.mode == kConvGeluCt) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f));
+                }
+                if (cp.mode != kConvSnakeCt && cp.mode != kConvGeluCt) {
                     float4* o4 = reinterpret_cast<float4*>(cp.out_f32 + orow * cp.ld_f32 + ocol0);
                     if (cp.mode == kConvResid && cp.accumulate) {
 #pragma unroll
@@ -207,9 +217,11 @@ __global__ void __launch_bounds__(192, 1)
                     for (int q = 0; q < 8; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
                 }
                 if (cp.mode != kConvStoreF32 && cp.out_ct) {
+                    if (cp.snake_a) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = snake_f(v[j], __ldg(cp.snake_a + ocol0 + j), __ldg(cp.snake_ib + ocol0 + j));
+                        for (int j = 0; j < 32; ++j)
+                            v[j] = snake_f(v[j], __ldg(cp.snake_a + ocol0 + j), __ldg(cp.snake_ib + ocol0 + j));
+                    }
                     uint32_t packed[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) packed[j] = CtTraits<CT>::pack2(v[2 * j], v[2 * j + 1]);
@@ -254,6 +266,44 @@ __global__ void take_channels_kernel(const float* __restrict__ y, int64_t ld, in
         const float v = y[(i / ch) * ld + i % ch];
         if (!isfinite(v)) atomicCAS(status, 0, kErrNonFinite);
         audio[i] = v;
+    }
+}
+
+// VibeVoice tokenizer blocks (src/models/vibevoice/tokenizer_audio.cpp:679-740), time-major rows of C channels.
+// Per-row RMS scale 1 / sqrt(mean(x^2) + eps); with `out` also ct(x * scale * w).  One warp per row.
+template <typename CT>
+__global__ void __launch_bounds__(256) tok_rms_kernel(const float* __restrict__ x, int C, int64_t rows,
+                                                      const float* __restrict__ w, float eps,
+                                                      float* __restrict__ scale, CT* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float* xr = x + row * C;
+    float ss = 0.f;
+    for (int c = lane; c < C; c += 32) ss += xr[c] * xr[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float sc = 1.0f / sqrtf(ss / float(C) + eps);
+    if (scale && lane == 0) scale[row] = sc;
+    if (out)
+        for (int c = lane; c < C; c += 32) out[row * C + c] = from_f32<CT>(xr[c] * sc * __ldg(w + c));
+}
+
+// Block mixer: y[t, c] = x[t, c] + gamma[c] (b[c] + sum_k dw[c, k] rms(x)[t - K + 1 + k, c]), rms(x) = x * scale[t]
+// * nw[c], zeros before t = 0 (the causal depthwise conv).  Rows of one sequence; y must not alias x.
+__global__ void tok_mixer_kernel(const float* __restrict__ x, const float* __restrict__ scale, int C, int64_t rows,
+                                 const float* __restrict__ nw, const float* __restrict__ dw, int K,
+                                 const float* __restrict__ db, const float* __restrict__ gamma, float* __restrict__ y) {
+    const int64_t total = rows * C;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+        const int c = int(i % C);
+        const int64_t t = i / C;
+        float acc = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const int64_t tt = t - (K - 1) + k;
+            if (tt >= 0) acc += dw[c * K + k] * (x[tt * C + c] * scale[tt] * nw[c]);
+        }
+        y[i] = x[i] + gamma[c] * (acc + db[c]);
     }
 }
 

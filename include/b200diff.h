@@ -298,6 +298,32 @@ B2D_API b2d_status b2d_oobleck_decode(b2d_ctx* ctx, const float* latents, int64_
 B2D_API b2d_status b2d_oobleck_decode_device(b2d_ctx* ctx, const float* latents, int64_t batch,
                                              int64_t latent_tokens, float* audio, void* stream);
 
+/* ------------------------------------------ VibeVoice acoustic sigma-VAE decode */
+/* VibeVoiceTokenizerConfig fields of the acoustic tokenizer's decoder (include/engine/models/vibevoice/assets.h:
+ * 15-37): stage s has n_filters << (n_stages - 1 - s) channels (multiples of 64 on this path), the decoder runs
+ * the encoder depths reversed, and stage s > 0 is entered by a transposed conv with ratio ratios[s - 1]. */
+typedef struct {
+    int64_t vae_dim;            /* 64 */
+    int64_t n_filters;          /* decoder_n_filters */
+    int32_t n_stages;           /* len(depths) = len(ratios) + 1 */
+    int64_t ratios[8];          /* decoder_ratios */
+    int64_t depths[8];          /* encoder_depths (the decoder uses them reversed) */
+    int32_t disable_last_norm;
+    float eps;                  /* layernorm_eps */
+} b2d_vvdec_config;
+
+/* Loads "model.acoustic_tokenizer.decoder.*" (load_decoder, src/models/vibevoice/tokenizer_audio.cpp:322-388). */
+B2D_API b2d_status b2d_vvdec_load(b2d_ctx* ctx, const b2d_vvdec_config* config, const b2d_tensor_view* tensors,
+                                  int32_t n_tensors);
+
+/* VibeVoiceTokenizerWeightsRuntime::decode_acoustic (tokenizer_audio.cpp:1855-1878): latents [frames, vae_dim]
+ * (time-major, host) -> mono samples [frames x prod(ratios)].  Convs and FFN linears on the tensor cores. */
+B2D_API b2d_status b2d_vvdec_decode(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples, void* stream);
+
+/* Same with device pointers; asynchronous on `stream`. */
+B2D_API b2d_status b2d_vvdec_decode_device(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples,
+                                           void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
