@@ -320,3 +320,83 @@ std::vector<float> FoundationRfDitRuntime::sample(const StableAudioSamplingState
 }
 
 }  // namespace engine::models::stable_audio::foundation
+
+namespace engine::models::vibevoice {
+
+VibeVoiceTokenizerWeightsRuntime::VibeVoiceTokenizerWeightsRuntime(const VibeVoiceTokenizerConfig & acoustic,
+                                                                   const std::vector<engine::b200::RawTensor> & tensors,
+                                                                   int device)
+    : config_(acoustic), device_(std::make_unique<engine::b200::Device>(device)) {
+    if (acoustic.encoder_depths.empty() || acoustic.encoder_depths.size() != acoustic.decoder_ratios.size() + 1 ||
+        acoustic.encoder_depths.size() > 8)
+        throw std::runtime_error("VibeVoice tokenizer decoder depths/ratios mismatch");
+    b2d_vvdec_config c{};
+    c.vae_dim = acoustic.vae_dim;
+    c.n_filters = acoustic.decoder_n_filters;
+    c.n_stages = static_cast<int32_t>(acoustic.encoder_depths.size());
+    for (size_t i = 0; i < acoustic.decoder_ratios.size(); ++i) c.ratios[i] = acoustic.decoder_ratios[i];
+    for (size_t i = 0; i < acoustic.encoder_depths.size(); ++i) c.depths[i] = acoustic.encoder_depths[i];
+    c.disable_last_norm = acoustic.disable_last_norm ? 1 : 0;
+    c.eps = acoustic.layernorm_eps;
+    const auto views = engine::b200::views_of(tensors);
+    device_->check(b2d_vvdec_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+// Validation and messages as decode_acoustic (src/models/vibevoice/tokenizer_audio.cpp:1855-1878).
+AudioBuffer VibeVoiceTokenizerWeightsRuntime::decode_acoustic(const VibeVoiceTokenizerLatents & latents) const {
+    if (latents.frames <= 0 || latents.dim != config_.vae_dim)
+        throw std::runtime_error("VibeVoice acoustic decoder received invalid latent shape");
+    if (static_cast<int64_t>(latents.values.size()) != latents.frames * latents.dim)
+        throw std::runtime_error("VibeVoice acoustic decoder latent payload size mismatch");
+    int64_t hop = 1;
+    for (const int64_t r : config_.decoder_ratios) hop *= r;
+    AudioBuffer out{24000, 1, std::vector<float>(static_cast<size_t>(latents.frames * hop))};
+    device_->check(b2d_vvdec_decode(device_->ctx(), latents.values.data(), latents.frames, out.samples.data(), nullptr));
+    return out;
+}
+
+}  // namespace engine::models::vibevoice
+
+namespace engine::models::stable_audio::foundation {
+
+OobleckAutoencoderRuntime::OobleckAutoencoderRuntime(const OobleckConfig & config,
+                                                     const std::vector<engine::b200::RawTensor> & tensors, int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    if (config.same_strides.empty() || config.same_strides.size() > 8 ||
+        config.same_c_mults.size() != config.same_strides.size())
+        throw std::runtime_error("Stable Audio Foundation Oobleck c_mults / strides mismatch");
+    b2d_oobleck_config c{};
+    c.latent_dim = config.latent_dim;
+    c.channels = config.same_channels;
+    c.audio_channels = config.audio_channels;
+    c.n_blocks = static_cast<int32_t>(config.same_strides.size());
+    for (size_t i = 0; i < config.same_strides.size(); ++i) {
+        c.c_mults[i] = config.same_c_mults[i];
+        c.strides[i] = config.same_strides[i];
+    }
+    const auto views = engine::b200::views_of(tensors);
+    device_->check(b2d_oobleck_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+// Validation and messages as DecodeGraph::decode (src/models/stable_audio/foundation/oobleck_autoencoder.cpp:600-640).
+std::vector<engine::models::vibevoice::AudioBuffer> OobleckAutoencoderRuntime::decode(const std::vector<float> & latents,
+                                                                                      int64_t batch,
+                                                                                      int64_t latent_tokens) const {
+    if (batch <= 0 || latent_tokens <= 0 ||
+        static_cast<int64_t>(latents.size()) != batch * config_.latent_dim * latent_tokens)
+        throw std::runtime_error("Stable Audio Foundation Oobleck latent shape mismatch");
+    int64_t hop = 1;
+    for (const int64_t s : config_.same_strides) hop *= s;
+    const int64_t frames = latent_tokens * hop;
+    std::vector<float> audio(static_cast<size_t>(batch * frames * config_.audio_channels));
+    device_->check(b2d_oobleck_decode(device_->ctx(), latents.data(), batch, latent_tokens, audio.data(), nullptr));
+    std::vector<engine::models::vibevoice::AudioBuffer> out;
+    const size_t per = static_cast<size_t>(frames * config_.audio_channels);
+    for (int64_t b = 0; b < batch; ++b)
+        out.push_back({config_.sample_rate, config_.audio_channels,
+                       std::vector<float>(audio.begin() + static_cast<std::ptrdiff_t>(b * per),
+                                          audio.begin() + static_cast<std::ptrdiff_t>((b + 1) * per))});
+    return out;
+}
+
+}  // namespace engine::models::stable_audio::foundation

@@ -8,6 +8,8 @@
 //   engine::models::vibevoice::sample_vibevoice_speech_latents       include/engine/models/vibevoice/diffusion_sampler.h:23-26
 //   engine::models::stable_audio::foundation::FoundationRfDitRuntime include/engine/models/stable_audio/foundation/rf_dit.h:73-106
 //   engine::models::stable_audio::StableAudioRfDitRuntime            include/engine/models/stable_audio/rf_dit.h:78-100
+//   engine::models::stable_audio::foundation::OobleckAutoencoderRuntime (decode) include/engine/models/stable_audio/foundation/oobleck_autoencoder.h:71-96
+//   engine::models::vibevoice::VibeVoiceTokenizerWeightsRuntime (decode_acoustic) include/engine/models/vibevoice/tokenizer_audio.h:94-140
 #pragma once
 
 #include <cstdint>
@@ -124,6 +126,34 @@ struct VibeVoiceSpeechDiffusionInput {
     float guidance_scale = 1.0F;
 };
 
+// VibeVoiceTokenizerConfig fields the acoustic decoder uses (include/engine/models/vibevoice/assets.h:15-37).
+struct VibeVoiceTokenizerConfig {
+    int64_t vae_dim = 64;
+    int64_t decoder_n_filters = 32;
+    std::vector<int64_t> decoder_ratios;
+    std::vector<int64_t> encoder_depths;  // the decoder runs them reversed (decoder_depths unset)
+    bool disable_last_norm = true;
+    float layernorm_eps = 1.0e-5F;
+};
+
+struct AudioBuffer {
+    int sample_rate = 0;
+    int channels = 0;
+    std::vector<float> samples;  // interleaved frames x channels
+};
+
+// The acoustic decode of VibeVoiceTokenizerWeightsRuntime on the GPU (b2d_vvdec_*).
+class VibeVoiceTokenizerWeightsRuntime final {
+public:
+    VibeVoiceTokenizerWeightsRuntime(const VibeVoiceTokenizerConfig & acoustic,
+                                     const std::vector<engine::b200::RawTensor> & tensors, int device);
+    AudioBuffer decode_acoustic(const VibeVoiceTokenizerLatents & latents) const;
+
+private:
+    VibeVoiceTokenizerConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
+};
+
 std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
     const VibeVoiceDiffusionHeadWeightsRuntime & prediction_head, VibeVoiceDPMSolverScheduler & scheduler,
     const VibeVoiceSpeechDiffusionInput & input);
@@ -204,6 +234,29 @@ private:
 };
 
 namespace foundation {
+
+// The Oobleck VAE fields of StableAudioConfig (include/engine/models/stable_audio/assets.h:14-84).
+struct OobleckConfig {
+    int64_t latent_dim = 64;
+    int64_t same_channels = 128;
+    std::vector<int64_t> same_c_mults;
+    std::vector<int64_t> same_strides;
+    int audio_channels = 2;
+    int sample_rate = 44100;
+};
+
+// OobleckAutoencoderRuntime's decode on the GPU (b2d_oobleck_*); audio per prompt as interleaved samples.
+class OobleckAutoencoderRuntime {
+public:
+    OobleckAutoencoderRuntime(const OobleckConfig & config, const std::vector<engine::b200::RawTensor> & tensors,
+                              int device);
+    std::vector<engine::models::vibevoice::AudioBuffer> decode(const std::vector<float> & latents, int64_t batch,
+                                                               int64_t latent_tokens) const;
+
+private:
+    OobleckConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
+};
 
 class FoundationRfDitRuntime {
 public:
