@@ -23,6 +23,7 @@
 #include "engine/framework/assets/tensor_source.h"
 #include "engine/framework/core/execution_context.h"
 #include "engine/framework/sampling/torch_random.h"
+#include "engine/models/stable_audio/foundation/conditioner.h"
 #include "engine/models/stable_audio/foundation/oobleck_autoencoder.h"
 #include "engine/models/stable_audio/foundation/rf_dit.h"
 #include "engine/models/stable_audio/rf_dit.h"
@@ -585,6 +586,84 @@ int cmd_vvdec(const std::string & w, const std::string & in_path, const std::str
     return 0;
 }
 
+// ------------------------------------------------ SAO 1.0 conditioner (T5)
+// FoundationConditionerRuntime::encode (src/models/stable_audio/foundation/conditioner.cpp:411-471): T5-base
+// encoder over the prompt tokens (relative position buckets, additive padding mask, ReLU FFN), cross tokens =
+// T5 states of the kept tokens + the seconds_start / seconds_total number embeddings, global = both embeddings.
+// The T5 and the number-conditioner tensors come from one bundle.
+int cmd_saocond(const std::string & w, const std::string & in_path, const std::string & out_path, int threads,
+                int reps) {
+    namespace sa = engine::models::stable_audio;
+    namespace sf = engine::models::stable_audio::foundation;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<sa::StableAudioAssets>();
+    auto & c = assets->config;
+    c.t5_hidden_size = i64_scalar(in, "t5_hidden_size");
+    c.t5_layers = i64_scalar(in, "t5_layers");
+    c.t5_attention_heads = i64_scalar(in, "t5_heads");
+    c.t5_head_dim = i64_scalar(in, "t5_head_dim");
+    c.t5_intermediate_size = i64_scalar(in, "t5_intermediate");
+    c.t5_vocab_size = i64_scalar(in, "t5_vocab");
+    c.t5_rms_norm_eps = f32_scalar(in, "t5_eps");
+    c.t5_pad_token_id = 0;
+    c.prompt_max_length = i64_scalar(in, "prompt_max_length");
+    c.cond_dim = c.t5_hidden_size;
+    c.cond_token_dim = c.cond_dim;
+    c.global_cond_dim = 2 * c.cond_dim;
+    auto src = std::make_shared<BundleTensorSource>(read_bundle(w));
+    assets->model_weights = src;
+    assets->t5_weights = src;
+    const int64_t batch = i64_scalar(in, "batch");
+    auto tokens = [&](const std::string & ids, const std::string & mask) {
+        sa::StableAudioTokenBatch t;
+        t.batch = batch;
+        t.tokens = c.prompt_max_length;
+        for (const int64_t v : i64s(in, ids)) t.input_ids.push_back(static_cast<int32_t>(v));
+        for (const int64_t v : i64s(in, mask)) t.attention_mask.push_back(static_cast<uint8_t>(v != 0));
+        return t;
+    };
+    const bool neg = i64_scalar(in, "has_negative") != 0;
+    const auto seconds = f32s(in, "normalized_seconds");
+    // On the CPU backend a FoundationConditionerRuntime computes its T5 graph correctly only once: a second
+    // encode on the same runtime trips ggml-cpu's get_rows bounds assert (the relative-bucket input is not
+    // rewritten between runs).  So every encode here runs on its own runtime; for the negative prompt that is
+    // exactly encode_one on the negative tokens (conditioner.cpp:414-418).
+    auto encode_fresh = [&](const std::string & ids, const std::string & mask, double & ms) {
+        sa::StableAudioConditioningBatch b;
+        b.prompt_tokens = tokens(ids, mask);
+        b.normalized_seconds = seconds;
+        engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+        sf::FoundationConditionerRuntime rt(exec, assets, engine::assets::TensorStorageType::Native, batch);
+        rt.prepare();
+        const double t0 = now_ms();
+        auto r = rt.encode(b);
+        ms = now_ms() - t0;
+        return r.positive;
+    };
+    std::vector<float> times;
+    sa::StableAudioConditioningInputs res;
+    for (int r = 0; r < std::max(reps, 1); ++r) {
+        double ms = 0.0;
+        res.positive = encode_fresh("input_ids", "attention_mask", ms);
+        times.push_back(static_cast<float>(ms));
+    }
+    if (neg) {
+        double ms = 0.0;
+        res.negative = encode_fresh("negative_ids", "negative_mask", ms);
+        res.has_negative = true;
+    }
+    Bundle out;
+    const int64_t P2 = c.prompt_max_length + 2;
+    out["cross_positive"] = f32_entry(res.positive.cross_attention, {batch, P2, c.cond_dim});
+    out["global"] = f32_entry(res.positive.global, {batch, c.global_cond_dim});
+    std::vector<float> mk(res.positive.cross_attention_mask.begin(), res.positive.cross_attention_mask.end());
+    out["cross_mask"] = f32_entry(mk, {batch, P2});
+    if (res.has_negative) out["cross_negative"] = f32_entry(res.negative.cross_attention, {batch, P2, c.cond_dim});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
 // ------------------------------------------------------------- Philox randn
 // torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
 int cmd_randn(const std::string & in_path, const std::string & out_path) {
@@ -662,6 +741,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "saocond") return cmd_saocond(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "vvdec") return cmd_vvdec(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "oobleck") return cmd_oobleck(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         std::fprintf(stderr, "unknown command %s\n", cmd.c_str());

@@ -651,3 +651,78 @@ def vvdec_inputs(cfg: VVDecConfig) -> Dict[str, B.Tensor]:
     d = cfg.scalars()
     d["latents"] = B.f32(_normal(np.random.default_rng(cfg.seed), (cfg.frames, cfg.vae_dim)))
     return d
+
+
+@dataclass
+class SaoCondConfig:
+    """StableAudioConfig T5 fields (include/engine/models/stable_audio/assets.h:14-84) of the SAO 1.0
+    conditioner, and one seeded token batch (ids, padding masks, normalized seconds_total)."""
+    hidden: int = 128
+    layers: int = 2
+    heads: int = 2
+    head_dim: int = 64
+    intermediate: int = 256
+    vocab: int = 200
+    eps: float = 1e-6
+    prompt_max_length: int = 12
+    batch: int = 2
+    has_negative: bool = True
+    wseed: int = 31
+    seed: int = 32
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        d = {"t5_" + k: B.i64(getattr(self, a)) for k, a in (
+            ("hidden_size", "hidden"), ("layers", "layers"), ("heads", "heads"), ("head_dim", "head_dim"),
+            ("intermediate", "intermediate"), ("vocab", "vocab"))}
+        d["t5_eps"] = B.f32(self.eps)
+        d["prompt_max_length"] = B.i64(self.prompt_max_length)
+        d["batch"] = B.i64(self.batch)
+        d["has_negative"] = B.i64(int(self.has_negative))
+        return d
+
+
+SAOCOND_CONFIGS = {
+    "saocond_tiny": SaoCondConfig(),
+    "saocond_tiny_b1_noneg": SaoCondConfig(layers=1, heads=4, head_dim=32, prompt_max_length=40, batch=1,
+                                           has_negative=False, wseed=33, seed=34),
+}
+
+
+def saocond_weights(cfg: SaoCondConfig) -> Dict[str, B.Tensor]:
+    """T5-base encoder tensors (load_t5_base_runtime_weights, conditioner.cpp:52-112, 202-233) and the two number
+    conditioners (load_number_conditioner :165-175), f32."""
+    rng = np.random.default_rng(cfg.wseed)
+    d, I, H = cfg.hidden, cfg.intermediate, cfg.heads * cfg.head_dim
+    w: Dict[str, B.Tensor] = {"shared.weight": B.f32(_normal(rng, (cfg.vocab, d)))}
+    w["encoder.block.0.layer.0.SelfAttention.relative_attention_bias.weight"] = B.f32(_normal(rng, (32, cfg.heads)))
+    for l in range(cfg.layers):
+        p = "encoder.block.%d.layer." % l
+        w[p + "0.layer_norm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+        w[p + "1.layer_norm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+        for n in "qkv":
+            w[p + "0.SelfAttention.%s.weight" % n] = B.f32(_normal(rng, (H, d), 1.0 / np.sqrt(d)))
+        w[p + "0.SelfAttention.o.weight"] = B.f32(_normal(rng, (d, H), 1.0 / np.sqrt(H)))
+        w[p + "1.DenseReluDense.wi.weight"] = B.f32(_normal(rng, (I, d), 1.0 / np.sqrt(d)))
+        w[p + "1.DenseReluDense.wo.weight"] = B.f32(_normal(rng, (d, I), 1.0 / np.sqrt(I)))
+    w["encoder.final_layer_norm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+    for n in ("seconds_start", "seconds_total"):
+        p = "conditioner.conditioners.%s.embedder.embedding." % n
+        w[p + "0.weights"] = B.f32(_normal(rng, (128,)))
+        w[p + "1.weight"] = B.f32(_normal(rng, (d, 257), 1.0 / np.sqrt(257)))
+        w[p + "1.bias"] = B.f32(_normal(rng, (d,), 0.02))
+    return w
+
+
+def saocond_inputs(cfg: SaoCondConfig) -> Dict[str, B.Tensor]:
+    """Token ids in [1, vocab), padding after a per-prompt length, normalized seconds_total in (0, 1)."""
+    rng = np.random.default_rng(cfg.seed)
+    P = cfg.prompt_max_length
+    d = cfg.scalars()
+    for ids, mask in (("input_ids", "attention_mask"), ("negative_ids", "negative_mask")):
+        lens = rng.integers(1, P + 1, cfg.batch)
+        ids_a = rng.integers(1, cfg.vocab, (cfg.batch, P))
+        m = (np.arange(P)[None, :] < lens[:, None]).astype(np.int64)
+        d[ids] = B.i64(ids_a * m)
+        d[mask] = B.i64(m)
+    d["normalized_seconds"] = B.f32(rng.random(cfg.batch).astype(np.float32))
+    return d

@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import dit, oobleck, ref_runner, sa3, synth, vibevoice, vvdec  # noqa: E402
+from oracle import dit, oobleck, ref_runner, sa3, saocond, synth, vibevoice, vvdec  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -35,6 +35,7 @@ DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vd
 SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
 OOBLECK_GOLDENS = [n for n in synth.OOBLECK_CONFIGS if "bench" not in n]
 VVDEC_GOLDENS = [n for n in synth.VVDEC_CONFIGS if "bench" not in n]
+SAOCOND_GOLDENS = list(synth.SAOCOND_CONFIGS)
 
 
 def digest(*bundles) -> np.ndarray:
@@ -135,10 +136,21 @@ def vvdec_golden(name: str) -> None:
     print("vvdec", name, "ok", out["samples"].dims)
 
 
+def saocond_golden(name: str) -> None:
+    """SAO 1.0 conditioner (FoundationConditionerRuntime::encode: T5-base + number conditioners), tiny config."""
+    cfg = synth.SAOCOND_CONFIGS[name]
+    w, inp = synth.saocond_weights(cfg), synth.saocond_inputs(cfg)
+    out = ref_runner.run("saocond", inp, w)
+    keep = {k: v for k, v in out.items() if k != "wall_ms"}
+    keep["input_sha256"] = B.Tensor(B.U8, (32,), digest(w, inp))
+    B.write(os.path.join(HERE, "%s.b2db" % name), keep)
+    print("saocond", name, "ok", out["cross_positive"].dims)
+
+
 def main(argv) -> None:
     names = argv or (["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS] +
                      ["sa3:" + n for n in SA3_GOLDENS] + ["oobleck:" + n for n in OOBLECK_GOLDENS] +
-                     ["vvdec:" + n for n in VVDEC_GOLDENS])
+                     ["vvdec:" + n for n in VVDEC_GOLDENS] + ["saocond:" + n for n in SAOCOND_GOLDENS])
     for n in names:
         if n == "q8":
             q8_golden()
@@ -154,6 +166,8 @@ def main(argv) -> None:
             oobleck_golden(n[8:])
         elif n.startswith("vvdec:"):
             vvdec_golden(n[6:])
+        elif n.startswith("saocond:"):
+            saocond_golden(n[8:])
         else:
             raise SystemExit("unknown fixture " + n)
 

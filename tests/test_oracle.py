@@ -178,3 +178,28 @@ def test_vvdec_port_vs_reference(name):
     assert mine.shape == ref.shape
     err = float(np.linalg.norm(mine - ref) / np.linalg.norm(ref))
     assert err < 1e-5, err
+
+
+@pytest.mark.parametrize("name", ["saocond_tiny", "saocond_tiny_b1_noneg"])
+def test_saocond_port_vs_reference(name):
+    """The SAO 1.0 conditioner restatement (oracle/saocond.py: T5-base encoder with relative position buckets and
+    padding mask, number conditioners, cross / global assembly) against FoundationConditionerRuntime::encode run by
+    the reference's own CPU build (fp32 weights)."""
+    from oracle import saocond, synth
+    cfg = synth.SAOCOND_CONFIGS[name]
+    w, inp = synth.saocond_weights(cfg), synth.saocond_inputs(cfg)
+    g = golden(name)
+    assert np.array_equal(digest(w, inp), g["input_sha256"].data), "synthetic generator drifted"
+    c = saocond.Conditioner(w, cfg)
+    secs = inp["normalized_seconds"].array()
+    cross, cmask, glob = c.encode_one(inp["input_ids"].array(), inp["attention_mask"].array(), secs)
+    rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))  # noqa: E731
+    assert rel(cross, g["cross_positive"].array()) < 1e-5
+    assert rel(glob, g["global"].array()) < 1e-5
+    assert np.array_equal(cmask, g["cross_mask"].array())
+    if cfg.has_negative:
+        neg, _, _ = c.encode_one(inp["negative_ids"].array(), inp["negative_mask"].array(), secs)
+        assert rel(neg, g["cross_negative"].array()) < 1e-5
+    # the bucket table's known values (T5's bidirectional scheme): 0 on the diagonal, 16 + d for small k > q
+    b = saocond.relative_buckets(40)
+    assert b[5, 5] == 0 and b[5, 6] == 17 and b[6, 5] == 1 and b.max() <= 31
