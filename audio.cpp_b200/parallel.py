@@ -40,6 +40,15 @@ def shard_prompts(arrays, batch: int, world: int, rank: int):
     return [a[lo:hi] for a in arrays], (lo, hi)
 
 
+def shard_prompts_rng(arrays, batch: int, world: int, rank: int):
+    """Prompts [lo, hi) of one batched DiT request, plus the ``rng_batch=(lo, batch)`` slice that makes this
+    shard's per-step noise (DPM++ 3M SDE, SA3 pingpong) the batched call's own draw: torch's TensorIterator
+    Philox layout depends on the total element count, so a shard that sampled on its own would draw a
+    different stream (b2d_dit_request / b2d_sa3_request ``rng_batch_total`` / ``rng_batch_first``)."""
+    local, (lo, hi) = shard_prompts(arrays, batch, world, rank)
+    return local, (lo, hi), (lo, batch)
+
+
 def gather_rows(local, n_total: int, world: int):
     """All ranks' row blocks (contiguous shard_range order) -> the full [n_total, ...] tensor on every rank.
 

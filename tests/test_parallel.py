@@ -99,3 +99,19 @@ def test_failed_rank_is_reported_on_host():
     assert res[1][0] == "error" and "injected failure" in res[1][1]
     # the surviving rank's gather ends with an error (peer gone / timeout), not a hang
     assert res[0][0] == "error"
+
+
+def test_prompt_shards_carry_the_batched_noise_slice():
+    """Each rank's rng_batch slice starts at its first prompt and names the whole batch, and the slices tile the
+    batch in rank order (the device side, shards == the batched call, is test_gpu_dit / test_gpu_sa3's)."""
+    par = _parallel()
+    batch, T = 5, 7
+    noise = np.arange(batch * 64 * T, dtype=np.float32).reshape(batch, 64, T)
+    for world in (1, 2, 3):
+        covered = []
+        for rank in range(world):
+            (local,), (lo, hi), (first, total) = par.shard_prompts_rng([noise], batch, world, rank)
+            assert first == lo and total == batch and local.shape[0] == hi - lo
+            assert np.array_equal(local, noise[lo:hi])
+            covered += list(range(lo, hi))
+        assert covered == list(range(batch))
