@@ -27,6 +27,7 @@
 #include "engine/models/stable_audio/foundation/oobleck_autoencoder.h"
 #include "engine/models/stable_audio/foundation/rf_dit.h"
 #include "engine/models/stable_audio/rf_dit.h"
+#include "engine/models/vibevoice/decoder.h"
 #include "engine/models/vibevoice/diffusion_head.h"
 #include "engine/models/vibevoice/diffusion_sampler.h"
 #include "engine/models/vibevoice/scheduler.h"
@@ -664,6 +665,60 @@ int cmd_saocond(const std::string & w, const std::string & in_path, const std::s
     return 0;
 }
 
+// ------------------------------------------------- VibeVoice LM (Qwen2.5)
+// VibeVoiceDecoderWeightsRuntime (src/models/vibevoice/decoder.cpp): prefill of `prefill` input embeddings, then
+// `steps` cached single-token steps (each fed the embedding of a given token id); logits and last hidden of the
+// prefill's final position and of every step.
+int cmd_vvlm(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+    namespace vv = engine::models::vibevoice;
+    const Bundle in = read_bundle(in_path);
+    auto assets = std::make_shared<vv::VibeVoiceAssets>();
+    auto & c = assets->config.decoder;
+    c.hidden_size = i64_scalar(in, "hidden_size");
+    c.intermediate_size = i64_scalar(in, "intermediate_size");
+    c.num_attention_heads = i64_scalar(in, "num_heads");
+    c.num_key_value_heads = i64_scalar(in, "num_kv_heads");
+    c.num_hidden_layers = i64_scalar(in, "num_layers");
+    c.vocab_size = i64_scalar(in, "vocab_size");
+    c.head_dim = i64_scalar(in, "head_dim");
+    c.max_position_embeddings = i64_scalar(in, "max_positions");
+    c.rms_norm_eps = f32_scalar(in, "rms_norm_eps");
+    c.rope_theta = f32_scalar(in, "rope_theta");
+    c.tie_word_embeddings = true;
+    assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
+    vv::VibeVoiceDecoderWeightsRuntime lm(assets, engine::core::BackendType::Cpu, 0, threads);
+    const int64_t prefill = i64_scalar(in, "prefill");
+    std::vector<int32_t> ids;
+    for (const int64_t v : i64s(in, "prefill_ids")) ids.push_back(static_cast<int32_t>(v));
+    std::vector<int32_t> step_ids;
+    for (const int64_t v : i64s(in, "step_ids")) step_ids.push_back(static_cast<int32_t>(v));
+    std::vector<float> logits, hidden, times;
+    const double t0 = now_ms();
+    const auto emb = lm.embed_tokens(ids);
+    auto pre = lm.prefill_embeddings(emb.values, prefill);
+    times.push_back(static_cast<float>(now_ms() - t0));
+    logits = pre.result.logits.values;
+    hidden = pre.result.last_hidden.values;
+    vv::VibeVoiceDecoderCachedState state;
+    lm.reset_cached_state(state, std::move(pre.state));
+    for (const int32_t id : step_ids) {
+        const auto e = lm.embed_tokens({id});
+        const double t1 = now_ms();
+        const auto r = lm.cached_step(e.values, state, prefill + static_cast<int64_t>(step_ids.size()));
+        times.push_back(static_cast<float>(now_ms() - t1));
+        logits.insert(logits.end(), r.logits.values.begin(), r.logits.values.end());
+        hidden.insert(hidden.end(), r.last_hidden.values.begin(), r.last_hidden.values.end());
+    }
+    (void)reps;
+    const int64_t n = 1 + static_cast<int64_t>(step_ids.size());
+    Bundle out;
+    out["logits"] = f32_entry(logits, {n, c.vocab_size});
+    out["last_hidden"] = f32_entry(hidden, {n, c.hidden_size});
+    out["wall_ms"] = f32_entry(times, {static_cast<int64_t>(times.size())});
+    write_bundle(out_path, out);
+    return 0;
+}
+
 // ------------------------------------------------------------- Philox randn
 // torch-CUDA compatible normals (src/framework/sampling/torch_random.cpp)
 int cmd_randn(const std::string & in_path, const std::string & out_path) {
@@ -741,6 +796,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "vvlm") return cmd_vvlm(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "saocond") return cmd_saocond(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "vvdec") return cmd_vvdec(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "oobleck") return cmd_oobleck(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));

@@ -726,3 +726,69 @@ def saocond_inputs(cfg: SaoCondConfig) -> Dict[str, B.Tensor]:
         d[mask] = B.i64(m)
     d["normalized_seconds"] = B.f32(rng.random(cfg.batch).astype(np.float32))
     return d
+
+
+@dataclass
+class VVLmConfig:
+    """VibeVoiceDecoderConfig fields (include/engine/models/vibevoice/assets.h:39-54) of the Qwen2.5 LM that
+    produces the diffusion head's conditions, and one prefill + cached-step request."""
+    hidden: int = 128
+    intermediate: int = 256
+    heads: int = 4
+    kv_heads: int = 2
+    head_dim: int = 32
+    layers: int = 2
+    vocab: int = 300
+    max_positions: int = 256
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    prefill: int = 9
+    steps: int = 3
+    wseed: int = 41
+    seed: int = 42
+
+    def scalars(self) -> Dict[str, B.Tensor]:
+        d = {k: B.i64(getattr(self, a)) for k, a in (
+            ("hidden_size", "hidden"), ("intermediate_size", "intermediate"), ("num_heads", "heads"),
+            ("num_kv_heads", "kv_heads"), ("num_layers", "layers"), ("vocab_size", "vocab"), ("head_dim", "head_dim"),
+            ("max_positions", "max_positions"), ("prefill", "prefill"))}
+        d["rms_norm_eps"] = B.f32(self.eps)
+        d["rope_theta"] = B.f32(self.rope_theta)
+        return d
+
+
+VVLM_CONFIGS = {
+    "vvlm_tiny": VVLmConfig(),
+    "vvlm_tiny_mha_long": VVLmConfig(heads=2, kv_heads=2, head_dim=64, layers=1, prefill=70, steps=2, wseed=43,
+                                     seed=44),
+}
+
+
+def vvlm_weights(cfg: VVLmConfig) -> Dict[str, B.Tensor]:
+    """load_decoder_weights tensors (src/models/vibevoice/decoder.cpp:186-365), tied embeddings, f32."""
+    rng = np.random.default_rng(cfg.wseed)
+    d, I = cfg.hidden, cfg.intermediate
+    q, kv = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    P = "model.language_model."
+    w: Dict[str, B.Tensor] = {P + "embed_tokens.weight": B.f32(_normal(rng, (cfg.vocab, d)))}
+    for l in range(cfg.layers):
+        p = P + "layers.%d." % l
+        w[p + "input_layernorm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+        w[p + "post_attention_layernorm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+        for n, rows in (("q", q), ("k", kv), ("v", kv)):
+            w[p + "self_attn.%s_proj.weight" % n] = B.f32(_normal(rng, (rows, d), 1.0 / np.sqrt(d)))
+            w[p + "self_attn.%s_proj.bias" % n] = B.f32(_normal(rng, (rows,), 0.1))
+        w[p + "self_attn.o_proj.weight"] = B.f32(_normal(rng, (d, q), 1.0 / np.sqrt(q)))
+        w[p + "mlp.gate_proj.weight"] = B.f32(_normal(rng, (I, d), 1.0 / np.sqrt(d)))
+        w[p + "mlp.up_proj.weight"] = B.f32(_normal(rng, (I, d), 1.0 / np.sqrt(d)))
+        w[p + "mlp.down_proj.weight"] = B.f32(_normal(rng, (d, I), 1.0 / np.sqrt(I)))
+    w[P + "norm.weight"] = B.f32(1.0 + _normal(rng, (d,), 0.1))
+    return w
+
+
+def vvlm_inputs(cfg: VVLmConfig) -> Dict[str, B.Tensor]:
+    rng = np.random.default_rng(cfg.seed)
+    d = cfg.scalars()
+    d["prefill_ids"] = B.i64(rng.integers(0, cfg.vocab, cfg.prefill))
+    d["step_ids"] = B.i64(rng.integers(0, cfg.vocab, cfg.steps))
+    return d

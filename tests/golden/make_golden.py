@@ -24,7 +24,7 @@ sys.path.insert(0, ROOT)
 os.environ.setdefault("B2D_REF_VARIANT", "v4")
 
 from oracle import bundle as B  # noqa: E402
-from oracle import dit, oobleck, ref_runner, sa3, saocond, synth, vibevoice, vvdec  # noqa: E402
+from oracle import dit, oobleck, ref_runner, sa3, saocond, synth, vibevoice, vvdec, vvlm  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
@@ -36,6 +36,7 @@ SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
 OOBLECK_GOLDENS = [n for n in synth.OOBLECK_CONFIGS if "bench" not in n]
 VVDEC_GOLDENS = [n for n in synth.VVDEC_CONFIGS if "bench" not in n]
 SAOCOND_GOLDENS = list(synth.SAOCOND_CONFIGS)
+VVLM_GOLDENS = list(synth.VVLM_CONFIGS)
 
 
 def digest(*bundles) -> np.ndarray:
@@ -147,10 +148,22 @@ def saocond_golden(name: str) -> None:
     print("saocond", name, "ok", out["cross_positive"].dims)
 
 
+def vvlm_golden(name: str) -> None:
+    """VibeVoice Qwen2.5 LM: prefill + cached steps (VibeVoiceDecoderWeightsRuntime), tiny config."""
+    cfg = synth.VVLM_CONFIGS[name]
+    w, inp = synth.vvlm_weights(cfg), synth.vvlm_inputs(cfg)
+    out = ref_runner.run("vvlm", inp, w)
+    B.write(os.path.join(HERE, "%s.b2db" % name),
+            {"logits": out["logits"], "last_hidden": out["last_hidden"],
+             "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("vvlm", name, "ok", out["logits"].dims)
+
+
 def main(argv) -> None:
     names = argv or (["q8", "sched"] + ["head:" + n for n in HEAD_GOLDENS] + ["dit:" + n for n in DIT_GOLDENS] +
                      ["sa3:" + n for n in SA3_GOLDENS] + ["oobleck:" + n for n in OOBLECK_GOLDENS] +
-                     ["vvdec:" + n for n in VVDEC_GOLDENS] + ["saocond:" + n for n in SAOCOND_GOLDENS])
+                     ["vvdec:" + n for n in VVDEC_GOLDENS] + ["saocond:" + n for n in SAOCOND_GOLDENS] +
+                     ["vvlm:" + n for n in VVLM_GOLDENS])
     for n in names:
         if n == "q8":
             q8_golden()
@@ -168,6 +181,8 @@ def main(argv) -> None:
             vvdec_golden(n[6:])
         elif n.startswith("saocond:"):
             saocond_golden(n[8:])
+        elif n.startswith("vvlm:"):
+            vvlm_golden(n[5:])
         else:
             raise SystemExit("unknown fixture " + n)
 

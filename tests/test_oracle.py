@@ -203,3 +203,19 @@ def test_saocond_port_vs_reference(name):
     # the bucket table's known values (T5's bidirectional scheme): 0 on the diagonal, 16 + d for small k > q
     b = saocond.relative_buckets(40)
     assert b[5, 5] == 0 and b[5, 6] == 17 and b[6, 5] == 1 and b.max() <= 31
+
+
+@pytest.mark.parametrize("name", ["vvlm_tiny", "vvlm_tiny_mha_long"])
+def test_vvlm_port_vs_reference(name):
+    """The VibeVoice LM restatement (oracle/vvlm.py: Qwen2.5 layers with GQA, NEOX RoPE base 1e6, causal attention,
+    SwiGLU MLP, tied lm_head) against VibeVoiceDecoderWeightsRuntime's prefill + cached steps run by the reference's
+    own CPU build (fp32 weights): logits and last hidden of the prefill's last position and of every step."""
+    from oracle import synth, vvlm
+    cfg = synth.VVLM_CONFIGS[name]
+    w, inp = synth.vvlm_weights(cfg), synth.vvlm_inputs(cfg)
+    g = golden(name)
+    assert np.array_equal(digest(w, inp), g["input_sha256"].data), "synthetic generator drifted"
+    logits, hidden = vvlm.LanguageModel(w, cfg).run(inp["prefill_ids"].array(), inp["step_ids"].array())
+    rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))  # noqa: E731
+    assert rel(logits, g["logits"].array()) < 1e-5
+    assert rel(hidden, g["last_hidden"].array()) < 1e-5
