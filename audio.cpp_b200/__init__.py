@@ -31,7 +31,8 @@ EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_vers
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
             "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
-            "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device"]
+            "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
+            "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device"]
 
 
 class B2DError(RuntimeError):
@@ -100,6 +101,12 @@ class VvdecConfig(C.Structure):
                 ("eps", C.c_float)]
 
 
+class SaoCondConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int64), ("layers", C.c_int64), ("heads", C.c_int64), ("head_dim", C.c_int64),
+                ("intermediate", C.c_int64), ("vocab", C.c_int64), ("prompt_max_length", C.c_int64),
+                ("eps", C.c_float)]
+
+
 SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
 
 SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
@@ -147,6 +154,9 @@ def lib() -> C.CDLL:
         L.b2d_vvdec_load.argtypes = [P, C.POINTER(VvdecConfig), C.POINTER(TensorView), I32]
         L.b2d_vvdec_decode.argtypes = [P, P, I64, P, P]
         L.b2d_vvdec_decode_device.argtypes = [P, P, I64, P, P]
+        L.b2d_saocond_load.argtypes = [P, C.POINTER(SaoCondConfig), C.POINTER(TensorView), I32]
+        L.b2d_saocond_encode.argtypes = [P, P, P, P, I64, P, P, P, P]
+        L.b2d_saocond_encode_device.argtypes = [P, P, P, P, I64, P, P, P, P]
         _lib = L
     return _lib
 
@@ -431,6 +441,33 @@ class VibeVoiceAcousticDecoder:
         self.ctx.check(lib().b2d_vvdec_decode_device(self.ctx.handle, _ptr(latents), latents.shape[0], _ptr(out),
                                                      C.c_void_p(stream)))
         return out
+
+
+class StableAudioConditioner:
+    """FoundationConditionerRuntime (include/engine/models/stable_audio/foundation/conditioner.h:43-66) on a B200
+    context: T5-base + the seconds number conditioners.  ``weights``: (name, ggml_type, dims, payload) with the
+    names ``shared.weight``, ``encoder.*`` and ``conditioner.conditioners.*``."""
+
+    def __init__(self, ctx: Context, hidden: int, layers: int, heads: int, head_dim: int, intermediate: int,
+                 vocab: int, prompt_max_length: int, eps: float = 1e-6, weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = SaoCondConfig(hidden, layers, heads, head_dim, intermediate, vocab, prompt_max_length, eps)
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_saocond_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    def encode_one(self, input_ids, attention_mask, normalized_seconds, stream: int = 0):
+        """Host ids / mask [B, P], seconds [B] -> (cross [B, P + 2, d], cross_mask [B, P + 2], global [B, 2 d])."""
+        ids = np.ascontiguousarray(input_ids, np.int32)
+        mask = np.ascontiguousarray(attention_mask, np.float32)
+        secs = np.ascontiguousarray(normalized_seconds, np.float32)
+        b, p = ids.shape
+        d = self.cfg.hidden
+        cross = np.empty((b, p + 2, d), np.float32)
+        cmask = np.empty((b, p + 2), np.float32)
+        glob = np.empty((b, 2 * d), np.float32)
+        self.ctx.check(lib().b2d_saocond_encode(self.ctx.handle, _ptr(ids), _ptr(mask), _ptr(secs), b, _ptr(cross),
+                                                _ptr(cmask), _ptr(glob), C.c_void_p(stream)))
+        return cross, cmask, glob
 
 
 class VibeVoiceDiffusionHead:

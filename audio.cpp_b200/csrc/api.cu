@@ -20,6 +20,7 @@
 #include "dit_kernels.cuh"
 #include "sa3_kernels.cuh"
 #include "conv_tc.cuh"
+#include "t5_kernels.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -318,6 +319,7 @@ struct DitModel;
 struct Sa3Model;
 struct OobModel;
 struct VdModel;
+struct T5Model;
 
 struct HeadModel {
     b2d_vv_head_config cfg{};
@@ -343,6 +345,7 @@ struct b2d_ctx {
     std::unique_ptr<Sa3Model> sa3;
     std::unique_ptr<OobModel> oob;
     std::unique_ptr<VdModel> vvdec;
+    std::unique_ptr<T5Model> t5;
 };
 
 namespace {
@@ -734,6 +737,7 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 #include "sa3_runtime.inc"
 #include "oobleck_runtime.inc"
 #include "vvdec_runtime.inc"
+#include "t5_runtime.inc"
 
 }  // namespace
 
@@ -778,6 +782,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         ctx->sa3.reset();
         ctx->oob.reset();
         ctx->vvdec.reset();
+        ctx->t5.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -1165,6 +1170,48 @@ b2d_status b2d_vvdec_decode(b2d_ctx* ctx, const float* latents, int64_t frames, 
 b2d_status b2d_vvdec_decode_device(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples,
                                    void* stream) {
     return vd_decode_common(ctx, latents, frames, samples, stream, false);
+}
+
+b2d_status b2d_saocond_load(b2d_ctx* ctx, const b2d_saocond_config* config, const b2d_tensor_view* tensors,
+                            int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "Stable Audio Foundation conditioner requires assets");
+        const b2d_saocond_config& c = *config;
+        if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.vocab <= 0 || c.intermediate <= 0 ||
+            c.prompt_max_length <= 0 || (c.head_dim != 64 && c.head_dim != 32))
+            fail(B2D_EINVAL, "T5BaseEncoderConfig dimensions must be positive (head_dim 32 or 64 on this path)");
+        if (c.hidden % 64 || (c.heads * c.head_dim) % 64 || c.intermediate % 64)
+            fail(B2D_EINVAL, "T5 hidden, heads x head_dim and intermediate sizes must be multiples of 64");
+        auto m = std::make_unique<T5Model>();
+        m->cfg = c;
+        ctx->t5.reset();
+        t5_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->t5 = std::move(m);
+    });
+}
+
+static b2d_status t5_encode_common(b2d_ctx* ctx, const int32_t* ids, const float* mask, const float* seconds,
+                                   int64_t batch, float* cross, float* cross_mask, float* global, void* stream,
+                                   bool host) {
+    return guarded(ctx, [&] {
+        if (!ctx->t5) fail(B2D_ESTATE, "Stable Audio Foundation conditioner weights are not loaded");
+        t5_encode<__half>(ctx, ids, mask, seconds, batch, cross, cross_mask, global, static_cast<cudaStream_t>(stream),
+                          host);
+    });
+}
+
+b2d_status b2d_saocond_encode(b2d_ctx* ctx, const int32_t* input_ids, const float* attention_mask,
+                              const float* normalized_seconds, int64_t batch, float* cross, float* cross_mask,
+                              float* global_cond, void* stream) {
+    return t5_encode_common(ctx, input_ids, attention_mask, normalized_seconds, batch, cross, cross_mask, global_cond,
+                            stream, true);
+}
+
+b2d_status b2d_saocond_encode_device(b2d_ctx* ctx, const int32_t* input_ids, const float* attention_mask,
+                                     const float* normalized_seconds, int64_t batch, float* cross, float* cross_mask,
+                                     float* global_cond, void* stream) {
+    return t5_encode_common(ctx, input_ids, attention_mask, normalized_seconds, batch, cross, cross_mask, global_cond,
+                            stream, false);
 }
 
 }  // extern "C"

@@ -324,6 +324,39 @@ B2D_API b2d_status b2d_vvdec_decode(b2d_ctx* ctx, const float* latents, int64_t 
 B2D_API b2d_status b2d_vvdec_decode_device(b2d_ctx* ctx, const float* latents, int64_t frames, float* samples,
                                            void* stream);
 
+/* ------------------------------------- Stable Audio Open 1.0 conditioner (T5) */
+/* StableAudioConfig T5 fields (include/engine/models/stable_audio/assets.h:14-84); cond_dim = hidden, global =
+ * 2 x hidden.  head_dim 32 or 64; hidden, heads x head_dim and intermediate multiples of 64. */
+typedef struct {
+    int64_t hidden;             /* t5_hidden_size: 768 */
+    int64_t layers;             /* 12 */
+    int64_t heads;              /* 12 */
+    int64_t head_dim;           /* 64 */
+    int64_t intermediate;       /* 3072 */
+    int64_t vocab;              /* t5_vocab_size */
+    int64_t prompt_max_length;  /* 128 */
+    float eps;                  /* t5_rms_norm_eps */
+} b2d_saocond_config;
+
+/* Loads the T5-base encoder ("shared.weight", "encoder.*", load_t5_base_runtime_weights, src/models/stable_audio/
+ * foundation/conditioner.cpp:202-233) and the seconds_start / seconds_total number conditioners
+ * ("conditioner.conditioners.*", :165-175). */
+B2D_API b2d_status b2d_saocond_load(b2d_ctx* ctx, const b2d_saocond_config* config, const b2d_tensor_view* tensors,
+                                    int32_t n_tensors);
+
+/* FoundationConditionerRuntime::encode_one (conditioner.cpp:422-471) for one token batch: input_ids / attention_mask
+ * (0 / 1) [batch, prompt_max_length], normalized seconds_total [batch] -> cross [batch, prompt_max_length + 2, hidden],
+ * cross_mask [batch, prompt_max_length + 2] (may be NULL), global [batch, 2 hidden].  Host buffers.  A negative
+ * prompt is a second call (as encode does). */
+B2D_API b2d_status b2d_saocond_encode(b2d_ctx* ctx, const int32_t* input_ids, const float* attention_mask,
+                                      const float* normalized_seconds, int64_t batch, float* cross, float* cross_mask,
+                                      float* global_cond, void* stream);
+
+/* Same with device pointers; asynchronous on `stream`. */
+B2D_API b2d_status b2d_saocond_encode_device(b2d_ctx* ctx, const int32_t* input_ids, const float* attention_mask,
+                                             const float* normalized_seconds, int64_t batch, float* cross,
+                                             float* cross_mask, float* global_cond, void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
