@@ -269,6 +269,8 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
     scaling).  Metric: sequence-steps/s over all ranks."""
     from oracle import synth
     cfg = synth.SA3_CONFIGS[SA3_WORKLOAD]
+    if args.small:  # profiling only: a shape an ncu capture finishes (the reported config says so)
+        cfg = synth.Sa3Config(**{**cfg.__dict__, "latent_tokens": 448, "steps": 2})
     cfg = synth.Sa3Config(**{**cfg.__dict__, "prompt_seeds": (rank,)})
     w = synth.sa3_weights(cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
@@ -300,7 +302,7 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
     fl = 2 * L1 * d * 18 * d + 4 * L1 * (L1 + cfg.prompt_max_length + 1) * d
     res = {"metric": "denoise sequence-steps/sec (SA3 DiT)", "value": round(seq_steps / (ms / 1e3), 2),
            "unit": "seq-steps/s", "ms_per_call": round(ms, 2), "timed_calls": calls, "warmup_calls": warm,
-           "config": {"workload": SA3_WORKLOAD,
+           "config": {"workload": SA3_WORKLOAD + ("_small" if args.small else ""),
                       "model": "Stable-Audio-3-layout DiT at SAO-1.0 transformer size (random-init)",
                       "weights": cfg.wtype, "sequences_per_rank": 2 * cfg.batch, "tokens": L1,
                       "steps": cfg.steps, "sampler": cfg.sampler, "cfg_scale": cfg.cfg, "apg_scale": cfg.apg,
@@ -333,6 +335,8 @@ def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
     Metric: decoded audio frames/s over all ranks."""
     from oracle import synth
     cfg = synth.OOBLECK_CONFIGS[OOBLECK_WORKLOAD]
+    if args.small:  # profiling only: 128 latents (262,144 frames), activations still larger than L2
+        cfg = synth.OobleckConfig(**{**cfg.__dict__, "latent_tokens": 128})
     w = synth.oobleck_weights(cfg)
     dec = b2d.OobleckDecoder(ctx, cfg.latent_dim, cfg.channels, cfg.c_mults, cfg.strides, cfg.audio_channels,
                              weights=[(n, 0, t.dims, t.data) for n, t in w.items()])
@@ -361,7 +365,7 @@ def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
     res = {"metric": "decoded audio frames/sec (Oobleck VAE)", "value": round(total / (ms / 1e3), 1),
            "unit": "frames/s", "ms_per_call": round(ms, 3), "timed_calls": calls, "warmup_calls": warm,
            "realtime_factor_44k1": round(total / (ms / 1e3) / 44100.0, 1),
-           "config": {"workload": OOBLECK_WORKLOAD, "model": "Stable-Audio-Open-1.0-shaped Oobleck decoder (random-init)",
+           "config": {"workload": OOBLECK_WORKLOAD + ("_small" if args.small else ""), "model": "Stable-Audio-Open-1.0-shaped Oobleck decoder (random-init)",
                       "latent_tokens": cfg.latent_tokens, "frames": frames, "channels": ch, "strides": cfg.strides,
                       "n_gpus": world},
            "dtype": "fp16 tensor-core operands, fp32 accumulate and residual stream",
@@ -591,6 +595,8 @@ def main():
     ap.add_argument("--dit-dpm-steps", type=int, default=0,
                     help="profiling only: DPM++ steps per DiT call instead of the workload's 100")
     ap.add_argument("--dit-warmup", type=int, default=1)
+    ap.add_argument("--small", action="store_true",
+                    help="profiling only: smaller SA3 / Oobleck shapes that an ncu capture can finish")
     args = ap.parse_args()
     if args.impl == "reference":
         bench_reference(args)
