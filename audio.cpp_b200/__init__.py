@@ -32,7 +32,8 @@ EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_vers
             "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
             "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
-            "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device"]
+            "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device",
+            "b2d_vvlm_load", "b2d_vvlm_prefill", "b2d_vvlm_step"]
 
 
 class B2DError(RuntimeError):
@@ -107,6 +108,12 @@ class SaoCondConfig(C.Structure):
                 ("eps", C.c_float)]
 
 
+class VvlmConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int64), ("intermediate", C.c_int64), ("heads", C.c_int64), ("kv_heads", C.c_int64),
+                ("head_dim", C.c_int64), ("layers", C.c_int64), ("vocab", C.c_int64), ("max_positions", C.c_int64),
+                ("eps", C.c_float), ("rope_theta", C.c_float)]
+
+
 SA3_SAMPLERS = {"": 0, "pingpong": 0, "euler": 1}
 
 SAMPLERS = {"dpmpp-2m": 0, "dpmpp-3m-sde": 1, "": 2, "euler": 2, "pingpong": 2}
@@ -157,6 +164,9 @@ def lib() -> C.CDLL:
         L.b2d_saocond_load.argtypes = [P, C.POINTER(SaoCondConfig), C.POINTER(TensorView), I32]
         L.b2d_saocond_encode.argtypes = [P, P, P, P, I64, P, P, P, P]
         L.b2d_saocond_encode_device.argtypes = [P, P, P, P, I64, P, P, P, P]
+        L.b2d_vvlm_load.argtypes = [P, C.POINTER(VvlmConfig), C.POINTER(TensorView), I32]
+        L.b2d_vvlm_prefill.argtypes = [P, P, I64, P, P, P]
+        L.b2d_vvlm_step.argtypes = [P, P, P, P, P]
         _lib = L
     return _lib
 
@@ -468,6 +478,36 @@ class StableAudioConditioner:
         self.ctx.check(lib().b2d_saocond_encode(self.ctx.handle, _ptr(ids), _ptr(mask), _ptr(secs), b, _ptr(cross),
                                                 _ptr(cmask), _ptr(glob), C.c_void_p(stream)))
         return cross, cmask, glob
+
+
+class VibeVoiceLanguageModel:
+    """VibeVoiceDecoderWeightsRuntime's prefill / cached step (include/engine/models/vibevoice/decoder.h:106-143) on a
+    B200 context; one KV cache per context.  ``weights``: the ``model.language_model.*`` tensors."""
+
+    def __init__(self, ctx: Context, hidden: int, intermediate: int, heads: int, kv_heads: int, head_dim: int,
+                 layers: int, vocab: int, max_positions: int, eps: float = 1e-6, rope_theta: float = 1e6,
+                 weights: Iterable[WeightSpec] = ()):
+        self.ctx = ctx
+        self.cfg = VvlmConfig(hidden, intermediate, heads, kv_heads, head_dim, layers, vocab, max_positions, eps,
+                              rope_theta)
+        views, keep = _views(weights)
+        ctx.check(lib().b2d_vvlm_load(ctx.handle, C.byref(self.cfg), views, len(keep) // 2))
+
+    def prefill(self, embeddings, stream: int = 0):
+        """Host embeddings [steps, hidden] -> (logits [vocab], last_hidden [hidden]) of the last position."""
+        e = np.ascontiguousarray(embeddings, np.float32)
+        logits = np.empty(self.cfg.vocab, np.float32)
+        hidden = np.empty(self.cfg.hidden, np.float32)
+        self.ctx.check(lib().b2d_vvlm_prefill(self.ctx.handle, _ptr(e), e.shape[0], _ptr(logits), _ptr(hidden),
+                                              C.c_void_p(stream)))
+        return logits, hidden
+
+    def step(self, embedding, stream: int = 0):
+        e = np.ascontiguousarray(embedding, np.float32).reshape(-1)
+        logits = np.empty(self.cfg.vocab, np.float32)
+        hidden = np.empty(self.cfg.hidden, np.float32)
+        self.ctx.check(lib().b2d_vvlm_step(self.ctx.handle, _ptr(e), _ptr(logits), _ptr(hidden), C.c_void_p(stream)))
+        return logits, hidden
 
 
 class VibeVoiceDiffusionHead:

@@ -21,6 +21,7 @@
 #include "sa3_kernels.cuh"
 #include "conv_tc.cuh"
 #include "t5_kernels.cuh"
+#include "lm_kernels.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
@@ -320,6 +321,7 @@ struct Sa3Model;
 struct OobModel;
 struct VdModel;
 struct T5Model;
+struct LmModel;
 
 struct HeadModel {
     b2d_vv_head_config cfg{};
@@ -346,6 +348,7 @@ struct b2d_ctx {
     std::unique_ptr<OobModel> oob;
     std::unique_ptr<VdModel> vvdec;
     std::unique_ptr<T5Model> t5;
+    std::unique_ptr<LmModel> lm;
 };
 
 namespace {
@@ -738,6 +741,7 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 #include "oobleck_runtime.inc"
 #include "vvdec_runtime.inc"
 #include "t5_runtime.inc"
+#include "lm_runtime.inc"
 
 }  // namespace
 
@@ -783,6 +787,7 @@ void b2d_destroy(b2d_ctx* ctx) {
         ctx->oob.reset();
         ctx->vvdec.reset();
         ctx->t5.reset();
+        ctx->lm.reset();
         ctx->status.release();
         if (ctx->load_stream) cudaStreamDestroy(ctx->load_stream);
     }
@@ -1212,6 +1217,41 @@ b2d_status b2d_saocond_encode_device(b2d_ctx* ctx, const int32_t* input_ids, con
                                      float* global_cond, void* stream) {
     return t5_encode_common(ctx, input_ids, attention_mask, normalized_seconds, batch, cross, cross_mask, global_cond,
                             stream, false);
+}
+
+b2d_status b2d_vvlm_load(b2d_ctx* ctx, const b2d_vvlm_config* config, const b2d_tensor_view* tensors,
+                         int32_t n_tensors) {
+    return guarded(ctx, [&] {
+        if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "VibeVoice decoder weights require model weights");
+        const b2d_vvlm_config& c = *config;
+        if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+            c.vocab <= 0 || c.max_positions <= 0 || (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128))
+            fail(B2D_EINVAL, "VibeVoice decoder config: positive sizes, heads a multiple of kv_heads, head_dim 32/64/128");
+        if (c.hidden % 64 || c.intermediate % 64 || (c.heads * c.head_dim) % 64)
+            fail(B2D_EINVAL, "VibeVoice decoder hidden, intermediate and heads x head_dim must be multiples of 64");
+        auto m = std::make_unique<LmModel>();
+        m->cfg = c;
+        ctx->lm.reset();
+        lm_load_t<__half>(ctx, *m, tensors, n_tensors);
+        ctx->lm = std::move(m);
+    });
+}
+
+b2d_status b2d_vvlm_prefill(b2d_ctx* ctx, const float* embeddings, int64_t steps, float* logits, float* last_hidden,
+                            void* stream) {
+    return guarded(ctx, [&] {
+        if (!ctx->lm) fail(B2D_ESTATE, "VibeVoice decoder weights are not loaded");
+        ctx->lm->pos = 0;
+        lm_forward<__half>(ctx, embeddings, steps, logits, last_hidden, static_cast<cudaStream_t>(stream));
+    });
+}
+
+b2d_status b2d_vvlm_step(b2d_ctx* ctx, const float* embedding, float* logits, float* last_hidden, void* stream) {
+    return guarded(ctx, [&] {
+        if (!ctx->lm) fail(B2D_ESTATE, "VibeVoice decoder weights are not loaded");
+        if (ctx->lm->pos == 0) fail(B2D_ESTATE, "VibeVoice decoder cached step before prefill");
+        lm_forward<__half>(ctx, embedding, 1, logits, last_hidden, static_cast<cudaStream_t>(stream));
+    });
 }
 
 }  // extern "C"

@@ -357,6 +357,35 @@ B2D_API b2d_status b2d_saocond_encode_device(b2d_ctx* ctx, const int32_t* input_
                                              const float* normalized_seconds, int64_t batch, float* cross,
                                              float* cross_mask, float* global_cond, void* stream);
 
+/* --------------------------------------------- VibeVoice language model (Qwen2.5) */
+/* VibeVoiceDecoderConfig fields (include/engine/models/vibevoice/assets.h:39-54); tied embeddings. */
+typedef struct {
+    int64_t hidden;          /* hidden_size */
+    int64_t intermediate;    /* intermediate_size */
+    int64_t heads;           /* num_attention_heads */
+    int64_t kv_heads;        /* num_key_value_heads */
+    int64_t head_dim;        /* 32, 64 or 128 */
+    int64_t layers;          /* num_hidden_layers */
+    int64_t vocab;           /* vocab_size */
+    int64_t max_positions;   /* KV cache capacity (max_position_embeddings) */
+    float eps;               /* rms_norm_eps */
+    float rope_theta;
+} b2d_vvlm_config;
+
+/* Loads "model.language_model.*" (load_decoder_weights, src/models/vibevoice/decoder.cpp:186-365). */
+B2D_API b2d_status b2d_vvlm_load(b2d_ctx* ctx, const b2d_vvlm_config* config, const b2d_tensor_view* tensors,
+                                 int32_t n_tensors);
+
+/* VibeVoiceDecoderWeightsRuntime::prefill_embeddings (include/engine/models/vibevoice/decoder.h:129): embeddings
+ * [steps, hidden] (host) from position 0, resetting the context's KV cache; returns the last position's logits
+ * [vocab] and final-norm hidden state [hidden] (host). */
+B2D_API b2d_status b2d_vvlm_prefill(b2d_ctx* ctx, const float* embeddings, int64_t steps, float* logits,
+                                    float* last_hidden, void* stream);
+
+/* VibeVoiceDecoderWeightsRuntime::cached_step (decoder.h:134-137): one more position after the cached ones. */
+B2D_API b2d_status b2d_vvlm_step(b2d_ctx* ctx, const float* embedding, float* logits, float* last_hidden,
+                                 void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */
