@@ -400,3 +400,81 @@ std::vector<engine::models::vibevoice::AudioBuffer> OobleckAutoencoderRuntime::d
 }
 
 }  // namespace engine::models::stable_audio::foundation
+
+namespace engine::models::vibevoice {
+
+VibeVoiceDecoderWeightsRuntime::VibeVoiceDecoderWeightsRuntime(const VibeVoiceDecoderConfig & config,
+                                                               const std::vector<engine::b200::RawTensor> & tensors,
+                                                               int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    const b2d_vvlm_config c{config.hidden_size,         config.intermediate_size, config.num_attention_heads,
+                            config.num_key_value_heads, config.head_dim,          config.num_hidden_layers,
+                            config.vocab_size,          config.max_position_embeddings,
+                            config.rms_norm_eps,        config.rope_theta};
+    const auto views = engine::b200::views_of(tensors);
+    device_->check(b2d_vvlm_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+VibeVoiceDecoderResult VibeVoiceDecoderWeightsRuntime::prefill_embeddings(const std::vector<float> & embeddings,
+                                                                          int64_t steps) const {
+    if (steps <= 0 || static_cast<int64_t>(embeddings.size()) != steps * config_.hidden_size)
+        throw std::runtime_error("VibeVoice decoder prefill embedding payload size mismatch");
+    VibeVoiceDecoderResult r{std::vector<float>(static_cast<size_t>(config_.vocab_size)),
+                             std::vector<float>(static_cast<size_t>(config_.hidden_size))};
+    device_->check(b2d_vvlm_prefill(device_->ctx(), embeddings.data(), steps, r.logits.data(), r.last_hidden.data(),
+                                    nullptr));
+    return r;
+}
+
+VibeVoiceDecoderResult VibeVoiceDecoderWeightsRuntime::cached_step(const std::vector<float> & embedding) const {
+    if (static_cast<int64_t>(embedding.size()) != config_.hidden_size)
+        throw std::runtime_error("VibeVoice decoder cached step embedding payload size mismatch");
+    VibeVoiceDecoderResult r{std::vector<float>(static_cast<size_t>(config_.vocab_size)),
+                             std::vector<float>(static_cast<size_t>(config_.hidden_size))};
+    device_->check(b2d_vvlm_step(device_->ctx(), embedding.data(), r.logits.data(), r.last_hidden.data(), nullptr));
+    return r;
+}
+
+}  // namespace engine::models::vibevoice
+
+namespace engine::models::stable_audio::foundation {
+
+FoundationConditionerRuntime::FoundationConditionerRuntime(const T5Config & config,
+                                                           const std::vector<engine::b200::RawTensor> & tensors,
+                                                           int device)
+    : config_(config), device_(std::make_unique<engine::b200::Device>(device)) {
+    const b2d_saocond_config c{config.t5_hidden_size,       config.t5_layers,     config.t5_attention_heads,
+                               config.t5_head_dim,          config.t5_intermediate_size, config.t5_vocab_size,
+                               config.prompt_max_length,    config.t5_rms_norm_eps};
+    const auto views = engine::b200::views_of(tensors);
+    device_->check(b2d_saocond_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
+}
+
+// Validation and messages as encode_one (src/models/stable_audio/foundation/conditioner.cpp:156-163, 422-430).
+StableAudioConditionedInput FoundationConditionerRuntime::encode_one(
+    const StableAudioTokenBatch & tokens, const std::vector<float> & normalized_total_seconds) const {
+    if (tokens.batch <= 0) throw std::runtime_error("Stable Audio Foundation conditioner requires a positive batch");
+    if (static_cast<int64_t>(normalized_total_seconds.size()) != tokens.batch)
+        throw std::runtime_error("Stable Audio Foundation conditioner seconds batch does not match prompt batch");
+    if (tokens.tokens != config_.prompt_max_length)
+        throw std::runtime_error("Stable Audio Foundation conditioner token length mismatch");
+    const int64_t B = tokens.batch, P = tokens.tokens, d = config_.t5_hidden_size;
+    std::vector<float> mask(static_cast<size_t>(B * P));
+    for (size_t i = 0; i < mask.size() && i < tokens.attention_mask.size(); ++i)
+        mask[i] = tokens.attention_mask[i] != 0 ? 1.0F : 0.0F;
+    StableAudioConditionedInput out;
+    out.batch = B;
+    out.cross_tokens = P + 2;
+    out.cond_dim = d;
+    out.cross_attention.resize(static_cast<size_t>(B * (P + 2) * d));
+    out.global.resize(static_cast<size_t>(B * 2 * d));
+    std::vector<float> cmask(static_cast<size_t>(B * (P + 2)));
+    device_->check(b2d_saocond_encode(device_->ctx(), tokens.input_ids.data(), mask.data(),
+                                      normalized_total_seconds.data(), B, out.cross_attention.data(), cmask.data(),
+                                      out.global.data(), nullptr));
+    out.cross_attention_mask.assign(cmask.size(), 0);
+    for (size_t i = 0; i < cmask.size(); ++i) out.cross_attention_mask[i] = cmask[i] != 0.0F ? 1 : 0;
+    return out;
+}
+
+}  // namespace engine::models::stable_audio::foundation

@@ -10,6 +10,8 @@
 //   engine::models::stable_audio::StableAudioRfDitRuntime            include/engine/models/stable_audio/rf_dit.h:78-100
 //   engine::models::stable_audio::foundation::OobleckAutoencoderRuntime (decode) include/engine/models/stable_audio/foundation/oobleck_autoencoder.h:71-96
 //   engine::models::vibevoice::VibeVoiceTokenizerWeightsRuntime (decode_acoustic) include/engine/models/vibevoice/tokenizer_audio.h:94-140
+//   engine::models::vibevoice::VibeVoiceDecoderWeightsRuntime (prefill / cached step) include/engine/models/vibevoice/decoder.h:106-143
+//   engine::models::stable_audio::foundation::FoundationConditionerRuntime (encode_one) include/engine/models/stable_audio/foundation/conditioner.h:43-66
 #pragma once
 
 #include <cstdint>
@@ -154,6 +156,38 @@ private:
     std::unique_ptr<engine::b200::Device> device_;
 };
 
+// VibeVoiceDecoderConfig (include/engine/models/vibevoice/assets.h:39-54), tied embeddings.
+struct VibeVoiceDecoderConfig {
+    int64_t hidden_size = 0;
+    int64_t intermediate_size = 0;
+    int64_t max_position_embeddings = 0;
+    int64_t num_attention_heads = 0;
+    int64_t num_hidden_layers = 0;
+    int64_t num_key_value_heads = 0;
+    int64_t vocab_size = 0;
+    int64_t head_dim = 0;
+    float rms_norm_eps = 1.0e-6F;
+    float rope_theta = 1000000.0F;
+};
+
+struct VibeVoiceDecoderResult {
+    std::vector<float> logits;
+    std::vector<float> last_hidden;
+};
+
+// The Qwen2.5 LM on the GPU (b2d_vvlm_*): one KV cache per runtime; prefill resets it, each step appends.
+class VibeVoiceDecoderWeightsRuntime final {
+public:
+    VibeVoiceDecoderWeightsRuntime(const VibeVoiceDecoderConfig & config,
+                                   const std::vector<engine::b200::RawTensor> & tensors, int device);
+    VibeVoiceDecoderResult prefill_embeddings(const std::vector<float> & embeddings, int64_t steps) const;
+    VibeVoiceDecoderResult cached_step(const std::vector<float> & embedding) const;
+
+private:
+    VibeVoiceDecoderConfig config_;
+    std::unique_ptr<engine::b200::Device> device_;
+};
+
 std::vector<VibeVoiceTokenizerLatents> sample_vibevoice_speech_latents(
     const VibeVoiceDiffusionHeadWeightsRuntime & prediction_head, VibeVoiceDPMSolverScheduler & scheduler,
     const VibeVoiceSpeechDiffusionInput & input);
@@ -243,6 +277,38 @@ struct OobleckConfig {
     std::vector<int64_t> same_strides;
     int audio_channels = 2;
     int sample_rate = 44100;
+};
+
+// T5 fields of StableAudioConfig (include/engine/models/stable_audio/assets.h:14-84).
+struct T5Config {
+    int64_t t5_hidden_size = 768;
+    int64_t t5_layers = 12;
+    int64_t t5_attention_heads = 12;
+    int64_t t5_head_dim = 64;
+    int64_t t5_intermediate_size = 3072;
+    int64_t t5_vocab_size = 32128;
+    int64_t prompt_max_length = 128;
+    float t5_rms_norm_eps = 1.0e-6F;
+};
+
+struct StableAudioTokenBatch {
+    int64_t batch = 0;
+    int64_t tokens = 0;
+    std::vector<int32_t> input_ids;
+    std::vector<uint8_t> attention_mask;
+};
+
+// FoundationConditionerRuntime::encode_one on the GPU (b2d_saocond_*).
+class FoundationConditionerRuntime {
+public:
+    FoundationConditionerRuntime(const T5Config & config, const std::vector<engine::b200::RawTensor> & tensors,
+                                 int device);
+    StableAudioConditionedInput encode_one(const StableAudioTokenBatch & tokens,
+                                           const std::vector<float> & normalized_total_seconds) const;
+
+private:
+    T5Config config_;
+    std::unique_ptr<engine::b200::Device> device_;
 };
 
 // OobleckAutoencoderRuntime's decode on the GPU (b2d_oobleck_*); audio per prompt as interleaved samples.
