@@ -271,8 +271,9 @@ __global__ void take_channels_kernel(const float* __restrict__ y, int64_t ld, in
 
 // VibeVoice tokenizer blocks (src/models/vibevoice/tokenizer_audio.cpp:679-740), time-major rows of C channels.
 // Per-row RMS scale 1 / sqrt(mean(x^2) + eps); with `out` also ct(x * scale * w).  One warp per row.
+// C is the row stride; cmean the channels the mean runs over (the rest are zero padding with zero weights).
 template <typename CT>
-__global__ void __launch_bounds__(256) tok_rms_kernel(const float* __restrict__ x, int C, int64_t rows,
+__global__ void __launch_bounds__(256) tok_rms_kernel(const float* __restrict__ x, int C, int cmean, int64_t rows,
                                                       const float* __restrict__ w, float eps,
                                                       float* __restrict__ scale, CT* __restrict__ out) {
     const int lane = threadIdx.x & 31;
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(256) tok_rms_kernel(const float* __restrict__ 
     for (int c = lane; c < C; c += 32) ss += xr[c] * xr[c];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float sc = 1.0f / sqrtf(ss / float(C) + eps);
+    const float sc = 1.0f / sqrtf(ss / float(cmean) + eps);
     if (scale && lane == 0) scale[row] = sc;
     if (out)
         for (int c = lane; c < C; c += 32) out[row * C + c] = from_f32<CT>(xr[c] * sc * __ldg(w + c));

@@ -586,6 +586,9 @@ VVDEC_CONFIGS = {
     "vvdec_tiny": VVDecConfig(),
     "vvdec_tiny_norm": VVDecConfig(ratios=(4, 2), depths=(2, 1, 1), disable_last_norm=False, frames=17, wseed=23,
                                    seed=24),
+    # the released decoders' channel plan: 32 filters, so the last stage has 32 channels (zero-padded on the GPU)
+    "vvdec_tiny_c32": VVDecConfig(n_filters=32, ratios=(2, 2), depths=(1, 1, 1), disable_last_norm=False, frames=20,
+                                  wseed=25, seed=26),
 }
 
 

@@ -14,8 +14,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("name", ["vvdec_tiny", "vvdec_tiny_norm"])
-def test_vvdec_decode_matches_reference(b2d, ctx, name):
+def _check(b2d, ctx, name):
     from oracle import vvdec
     cfg = synth.VVDEC_CONFIGS[name]
     w = synth.vvdec_weights(cfg)
@@ -36,3 +35,15 @@ def test_vvdec_decode_matches_reference(b2d, ctx, name):
     dec.decode_device(d_lat, d_out, stream=torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(d_out.cpu().numpy(), out)
+
+
+@pytest.mark.parametrize("name", ["vvdec_tiny", "vvdec_tiny_norm"])
+def test_vvdec_decode_matches_reference(b2d, ctx, name):
+    _check(b2d, ctx, name)
+
+
+# The 32-channel stage of the released decoders runs zero-padded to a 64-column tile (RMS means over the true
+# channel count).  This case has not yet run on a B200; it stays out of the GPU pass until its first supervised run.
+@pytest.mark.skip(reason="zero-padded channel path not yet run on a B200")
+def test_vvdec_decode_32_channel_stage_matches_reference(b2d, ctx):
+    _check(b2d, ctx, "vvdec_tiny_c32")

@@ -164,7 +164,7 @@ def test_oobleck_port_vs_reference(name):
     assert err < 1e-5, err
 
 
-@pytest.mark.parametrize("name", ["vvdec_tiny", "vvdec_tiny_norm"])
+@pytest.mark.parametrize("name", ["vvdec_tiny", "vvdec_tiny_norm", "vvdec_tiny_c32"])
 def test_vvdec_port_vs_reference(name):
     """The VibeVoice acoustic decoder restatement (oracle/vvdec.py) against
     VibeVoiceTokenizerWeightsRuntime::decode_acoustic run by the reference's own CPU build (fp32 weights)."""
