@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
+            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_gemm_splitk_noalloc_status", "b2d_gemm_splitk_noalloc_selftest_timeout", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
             "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
             "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device",
@@ -146,6 +146,8 @@ def lib() -> C.CDLL:
         L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
+        L.b2d_gemm_splitk_noalloc_status.argtypes = [P, C.c_char_p, C.c_size_t]
+        L.b2d_gemm_splitk_noalloc_selftest_timeout.argtypes = [C.c_uint32, P, C.c_char_p, C.c_size_t]
         L.b2d_attention.argtypes = [P, I32, P, I64, I64, P, P, I64, I64, P, I64, I64, I32, I32, I32, I32, I32, P]
         L.b2d_selftest_wait_timeout.argtypes = [P, C.c_uint32, P]
         L.b2d_torch_randn.argtypes = [P, I32, C.c_uint64, C.c_uint64, I64, I64, I64, I32, P, P]

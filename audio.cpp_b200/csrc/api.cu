@@ -8,14 +8,16 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <map>
+#include <mutex>
+#include <set>
 #include <memory>
 #include <string>
 #include <tuple>
 #include <vector>
 
 #include "../../include/b200diff.h"
-#include "attention.cuh"
 #include "attention_tc.cuh"
 #include "dit_kernels.cuh"
 #include "sa3_kernels.cuh"
@@ -88,16 +90,35 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+std::mutex g_host_mutex;  // guards the process-wide lookups below
+
 EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
+    static std::atomic<EncodeTiledFn> fn{nullptr};
+    EncodeTiledFn f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        std::lock_guard<std::mutex> lock(g_host_mutex);
         void* p = nullptr;
         cudaDriverEntryPointQueryResult q;
         CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
         if (q != cudaDriverEntryPointSuccess || !p) fail(B2D_ECUDA, "cuTensorMapEncodeTiled unavailable");
-        fn = reinterpret_cast<EncodeTiledFn>(p);
+        f = reinterpret_cast<EncodeTiledFn>(p);
+        fn.store(f, std::memory_order_release);
     }
-    return fn;
+    return f;
+}
+
+// A kernel's dynamic shared-memory limit is an attribute of the function in the CURRENT device's context, so it
+// is set once per (kernel, device): a second context on another device in the same process sets its own.
+template <typename K>
+void set_smem_limit(K* kernel, int bytes) {
+    static std::set<std::pair<const void*, int>> done;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+    std::lock_guard<std::mutex> lock(g_host_mutex);
+    if (done.count(key)) return;
+    CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    done.insert(key);
 }
 
 // 2-D K-major operand [rows, k] of 16-bit elements, boxes of 64 (K) x box_rows, 128B swizzle.
@@ -122,12 +143,7 @@ template <int BN, int EPI, typename CT>
 void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K, const EpiParams& ep,
                    int num_sms, cudaStream_t st) {
     using S = GemmShape<BN>;
-    static bool configured = false;  // per instantiation; attribute is per device-function
-    if (!configured) {
-        CK(cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(S::SMEM_BYTES)));
-        configured = true;
-    }
+    set_smem_limit(gemm_tc_kernel<BN, EPI, CT>, int(S::SMEM_BYTES));
     const int splits = ep.splits > 1 ? ep.splits : 1;
     if ((K / 64) % splits) fail(B2D_EINVAL, "split-K %d does not divide the %lld K blocks", splits, (long long)(K / 64));
     if (splits > 1 && EPI != EPI_F32) fail(B2D_EINVAL, "split-K needs the fp32 partial-output epilogue");
@@ -154,18 +170,12 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
 }
 
 // 2-SM (cta_group::2) 256 x 256 pair tiles; B operands need a 128-row TMA box.
-int g_gemm_pair = -1;  // -1 automatic, 0 off, 1 forced (B2D_GEMM_PAIR)
 
 template <int BN, int EPI, typename CT>
 void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb_half, int64_t M, int64_t N, int64_t K,
                         const EpiParams& ep, int num_sms, cudaStream_t st) {
     using S = GemmPairShape<BN>;
-    static bool configured = false;
-    if (!configured) {
-        CK(cudaFuncSetAttribute(gemm_tc2_kernel<BN, EPI, CT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(S::SMEM_BYTES)));
-        configured = true;
-    }
+    set_smem_limit(gemm_tc2_kernel<BN, EPI, CT>, int(S::SMEM_BYTES));
     const int64_t units = ((M + 255) / 256) * (N / BN);
     if (units == 0) return;
     const int64_t pairs = units < num_sms / 2 ? units : num_sms / 2;
@@ -768,8 +778,6 @@ b2d_status b2d_create(int device, b2d_ctx** out) {
         CK(cudaMemset(ctx->status.p, 0, 256));
         CK(cudaStreamCreateWithFlags(&ctx->load_stream, cudaStreamNonBlocking));
         encode_fn();
-        if (const char* mt = std::getenv("B2D_ATTN_MT")) g_attn_mt = std::atoi(mt);
-        if (const char* at = std::getenv("B2D_ATTN")) g_attn_tc = std::strcmp(at, "mma") != 0;
     });
     if (s != B2D_OK) return s;
     *out = ctx.release();
@@ -1146,9 +1154,10 @@ b2d_status b2d_vvdec_load(b2d_ctx* ctx, const b2d_vvdec_config* config, const b2
     return guarded(ctx, [&] {
         if (!config || (!tensors && n_tensors > 0)) fail(B2D_EINVAL, "VibeVoice tokenizer weights runtime requires assets");
         const b2d_vvdec_config& c = *config;
+        // stages narrower than 64 channels (the released decoders' 32-channel last stage) run zero-padded to 64
         if (c.n_stages < 1 || c.n_stages > 8 || c.vae_dim <= 0 || c.vae_dim % 64 || c.n_filters <= 0 ||
-            c.n_filters % 64)
-            fail(B2D_EINVAL, "tokenizer decoder config: 1..8 stages, vae_dim and n_filters multiples of 64");
+            c.n_filters % 32)
+            fail(B2D_EINVAL, "tokenizer decoder config: 1..8 stages, vae_dim a multiple of 64, n_filters of 32");
         for (int i = 0; i < c.n_stages; ++i)
             if (c.depths[i] <= 0 || (i + 1 < c.n_stages && c.ratios[i] <= 0))
                 fail(B2D_EINVAL, "tokenizer decoder config: depths / ratios must be positive");

@@ -48,29 +48,6 @@ constexpr uint32_t kFaBar = kFaP + 8 * kFaTile;
 constexpr uint32_t kFaSmemBytes = kFaBar + 256 + 1024;  // + barriers + alignment slack
 constexpr float kFaRescaleLog2 = 8.0f;                  // lazy-rescale bound (log2 units)
 
-// Optional phase trace of CTA (0,0,0) for profiling builds (-DB2D_FA_TRACE): clock64 stamps
-// at trace[event * 64 + block].
-#ifdef B2D_FA_TRACE
-__device__ unsigned long long g_fa_trace[32 * 64];
-__device__ int g_fa_where[32];  // last wait point per warp of CTA (0,0,0)
-#define FA_WHERE(code)                                                                                     \
-    do {                                                                                                   \
-        if (blockIdx.x == gridDim.x - 1 && blockIdx.y == 0 && blockIdx.z == 0 && (threadIdx.x & 31) == 0) \
-            g_fa_where[threadIdx.x >> 5] = (code);                                                          \
-    } while (0)
-#define FA_STAMP(ev, j)                                                                      \
-    do {                                                                                     \
-        if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 64)               \
-            g_fa_trace[(ev) * 64 + (j)] = clock64();                                         \
-    } while (0)
-#else
-#define FA_STAMP(ev, j) \
-    do {                \
-    } while (0)
-#define FA_WHERE(code) \
-    do {               \
-    } while (0)
-#endif
 
 struct FaArgs {
     int lq, lk, kv_rep, nseq;
@@ -156,14 +133,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int j = 0; j < nb; ++j) {
                 const int s = j % kFaStages;
                 const uint32_t ph = uint32_t(j / kFaStages) & 1u;
-                FA_WHERE(1000 + j);
                 if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutProducer)) break;
-                FA_STAMP(0, j);
                 mbar_arrive_expect_tx(&k_full[s], kFaTile);
                 tma_load_3d(smem + kFaK + s * kFaTile, &tmK, &k_full[s], kvh * 64, j * 128, seq);
-                FA_WHERE(2000 + j);
                 if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutProducer)) break;
-                FA_STAMP(1, j);
                 mbar_arrive_expect_tx(&v_full[s], kFaTile);
                 tma_load_3d(smem + kFaV + s * kFaTile, &tmV, &v_full[s], kvh * 64, j * 128, seq);
             }
@@ -180,18 +153,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int j = 0; ok && j <= nb; ++j) {
                 if (j < nb) {
                     const int s = j % kFaStages;
-                    FA_WHERE(3000 + j);
                     if (!(ok = mbar_wait(&k_full[s], uint32_t(j / kFaStages) & 1u, abort_flag, a.status,
                                          kErrTimeoutMma)))
                         break;
                     const uint64_t kd = smem_desc_sw128(smem + kFaK + s * kFaTile);
                     for (int h = 0; h < 2; ++h) {
-                        FA_WHERE(4000 + 100 * h + j);
                         if (j > 0 && !(ok = mbar_wait(&s_free[t * 2 + h], uint32_t(j - 1) & 1u, abort_flag,
                                                       a.status, kErrTimeoutMma)))
                             break;
                         tc_fence_after();
-                        if (h == 0) FA_STAMP(2 + t, j);
                         // keys 64h.. of the K tile start 64 rows = 8 KB in (8 x 1024 B swizzle atoms)
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
@@ -204,18 +174,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 }
                 if (j > 0) {
                     const int jj = j - 1, s = jj % kFaStages;
-                    FA_WHERE(5000 + jj);
                     if (!(ok = mbar_wait(&v_full[s], uint32_t(jj / kFaStages) & 1u, abort_flag, a.status,
                                          kErrTimeoutMma)))
                         break;
                     const uint64_t vd = smem_desc_sw128(smem + kFaV + s * kFaTile);
                     for (int h = 0; h < 2; ++h) {
-                        FA_WHERE(6000 + 100 * h + jj);
                         if (!(ok = mbar_wait(&p_full[t * 2 + h], uint32_t(jj) & 1u, abort_flag, a.status,
                                              kErrTimeoutMma)))
                             break;
                         tc_fence_after();
-                        if (h == 0) FA_STAMP(4 + t, jj);
                         const uint64_t pd = smem_desc_sw128(smem + kFaP + ((t * 2 + (jj & 1)) * 2 + h) * kFaTile);
 #pragma unroll
                         for (int k = 0; k < 4; ++k)
@@ -253,17 +220,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 const int kv = min(64, a.lk - j * 128 - h * 64);  // valid keys of this half (may be <= 0)
                 uint8_t* prow = smem + kFaP + ((t * 2 + (j & 1)) * 2 + h) * kFaTile + row * 128;
                 // this P buffer was last read by P V of block j - 2
-                FA_WHERE(7000 + j);
                 if (j >= 2) {
                     ok = mbar_wait(&my_pv[j & 1], uint32_t((j >> 1) - 1) & 1u, abort_flag, a.status,
                                    kErrTimeoutEpilogue);
                     if (!ok) break;
                 }
-                FA_WHERE(8000 + j);
                 ok = mbar_wait(my_s_full, uint32_t(j) & 1u, abort_flag, a.status, kErrTimeoutEpilogue);
                 if (!ok) break;
                 tc_fence_after();
-                if (wq == 0 && lane == 0) FA_STAMP(6 + 6 * h + t, j);
                 // max over this half's valid keys, scaled to log2 units (S reloaded from TMEM)
                 auto half_max = [&]() -> float {
                     float mx[8];
@@ -356,7 +320,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(my_s_free);
                 fence_proxy_async_smem();
-                if (wq == 0 && lane == 0) FA_STAMP(8 + 6 * h + t, j);
                 // P V of block j - 1 must be complete before P of block j is announced: it proves the
                 // MMA warp consumed the previous announcement (an mbarrier phase must not be
                 // completed twice before its waiter looks), and O is only rescaled after it
@@ -382,10 +345,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(my_p_full);
-                if (wq == 0 && lane == 0) FA_STAMP(10 + 6 * h + t, j);
             }
             // every warp of the tile reaches both named barriers below exactly once, aborted or not
-            FA_WHERE(9000);
             if (ok)
                 ok = mbar_wait(&my_pv[(nb - 1) & 1], uint32_t((nb - 1) >> 1) & 1u, abort_flag, a.status,
                                kErrTimeoutEpilogue);
@@ -393,9 +354,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             float2* ml = reinterpret_cast<float2*>(smem + kFaP + ((t * 2 + ((nb - 1) & 1)) * 2 + 1) * kFaTile) + row;
             if (h == 1) *ml = make_float2(m_used, l);
             const uint32_t tile_threads = 64u * uint32_t(vw[t]);
-            if (*abort_flag == 0) FA_WHERE(9100);
             named_bar_sync(1 + t, tile_threads);
-            if (*abort_flag == 0) FA_WHERE(9200);
             if (ok && h == 0) {
                 tc_fence_after();
                 const float2 o1 = *ml;
@@ -426,7 +385,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 fence_proxy_async_smem();
             }
             named_bar_sync(1 + t, tile_threads);
-            if (*abort_flag == 0) FA_WHERE(9300);
             if (h == 0 && wq == 0 && lane == 0 && *abort_flag == 0) {
                 tma_store_3d(&tmO, smem + kFaQ + t * kFaTile, head * 64, q0[t], seq);
                 bulk_commit_group();
@@ -434,7 +392,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             }
         }
     }
-    if (*abort_flag == 0) FA_WHERE(9900);
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {

@@ -22,18 +22,6 @@
 
 namespace b2d {
 
-// Optional per-k-block clock64 trace of CTA 0's first tile for profiling builds (-DB2D_GEMM_TRACE).
-#ifdef B2D_GEMM_TRACE
-__device__ unsigned long long g_gemm_trace[4 * 256];
-#define GEMM_STAMP(ev, i)                                                                       \
-    do {                                                                                        \
-        if (blockIdx.x == 0 && (i) < 256) g_gemm_trace[(ev) * 256 + (i)] = clock64();          \
-    } while (0)
-#else
-#define GEMM_STAMP(ev, i) \
-    do {                  \
-    } while (0)
-#endif
 
 
 enum EpiKind : int {
@@ -325,7 +313,6 @@ __global__ void __launch_bounds__(192, 1)
                 for (int i = 0; i < k_blocks; ++i) {
                     const int kb = kb0 + (rot + i < k_blocks ? rot + i : rot + i - k_blocks);
                     if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, ep.status, kErrTimeoutProducer)) goto done;
-                    GEMM_STAMP(0, (u / int(gridDim.x)) * k_blocks + i);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[stage], S::STAGE_BYTES);
                     tma_load_2d(sa, &tmA, &full[stage], kb * BK, m0);
@@ -351,7 +338,6 @@ __global__ void __launch_bounds__(192, 1)
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag, ep.status, kErrTimeoutMma)) goto done;
                     tc_fence_after();
-                    GEMM_STAMP(1, (u / int(gridDim.x)) * k_blocks + kb);
                     uint8_t* sa = smem + size_t(stage) * S::STAGE_BYTES;
                     const uint64_t adesc = smem_desc_sw128(sa);
                     const uint64_t bdesc = smem_desc_sw128(sa + S::A_BYTES);
@@ -392,9 +378,7 @@ __global__ void __launch_bounds__(192, 1)
             const int rbase = m0 + quarter * 32;
             const int rows_live = M - rbase < 32 ? M - rbase : 32;
             const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-            if (lane == 0 && quarter == 0) GEMM_STAMP(2, u / int(gridDim.x));
             epilogue_tile<BN, EPI, CT>(tbase, rbase, rows_live, n0, out_f32, ep, stg, lane, &tmO);
-            if (lane == 0 && quarter == 0) GEMM_STAMP(3, u / int(gridDim.x));
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
             acc ^= 1;

@@ -30,11 +30,16 @@ static __device__ __align__(256) float g_scratch[kNoAllocScratchFloats];
 // Status word for the kernel's bounded waits (cleared at the start of each call).
 static __device__ __align__(256) int g_status[64];
 
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
 struct DeviceSetup {
     bool done = false;
     float* scratch = nullptr;
     int* status = nullptr;
     int num_sms = 0;
+    EncodeFn encode = nullptr;
 };
 DeviceSetup g_setup[kMaxDevices];
 std::mutex g_setup_mutex;
@@ -66,26 +71,21 @@ b2d_status device_setup(int dev, DeviceSetup*& out, char* err, size_t err_len) {
             put_err(err, err_len, "cudaDeviceGetAttribute failed");
             return B2D_ECUDA;
         }
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !p) {
+            cudaGetLastError();
+            put_err(err, err_len, "cuTensorMapEncodeTiled entry point not found");
+            return B2D_ECUDA;
+        }
+        s.encode = reinterpret_cast<EncodeFn>(p);
         s.done = true;
     }
     out = &s;
     return B2D_OK;
 }
 
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-bool encode(CUtensorMap* m, const void* base, bool bf16, uint64_t rows, uint64_t k, uint32_t box_rows) {
-    static EncodeFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess || !p)
-            return false;
-        fn = reinterpret_cast<EncodeFn>(p);
-    }
+bool encode(EncodeFn fn, CUtensorMap* m, const void* base, bool bf16, uint64_t rows, uint64_t k, uint32_t box_rows) {
     const cuuint64_t dims[2] = {k, rows};
     const cuuint64_t strides[1] = {k * 2};
     const cuuint32_t box[2] = {64, box_rows};
@@ -95,15 +95,32 @@ bool encode(CUtensorMap* m, const void* base, bool bf16, uint64_t rows, uint64_t
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// out[r, c] = bias[c] + sum_s part[s, r, c]  (fixed order: deterministic)
+// out[r, c] = bias[c] + sum_s part[s, r, c]  (fixed order: deterministic).  When the GEMM gave up on a bounded
+// wait (status word non-zero) its partials are incomplete: the output is set to NaN instead of a plausible sum.
 static __global__ void noalloc_reduce_kernel(const float* __restrict__ part, int splits, int64_t m, int64_t n,
-                                             const float* __restrict__ bias, float* __restrict__ out, int64_t ldo) {
+                                             const float* __restrict__ bias, float* __restrict__ out, int64_t ldo,
+                                             const int* __restrict__ status) {
+    const bool failed = *reinterpret_cast<const volatile int*>(status) != 0;
     const int64_t total = m * n;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
         float v = bias ? bias[i % n] : 0.f;
         for (int s = 0; s < splits; ++s) v += part[s * total + i];
-        out[(i / n) * ldo + (i % n)] = v;
+        out[(i / n) * ldo + (i % n)] = failed ? __int_as_float(0x7fc00000) : v;
     }
+}
+
+// The bounded wait every kernel of the library uses, on an mbarrier nothing arrives on: it gives up after
+// `polls` polls and records a timeout code in the status word.  No fault is involved.
+static __global__ void noalloc_selftest_wait_kernel(uint32_t polls, int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, kErrTimeoutMma, polls);
 }
 
 template <int BN, typename CT>
@@ -166,8 +183,8 @@ extern "C" B2D_API b2d_status b2d_gemm_splitk_noalloc(int32_t bf16, const void* 
     b2d_status rc = device_setup(dev, ds, err, err_len);
     if (rc != B2D_OK) return rc;
     CUtensorMap ta, tb;
-    if (!encode(&ta, a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128) ||
-        !encode(&tb, b_dev, bf16 != 0, uint64_t(n), uint64_t(k), uint32_t(bn))) {
+    if (!encode(ds->encode, &ta, a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128) ||
+        !encode(ds->encode, &tb, b_dev, bf16 != 0, uint64_t(n), uint64_t(k), uint32_t(bn))) {
         put_err(err, err_len, "b2d_gemm_splitk_noalloc: cuTensorMapEncodeTiled failed");
         return B2D_ECUDA;
     }
@@ -194,9 +211,64 @@ extern "C" B2D_API b2d_status b2d_gemm_splitk_noalloc(int32_t bf16, const void* 
     }
     int64_t blocks = (m * n + 255) / 256;
     if (blocks > int64_t(ds->num_sms) * 8) blocks = int64_t(ds->num_sms) * 8;
-    noalloc_reduce_kernel<<<unsigned(blocks), 256, 0, st>>>(ds->scratch, splits, m, n, bias_dev, out_dev, ldo);
+    noalloc_reduce_kernel<<<unsigned(blocks), 256, 0, st>>>(ds->scratch, splits, m, n, bias_dev, out_dev, ldo,
+                                                            ds->status);
     if (cudaGetLastError() != cudaSuccess) {
         put_err(err, err_len, "b2d_gemm_splitk_noalloc: reduce launch failed");
+        return B2D_ECUDA;
+    }
+    return B2D_OK;
+}
+
+extern "C" B2D_API b2d_status b2d_gemm_splitk_noalloc_status(void* stream, char* err, size_t err_len) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        put_err(err, err_len, "b2d_gemm_splitk_noalloc_status: no current CUDA device");
+        return B2D_ENODEV;
+    }
+    DeviceSetup* ds = nullptr;
+    b2d_status rc = device_setup(dev, ds, err, err_len);
+    if (rc != B2D_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int code = 0;
+    if (cudaMemcpyAsync(&code, ds->status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
+        cudaGetLastError();
+        put_err(err, err_len, "b2d_gemm_splitk_noalloc_status: status read failed");
+        return B2D_ECUDA;
+    }
+    if (code == 0) return B2D_OK;
+    if (cudaMemsetAsync(ds->status, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+        cudaGetLastError();
+        put_err(err, err_len, "b2d_gemm_splitk_noalloc_status: status clear failed");
+        return B2D_ECUDA;
+    }
+    char msg[160];
+    std::snprintf(msg, sizeof(msg),
+                  "b2d_gemm_splitk_noalloc: device-side wait expired (code %d); the output was set to NaN", code);
+    put_err(err, err_len, msg);
+    return B2D_ETIMEOUT;
+}
+
+extern "C" B2D_API b2d_status b2d_gemm_splitk_noalloc_selftest_timeout(uint32_t polls, void* stream, char* err,
+                                                                        size_t err_len) {
+    if (polls == 0 || polls > (1u << 24)) {
+        put_err(err, err_len, "polls must be in [1, 2^24]");
+        return B2D_EINVAL;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        put_err(err, err_len, "no current CUDA device");
+        return B2D_ENODEV;
+    }
+    DeviceSetup* ds = nullptr;
+    b2d_status rc = device_setup(dev, ds, err, err_len);
+    if (rc != B2D_OK) return rc;
+    noalloc_selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(polls, ds->status);
+    if (cudaGetLastError() != cudaSuccess) {
+        put_err(err, err_len, "self-test launch failed");
         return B2D_ECUDA;
     }
     return B2D_OK;

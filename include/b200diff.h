@@ -300,7 +300,7 @@ B2D_API b2d_status b2d_oobleck_decode_device(b2d_ctx* ctx, const float* latents,
 
 /* ------------------------------------------ VibeVoice acoustic sigma-VAE decode */
 /* VibeVoiceTokenizerConfig fields of the acoustic tokenizer's decoder (include/engine/models/vibevoice/assets.h:
- * 15-37): stage s has n_filters << (n_stages - 1 - s) channels (multiples of 64 on this path), the decoder runs
+ * 15-37): stage s has n_filters << (n_stages - 1 - s) channels (n_filters a multiple of 32; stages narrower than 64 channels run zero-padded to 64), the decoder runs
  * the encoder depths reversed, and stage s > 0 is entered by a transposed conv with ratio ratios[s - 1]. */
 typedef struct {
     int64_t vae_dim;            /* 64 */
@@ -454,11 +454,25 @@ B2D_API b2d_status b2d_selftest_wait_timeout(b2d_ctx* ctx, uint32_t polls, void*
  *     clearing (each split writes its whole slice); the status word is cleared
  *     at the start of every call.
  *   - k % 64 == 0, bn in {64, 128, 256}, n % bn == 0, splits divides k / 64.
- *   - err / err_len (may be NULL / 0) receive a message when the call fails. */
+ *   - err / err_len (may be NULL / 0) receive a message when the call fails.
+ *   - The call returns once its kernels are queued.  If the GEMM's bounded
+ *     device-side wait expires, the kernel unwinds, records a code in the
+ *     array's status word and the output is written as NaN; call
+ *     b2d_gemm_splitk_noalloc_status after the stream to learn of it. */
 #define B2D_NOALLOC_SCRATCH_FLOATS (8ll * 1024 * 1024)
 B2D_API b2d_status b2d_gemm_splitk_noalloc(int32_t bf16, const void* a_dev, const void* b_dev, int64_t m, int64_t n,
                                            int64_t k, int32_t splits, int32_t bn, const float* bias_dev,
                                            float* out_dev, int64_t ldo, void* stream, char* err, size_t err_len);
+
+/* Waits for `stream`, then reads the status word of b2d_gemm_splitk_noalloc on the current device:
+ * B2D_OK, or B2D_ETIMEOUT with a message when a call's bounded wait expired (the word is then
+ * cleared).  Allocates nothing.  No counterpart in the reference. */
+B2D_API b2d_status b2d_gemm_splitk_noalloc_status(void* stream, char* err, size_t err_len);
+
+/* Test hook for the above: runs the library's bounded wait on an mbarrier nothing arrives on, with
+ * `polls` in [1, 2^24] as its limit, so that it gives up and records a timeout in the same status
+ * word (no GPU fault).  No counterpart in the reference. */
+B2D_API b2d_status b2d_gemm_splitk_noalloc_selftest_timeout(uint32_t polls, void* stream, char* err, size_t err_len);
 
 #ifdef __cplusplus
 }

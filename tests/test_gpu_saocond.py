@@ -9,9 +9,7 @@ import pytest
 from oracle import synth
 from tests.helpers import golden, rel_l2, weight_specs
 
-# The conditioner's device path compiles and its host logic is exercised on CPU, but it has not yet run on a B200;
-# it stays out of the GPU pass until its first supervised run.
-pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="device path not yet run on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("name", ["saocond_tiny", "saocond_tiny_b1_noneg"])

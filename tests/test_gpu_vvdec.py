@@ -43,7 +43,6 @@ def test_vvdec_decode_matches_reference(b2d, ctx, name):
 
 
 # The 32-channel stage of the released decoders runs zero-padded to a 64-column tile (RMS means over the true
-# channel count).  This case has not yet run on a B200; it stays out of the GPU pass until its first supervised run.
-@pytest.mark.skip(reason="zero-padded channel path not yet run on a B200")
+# channel count).
 def test_vvdec_decode_32_channel_stage_matches_reference(b2d, ctx):
     _check(b2d, ctx, "vvdec_tiny_c32")

@@ -10,9 +10,7 @@ import pytest
 from oracle import synth
 from tests.helpers import golden, rel_l2, weight_specs
 
-# The language model's device path compiles and its host logic builds, but it has not yet run on a B200; it stays
-# out of the GPU pass until its first supervised run.
-pytestmark = [pytest.mark.gpu, pytest.mark.skip(reason="device path not yet run on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("name", ["vvlm_tiny", "vvlm_tiny_mha_long"])

@@ -56,3 +56,26 @@ def test_noalloc_rejects_oversize(b2d, ctx):
     out = torch.zeros(m, n, device="cuda")
     st, msg = _noalloc(b2d, a, b, m, n, k, 2, 256, None, out)  # 2 * 4096 * 4096 floats > 8 Mi floats
     assert st == -1 and "exceeds the fixed scratch" in msg
+
+
+def test_noalloc_reports_an_expired_wait(b2d, ctx):
+    """A bounded device-side wait that expires is reported by b2d_gemm_splitk_noalloc_status (B2D_ETIMEOUT, then
+    cleared), not swallowed; the test drives the library's own bounded wait to its limit, with no GPU fault."""
+    L = b2d.lib()
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    err = C.create_string_buffer(256)
+    assert L.b2d_gemm_splitk_noalloc_status(s, err, 256) == 0, err.value
+    assert L.b2d_gemm_splitk_noalloc_selftest_timeout(1 << 12, s, err, 256) == 0, err.value
+    assert L.b2d_gemm_splitk_noalloc_status(s, err, 256) == -6
+    assert b"device-side wait expired" in err.value
+    assert L.b2d_gemm_splitk_noalloc_status(s, err, 256) == 0  # cleared after it was reported
+    # the next call on the shared array is exact again
+    m, n, k = 256, 256, 512
+    a = torch.randn(m, k, device="cuda").half()
+    b = torch.randn(n, k, device="cuda").half()
+    out = torch.empty(m, n, device="cuda")
+    st, msg = _noalloc(b2d, a, b, m, n, k, 2, 256, None, out)
+    assert st == 0, msg
+    assert L.b2d_gemm_splitk_noalloc_status(s, err, 256) == 0
+    ref = a.float() @ b.float().t()
+    assert float((out - ref).norm() / ref.norm()) < TOL
