@@ -139,10 +139,24 @@ CUtensorMap make_tmap(const void* base, bool bf16, uint64_t rows, uint64_t k, ui
 }
 
 // ------------------------------------------------------------ GEMM launcher
+// fp32 [rows][cols] matrix with row stride ld (elements) as 32 x 32 boxes, 128B swizzle (TMA epilogues).
+CUtensorMap make_tmap_f32_box32(const void* base, int64_t rows, int64_t cols, int64_t ld) {
+    CUtensorMap m{};
+    const cuuint64_t dims[2] = {uint64_t(cols), uint64_t(rows)};
+    const cuuint64_t strides[1] = {uint64_t(ld) * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(B2D_ECUDA, "cuTensorMapEncodeTiled (fp32 box) failed (%d)", int(r));
+    return m;
+}
+
 template <int BN, int EPI, typename CT>
 void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K, const EpiParams& ep,
                    int num_sms, cudaStream_t st) {
-    using S = GemmShape<BN>;
+    using S = GemmShape<BN, EPI>;
     set_smem_limit(gemm_tc_kernel<BN, EPI, CT>, int(S::SMEM_BYTES));
     const int splits = ep.splits > 1 ? ep.splits : 1;
     if ((K / 64) % splits) fail(B2D_EINVAL, "split-K %d does not divide the %lld K blocks", splits, (long long)(K / 64));
@@ -150,22 +164,23 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
     const int64_t tiles = ((M + 127) / 128) * (N / BN) * splits;
     if (tiles == 0) return;
     const int grid = int(tiles < num_sms ? tiles : num_sms);
-    // fp32 output through TMA stores when the output is a plain [M, ldo] fp32 matrix
-    CUtensorMap to{};
+    CUtensorMap to{}, tg{};
     EpiParams e = ep;
+    // fp32 output through TMA stores when the output is a plain [M, ldo] fp32 matrix
     if (EPI == EPI_F32 && S::TMA_F32_OUT && splits == 1 && !ep.seg_rows && ep.out &&
         reinterpret_cast<uintptr_t>(ep.out) % 16 == 0 && ep.ldo % 4 == 0 && ep.ldo >= N) {
-        const cuuint64_t dims[2] = {uint64_t(N), uint64_t(M)};
-        const cuuint64_t strides[1] = {uint64_t(ep.ldo) * 4};
-        const cuuint32_t box[2] = {32, 32};
-        const cuuint32_t estr[2] = {1, 1};
-        CUresult r = encode_fn()(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ep.out, dims, strides, box, estr,
-                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) fail(B2D_ECUDA, "cuTensorMapEncodeTiled (fp32 output) failed (%d)", int(r));
+        to = make_tmap_f32_box32(ep.out, M, N, ep.ldo);
         e.tma_out = 1;
     }
-    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, to, int(M), int(N), int(K), e);
+    // residual (and gate) through TMA boxes when both are plain 16-byte aligned fp32 matrices
+    if (EPI == EPI_RESID && !ep.gate_rows && reinterpret_cast<uintptr_t>(ep.resid) % 16 == 0 && ep.ldr % 4 == 0 &&
+        ep.ldr >= N && (!ep.gate || (reinterpret_cast<uintptr_t>(ep.gate) % 16 == 0 && ep.ldg % 4 == 0 &&
+                                     ep.ldg >= N))) {
+        to = make_tmap_f32_box32(ep.resid, M, N, ep.ldr);
+        if (ep.gate) tg = make_tmap_f32_box32(ep.gate, M, N, ep.ldg);
+        e.tma_resid = 1;
+    }
+    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, to, tg, int(M), int(N), int(K), e);
     CK(cudaGetLastError());
 }
 

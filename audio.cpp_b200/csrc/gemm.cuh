@@ -56,6 +56,11 @@ struct EpiParams {
     // EPI_F32 through TMA stores (the kernel's tmO map: fp32 [M rows][N cols], box 32 x 32, 128B
     // swizzle); set by the launcher when there is no split-K and no row remap.
     int tma_out = 0;
+    // EPI_RESID through TMA: the residual (tmO) and, when gate != nullptr, the gate (tmG) are loaded as
+    // 32 x 32 fp32 boxes into a per-warp ring while the accumulator is still being computed, updated in
+    // shared memory and written back by TMA stores; set by the launcher (no per-sequence gate rows,
+    // 16-byte aligned bases and strides).
+    int tma_resid = 0;
 };
 
 template <typename CT>
@@ -83,21 +88,129 @@ struct CtTraits<__nv_bfloat16> {
 // rounded to fp16/bf16 or consumed by an fp32 accumulation downstream).
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-template <int BN>
+// Residual epilogue staging: per epilogue warp four 4 KB boxes (a ring of 4 residual boxes, or of 2
+// residual + gate pairs) and, after all warps' boxes, 4 mbarriers per warp.
+constexpr uint32_t kResidBoxBytes = 4096;
+constexpr uint32_t kResidWarpBytes = 4 * kResidBoxBytes;
+constexpr size_t kResidStageBytes = 4 * kResidWarpBytes + 4 * 4 * 8;
+
+template <int BN, int EPI = -1>
 struct GemmShape {
     static constexpr int BM = 128;
     static constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
-    static constexpr int STAGES = BN >= 192 ? (BN == 192 ? 5 : 4) : (BN >= 128 ? 6 : 8);
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = BN * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr bool RESID_TMA = EPI == EPI_RESID;
+    // operand ring depth: as deep as fits next to the epilogue staging, at most 8
+    static constexpr int STAGES_FIT = int((232448 - 1024 - 256 - (RESID_TMA ? kResidStageBytes : 0)) /
+                                          STAGE_BYTES);
+    static constexpr int STAGES_DEF = BN >= 192 ? (BN == 192 ? 5 : 4) : (BN >= 128 ? 6 : 8);
+    static constexpr int STAGES = RESID_TMA ? (STAGES_FIT < 6 ? STAGES_FIT : 6) : STAGES_DEF;
     static constexpr uint32_t TMEM_COLS = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;  // power of two
     // Epilogue staging right after the operand ring (1024-aligned): per warp either a 32 x 33 fp32
-    // transpose buffer or, for the TMA-store fp32 path, two 128B-swizzled 32 x 32 fp32 boxes.
+    // transpose buffer or, for the TMA-store fp32 path, two 128B-swizzled 32 x 32 fp32 boxes; for the
+    // residual epilogue the TMA box ring (which also holds the fallback path's transpose buffers).
     static constexpr bool TMA_F32_OUT = BN != 192;  // the two 4 KB boxes per warp fit next to the ring
-    static constexpr size_t EPI_STAGE_BYTES = TMA_F32_OUT ? 4 * 2 * 4096 : 4 * 32 * 33 * 4;
+    static constexpr size_t EPI_STAGE_BYTES = RESID_TMA ? kResidStageBytes
+                                                        : (TMA_F32_OUT ? 4 * 2 * 4096 : 4 * 32 * 33 * 4);
     static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + EPI_STAGE_BYTES + 256 + 1024;
+    static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
+
+// Residual epilogue over all of this warp's units: x[r, n] += g[r, n] * (acc + bias[n]) on the fp32
+// residual stream, 32 x 32 boxes through TMA.  The warp keeps up to 4 (2 with a gate) box loads in flight
+// ahead of the chunk it is updating, including the next unit's first chunks, so the residual / gate reads
+// overlap the MMA main loop instead of following it.  Returns false when a wait gave up.
+template <int BN>
+__device__ __forceinline__ bool resid_tma_epilogue(uint32_t tmem_base, int quarter, int lane, uint8_t* boxes,
+                                                   uint64_t* bars, const CUtensorMap* tmR, const CUtensorMap* tmG,
+                                                   const EpiParams& ep, int m_tiles, int num_tiles, int num_units,
+                                                   uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag) {
+    constexpr int C = BN / 32;
+    const bool has_gate = ep.gate != nullptr;
+    const uint32_t nb = has_gate ? 2u : 4u;
+    const uint32_t slot_bytes = has_gate ? 2 * kResidBoxBytes : kResidBoxBytes;
+    int lu = blockIdx.x, lc = 0;  // next box load: unit, chunk
+    uint32_t ld_seq = 0, cs_seq = 0;
+    auto issue_next = [&]() {
+        if (lu >= num_units) return;
+        const int tile = lu % num_tiles;
+        const int m0 = (tile % m_tiles) * 128, n0 = (tile / m_tiles) * BN;
+        const uint32_t slot = ld_seq % nb;
+        uint8_t* box = boxes + slot * slot_bytes;
+        mbar_arrive_expect_tx(&bars[slot], slot_bytes);
+        tma_load_2d(box, tmR, &bars[slot], n0 + lc * 32, m0 + quarter * 32);
+        if (has_gate) tma_load_2d(box + kResidBoxBytes, tmG, &bars[slot], n0 + lc * 32, m0 + quarter * 32);
+        ++ld_seq;
+        if (++lc == C) {
+            lc = 0;
+            lu += gridDim.x;
+        }
+    };
+    if (lane == 0)
+        for (uint32_t i = 0; i < nb; ++i) issue_next();
+    const uint32_t sw = uint32_t(lane & 7);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+        const int tile = u % num_tiles;
+        const int m0 = (tile % m_tiles) * 128, n0 = (tile / m_tiles) * BN;
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.status, kErrTimeoutEpilogue)) return false;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+        for (int c = 0; c < C; ++c) {
+            float v[32];
+            tmem_ld_32x32b_x32(tbase + uint32_t(c * 32), v);
+            tmem_ld_wait();
+            if (c == C - 1) {  // the accumulator is in registers: hand TMEM back to the MMA warp
+                tc_fence_before();
+                mbar_arrive(&tempty[acc]);
+            }
+            if (ep.bias) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __ldg(ep.bias + n0 + c * 32 + j);
+            }
+            const uint32_t slot = cs_seq % nb;
+            if (!mbar_wait(&bars[slot], (cs_seq / nb) & 1u, abort_flag, ep.status, kErrTimeoutEpilogue)) return false;
+            uint8_t* rrow = boxes + slot * slot_bytes + lane * 128;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4* rp = reinterpret_cast<float4*>(rrow + ((uint32_t(q) ^ sw) << 4));
+                float4 r = *rp;
+                if (has_gate) {
+                    const float4 g = *reinterpret_cast<const float4*>(rrow + kResidBoxBytes + ((uint32_t(q) ^ sw) << 4));
+                    r.x += g.x * v[4 * q];
+                    r.y += g.y * v[4 * q + 1];
+                    r.z += g.z * v[4 * q + 2];
+                    r.w += g.w * v[4 * q + 3];
+                } else {
+                    r.x += v[4 * q];
+                    r.y += v[4 * q + 1];
+                    r.z += v[4 * q + 2];
+                    r.w += v[4 * q + 3];
+                }
+                *rp = r;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(tmR, boxes + slot * slot_bytes, n0 + c * 32, m0 + quarter * 32);
+                bulk_commit_group();
+                bulk_wait_read_all();  // the store has read the box: its slot takes the next load
+                issue_next();
+            }
+            __syncwarp();
+            ++cs_seq;
+        }
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+    return true;
+}
 
 // Drains one 128-row accumulator tile (this warp's 32 TMEM lanes at `tbase`) through the epilogue.
 template <int BN, int EPI, typename CT>
@@ -248,8 +361,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tbase, int rbase, int row
 template <int BN, int EPI, typename CT>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, int M, int N, int K, EpiParams ep) {
-    using S = GemmShape<BN>;
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG, int M, int N,
+                   int K, EpiParams ep) {
+    using S = GemmShape<BN, EPI>;
     constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES;
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert(EPI != EPI_SWIGLU || BN == 256, "SwiGLU tiles pair 128 + 128 columns");
@@ -280,6 +394,10 @@ __global__ void __launch_bounds__(192, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 128);
+        }
+        if constexpr (S::RESID_TMA) {
+            uint64_t* rb = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES + 4 * kResidWarpBytes);
+            for (int i = 0; i < 16; ++i) mbar_init(&rb[i], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -364,8 +482,17 @@ __global__ void __launch_bounds__(192, 1)
         // instruction reads/writes one contiguous 32-column row segment (coalesced, and the
         // residual read-modify-write issues all 32 rows' loads before any store instead of serialising).
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
+        if constexpr (S::RESID_TMA) {
+            if (ep.tma_resid) {
+                uint8_t* epi = smem + size_t(STAGES) * S::STAGE_BYTES;
+                resid_tma_epilogue<BN>(tmem_base, quarter, lane, epi + quarter * kResidWarpBytes,
+                                       reinterpret_cast<uint64_t*>(epi + 4 * kResidWarpBytes) + quarter * 4, &tmO,
+                                       &tmG, ep, m_tiles, num_tiles, num_units, tfull, tempty, abort_flag);
+                goto done;
+            }
+        }
         float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES +
-                                              quarter * (S::EPI_STAGE_BYTES / 4));
+                                              quarter * (S::RESID_TMA ? kResidWarpBytes : S::EPI_STAGE_BYTES / 4));
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = blockIdx.x; u < num_units; u += gridDim.x) {

@@ -139,7 +139,8 @@ b2d_status launch(const CUtensorMap& ta, const CUtensorMap& tb, int64_t m, int64
     const int64_t units = ((m + 127) / 128) * (n / BN) * splits;
     const int grid = int(units < num_sms ? units : num_sms);
     const CUtensorMap no_out{};  // split-K partials take the plain fp32 store path
-    gemm_tc_kernel<BN, EPI_F32, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, no_out, int(m), int(n), int(k), ep);
+    gemm_tc_kernel<BN, EPI_F32, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, no_out, no_out, int(m), int(n), int(k),
+                                                                       ep);
     return cudaGetLastError() == cudaSuccess ? B2D_OK : B2D_ECUDA;
 }
 

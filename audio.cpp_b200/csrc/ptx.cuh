@@ -98,6 +98,17 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
                  : "memory");
 }
 
+// 2-D tiled store from shared memory (bulk group); rows / columns outside the map's extent are not written.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
+// Waits until every committed bulk store has finished writing global memory.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until every committed bulk store finished reading its shared-memory source.

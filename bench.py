@@ -121,7 +121,7 @@ def bench_reference(args):
     from oracle import ref_runner, synth
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
     threads = os.cpu_count() or 1
-    frames = 128  # bounded sample of the 1024-frame workload (same weights, 10 steps, CFG)
+    frames = cfg.frames  # the full 1024-frame call (same weights, inputs, 10 steps, CFG) -- about 7 s on 16 cores
     if not ref_runner.available():
         print(json.dumps({"impl": "reference", "unavailable": "reference CPU build (oracle/_ref) not present"}))
         return
@@ -132,7 +132,7 @@ def bench_reference(args):
             "warmup": args.warmup, "ms_per_step": float(timed.mean()), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 graph, Q8_0 weights (ggml CPU)", "data": "synthetic",
             "impl": "reference",
-            "config": config_json(cfg, 1, {"sample_frames": frames}),
+            "config": config_json(cfg, 1),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
                              "sample": "%d frames x %d DPM steps x CFG per call, audio.cpp ggml CPU build (%s)" % (
                                  frames, cfg.steps, variant)},
@@ -174,6 +174,7 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
 
 
 DIT_WORKLOAD = "sao_bf16_1x1024"
+RESID_TRAFFIC_DIT = None  # filled from the ncu capture of the three residual-GEMM launches
 
 
 def gemm_time(b2d, ctx, torch, M, N, K, epilogue, bn=256, bf16=False, reps=30):
@@ -181,11 +182,16 @@ def gemm_time(b2d, ctx, torch, M, N, K, epilogue, bn=256, bf16=False, reps=30):
     dt = torch.bfloat16 if bf16 else torch.float16
     a = torch.randn(M, K, device="cuda").to(dt)
     w = (torch.randn(N, K, device="cuda") * 0.02).to(dt)
-    out = torch.empty(M, N, device="cuda")
+    out = torch.zeros(M, N, device="cuda")
+    bias = torch.zeros(N, device="cuda")
     st = torch.cuda.current_stream()
     ldo = N // 2 if epilogue == b2d.EPI_SWIGLU else N
-    launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, bf16=bf16, epilogue=epilogue, bn=bn,
-                              out=out.data_ptr(), ldo=ldo, stream=st.cuda_stream)
+    if epilogue == b2d.EPI_RESID:  # x[M, N] += acc + bias, fp32 residual stream read and written in place
+        launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, bf16=bf16, epilogue=epilogue, bn=bn,
+                                  bias=bias.data_ptr(), resid=out.data_ptr(), ldr=N, stream=st.cuda_stream)
+    else:
+        launch = lambda: ctx.gemm(a.data_ptr(), w.data_ptr(), M, N, K, bf16=bf16, epilogue=epilogue, bn=bn,
+                                  out=out.data_ptr(), ldo=ldo, stream=st.cuda_stream)
     for _ in range(3):
         launch()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -240,14 +246,31 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     assert np.isfinite(out_host.numpy()).all()
     if rank == 0:
         R = 2 * cfg.batch * (cfg.latent_tokens + 1)
-        t_ff = gemm_time(b2d, ctx, torch, R, 8 * cfg.embed_dim, cfg.embed_dim, b2d.EPI_SWIGLU, bn=512, bf16=True)
-        fl = 2.0 * R * 8 * cfg.embed_dim * cfg.embed_dim
+        # The dominant kernel of the DiT step (largest device-time share in the launch list): the gated-residual GEMM
+        # gemm_tc_kernel<192, RESID>, launched three times per layer -- self-attention out (K = d), cross-attention
+        # out (K = d) and FF out (K = 4d), each x += acc + b on the fp32 residual stream.  Reported over those three
+        # launches: their FLOPs / their summed event time.
+        d = cfg.embed_dim
+        t_o = gemm_time(b2d, ctx, torch, R, d, d, b2d.EPI_RESID, bn=192, bf16=True)
+        t_f = gemm_time(b2d, ctx, torch, R, d, 4 * d, b2d.EPI_RESID, bn=192, bf16=True)
+        fl = 2.0 * R * d * d * 2 + 2.0 * R * d * 4 * d
+        t = 2 * t_o + t_f
         peak = peaks.get("bf16_tflops", 1590.0)
-        res["roofline"] = {"kernel": "gemm_tc2_kernel<SWIGLU,bf16> 2-SM (FFN in, %dx%dx%d)" % (R, 8 * cfg.embed_dim,
-                                                                                            cfg.embed_dim),
-                           "bound": "tensor", "achieved": round(fl / t_ff / 1e12, 1), "peak": peak,
-                           "unit": "TFLOP/s", "frac": round(fl / t_ff / 1e12 / peak, 4), "traffic": None}
-        if not args.no_cpu_baseline:
+        res["roofline"] = {"kernel": "gemm_tc_kernel<192,RESID,bf16> (out-proj %dx%dx%d x2, FF-out %dx%dx%d)"
+                                     % (R, d, d, R, d, 4 * d),
+                           "bound": "tensor", "achieved": round(fl / t / 1e12, 1), "peak": peak,
+                           "unit": "TFLOP/s", "frac": round(fl / t / 1e12 / peak, 4),
+                           "launch_us": {"out_proj": round(t_o * 1e6, 2), "ff_out": round(t_f * 1e6, 2)},
+                           "flop_per_layer": fl,
+                           # dram__bytes_read.sum + dram__bytes_write.sum summed over the three launches (ncu,
+                           # profiles/gemm_resid_sao_bf16_1x1024.md)
+                           "traffic": RESID_TRAFFIC_DIT, "traffic_unit": "bytes per layer (3 launches)"}
+        t_ff = gemm_time(b2d, ctx, torch, R, 8 * d, d, b2d.EPI_SWIGLU, bn=512, bf16=True)
+        fl_ff = 2.0 * R * 8 * d * d
+        res["ffn_in_gemm"] = {"kernel": "gemm_tc2_kernel<SWIGLU,bf16> 2-SM (FFN in, %dx%dx%d)" % (R, 8 * d, d),
+                              "achieved": round(fl_ff / t_ff / 1e12, 1), "unit": "TFLOP/s",
+                              "frac": round(fl_ff / t_ff / 1e12 / peak, 4)}
+        if not args.no_cpu_baseline and world == 1:
             from oracle import ref_runner
             if ref_runner.available():
                 c1 = synth.DitConfig(**{**cfg.__dict__, "steps": 1})
@@ -314,7 +337,7 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
            "gpu_launches_per_call": 18 + 5 * cfg.depth + cfg.steps * (7 + 14 * cfg.depth),
            "whole_call_tflops": round(seq_steps / world * cfg.depth * fl / (ms / 1e3) / 1e12, 1)}
     assert np.isfinite(out_host.numpy()).all()
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
         from oracle import ref_runner
         if ref_runner.available():
             c1 = synth.Sa3Config(**{**cfg.__dict__, "steps": 1})
@@ -375,7 +398,7 @@ def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
            "gpu_launches_per_call": 4 + 7 * len(cfg.strides),
            "whole_call_tflops": round(fl / (ms / 1e3) / 1e12, 1)}
     assert np.isfinite(h_out.numpy()).all()
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
         from oracle import ref_runner
         if ref_runner.available():
             c1 = synth.OobleckConfig(**{**cfg.__dict__, "latent_tokens": 16})
@@ -387,6 +410,173 @@ def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
                                    "sample": "16 of the 1024 latents (%d frames), audio.cpp ggml CPU (%s)"
                                              % (f1, ref_runner.variant())}
     return res
+
+
+def _parallel_module():
+    spec = importlib.util.spec_from_file_location("b2d_parallel", os.path.join(ROOT, "audio.cpp_b200", "parallel.py"))
+    par = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(par)
+    return par
+
+
+GT = {0: 0, 1: 1, 3: 8, 2: 30}  # bundle dtype -> ggml type id
+
+
+def head_weight_bytes_per_step(cfg, bytes_per_weight=2.0):
+    """Weights one denoising step must stream: every layer's adaLN [3H, H], gate/up [F, H], down [H, F], the final
+    adaLN [2H, H], final linear [64, H] and noisy_images_proj [H, 64] (cond_proj and the timestep MLP are once per
+    call), at the resident operand width."""
+    H, F, L = cfg.hidden, cfg.ffn, cfg.latent
+    return bytes_per_weight * (cfg.layers * (3 * H * H + 3 * F * H) + 2 * H * H + 2 * L * H)
+
+
+def bench_c1(args, torch, b2d, ctx, world, rank, timed, peaks):
+    """C1: VibeVoice-1.5B head, F16 weights, 64 frames (128 head rows), 10 steps, CFG 1.3.  Weight streaming:
+    judged on weight bytes per call against the measured HBM copy bandwidth.  Per rank its own 64 frames."""
+    from oracle import synth
+    cfg = synth.HEAD_CONFIGS["vv15_f16_64"]
+    w = synth.head_weights(cfg)
+    inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
+    head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
+                                      weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
+    del w
+    keys = ("positive_condition", "negative_condition", "initial_speech")
+    dev = [torch.from_numpy(inp[k].array().copy()).cuda() for k in keys]
+    host = [torch.from_numpy(inp[k].array().copy()).pin_memory() for k in keys]
+    out_dev = torch.empty(cfg.frames, 64, device="cuda")
+    out_host = torch.empty(cfg.frames, 64).pin_memory()
+    st = torch.cuda.current_stream()
+    ms = timed(lambda: head.sample_device(*dev, cfg.steps, cfg.cfg, out_dev, stream=st.cuda_stream), 20, 5)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(lambda: head.sample(*host, cfg.steps, cfg.cfg, out=out_host, stream=st.cuda_stream), 20, 3)
+    assert np.isfinite(out_host.numpy()).all()
+    wbytes = head_weight_bytes_per_step(cfg) * cfg.steps + 2.0 * (cfg.hidden * cfg.hidden + cfg.hidden * 256 +
+                                                                  cfg.hidden * cfg.hidden)
+    peak = peaks.get("hbm_gbs", 6650.0)
+    ach = wbytes / (ms / 1e3) / 1e9
+    frames = cfg.frames * world
+    res = {"metric": "latent frames/sec (VibeVoice diffusion head, C1 weight streaming)",
+           "value": round(frames / (ms / 1e3), 1), "unit": "frames/s", "ms_per_call": round(ms, 4),
+           "timed_calls": 20, "warmup_calls": 5,
+           "config": {"workload": "vv15_f16_64", "model": "VibeVoice-1.5B diffusion head (random-init)",
+                      "weights": "f16", "frames_per_rank": cfg.frames, "head_rows_per_rank": 2 * cfg.frames,
+                      "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg, "n_gpus": world},
+           "dtype": "f16 tensor-core operands, fp32 accumulate",
+           "e2e": {"value": round(frames / (ms_e2e / 1e3), 1), "unit": "frames/s",
+                   "h2d_bytes_per_step": sum(t.numel() * 4 for t in host), "d2h_bytes_per_step": out_host.numel() * 4,
+                   "api": "b2d_vv_sample (host buffers, pinned)"},
+           "roofline": {"kernel": "whole sampling call (weight stream)", "bound": "hbm", "achieved": round(ach, 1),
+                        "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                        "algorithmic_bytes_per_call": wbytes,
+                        "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback 6650"}}
+    return res
+
+
+def bench_c5(args, torch, b2d, ctx, world, rank, timed, peaks):
+    """C5: VibeVoice-7B-shaped head (H 3584), Q8_0, 8192 frames split over the ranks (strong scaling: the job is
+    fixed), 10 steps, CFG 1.3, plus the final gather of all latents to every rank inside the timed region."""
+    from oracle import synth
+    par = _parallel_module()
+    cfg = synth.HEAD_CONFIGS["vv7_q8_8192"]
+    w = synth.head_weights(cfg)
+    head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
+                                      weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
+    del w
+    inp = synth.head_inputs(cfg)
+    pos, neg, init, (lo, hi) = par.shard_head_inputs(inp["positive_condition"].array(),
+                                                     inp["negative_condition"].array(),
+                                                     inp["initial_speech"].array(), world, rank)
+    del inp
+    n = hi - lo
+    dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (pos, neg, init)]
+    host = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in (pos, neg, init)]
+    out_dev = torch.empty(n, 64, device="cuda")
+    out_host = torch.empty(n, 64).pin_memory()
+    st = torch.cuda.current_stream()
+
+    def job():
+        head.sample_device(*dev, cfg.steps, cfg.cfg, out_dev, stream=st.cuda_stream)
+        return par.gather_rows(out_dev, cfg.frames, world)
+
+    def job_e2e():
+        return head.sample(*host, cfg.steps, cfg.cfg, out=out_host, stream=st.cuda_stream)
+
+    calls = 5
+    ms = timed(job, calls, 2)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(job_e2e, calls, 1)
+    full = job()
+    assert full.shape == (cfg.frames, 64) and bool(torch.isfinite(full).all())
+    fl = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
+    peak = peaks.get("bf16_tflops", 1590.0)
+    tf = fl / (ms / 1e3) / 1e12 / world
+    return {"metric": "latent frames/sec (VibeVoice-7B head, C5 strong scaling)",
+            "value": round(cfg.frames / (ms / 1e3), 1), "unit": "frames/s", "ms_per_call": round(ms, 3),
+            "timed_calls": calls, "warmup_calls": 2, "scaling": "strong",
+            "config": {"workload": "vv7_q8_8192", "model": "VibeVoice-7B-shaped diffusion head (random-init)",
+                       "weights": "q8_0", "hidden": cfg.hidden, "global_frames": cfg.frames,
+                       "frames_per_rank": n, "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg, "n_gpus": world,
+                       "parallelism": "dp%d (frames sharded, CFG pairs kept per rank; one all_gather timed)" % world},
+            "dtype": "f16 tensor-core operands (Q8_0 dequantised), fp32 accumulate",
+            "e2e": {"value": round(cfg.frames / (ms_e2e / 1e3), 1), "unit": "frames/s",
+                    "h2d_bytes_per_step": sum(t.numel() * 4 for t in host), "d2h_bytes_per_step": n * 64 * 4,
+                    "api": "b2d_vv_sample (host buffers, pinned), each rank its shard (no gather)"},
+            "per_gpu_tflops": round(tf, 1), "per_gpu_frac_of_bf16_peak": round(tf / peak, 4)}
+
+
+def bench_c4(args, torch, b2d, ctx, world, rank, timed, peaks):
+    """C4: SAO-1.0 DiT, Q8_0, 16 prompts (seeds 0-15) + CFG = 32 sequences x 1025 tokens, 100 DPM++ 2M steps,
+    prompts split over the ranks (strong scaling), plus the final gather of all latents inside the timed region."""
+    from oracle import synth
+    par = _parallel_module()
+    cfg = synth.DIT_CONFIGS["sao_q8_16x1024"]
+    if args.dit_dpm_steps:
+        cfg = synth.DitConfig(**{**cfg.__dict__, "steps": args.dit_dpm_steps})
+    w = synth.dit_weights(cfg)
+    dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
+                             cfg.io_channels, cfg.prompt_max_length,
+                             weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
+    del w
+    inp = synth.dit_inputs(cfg)
+    keys = ("noise", "padding_mask", "cross_positive", "cross_negative", "global")
+    local, (lo, hi) = par.shard_prompts([inp[k].array() for k in keys], cfg.batch, world, rank)
+    dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in local]
+    host = [torch.from_numpy(np.ascontiguousarray(a)).pin_memory() for a in local]
+    out_dev = torch.empty_like(dev[0])
+    out_host = torch.empty(dev[0].shape).pin_memory()
+    st = torch.cuda.current_stream()
+    kw = dict(steps=cfg.steps, sigma_min=cfg.sigma_min, sigma_max=cfg.sigma_max, rho=cfg.rho, cfg_scale=cfg.cfg,
+              apg_scale=cfg.apg, stream=st.cuda_stream)
+
+    def job():
+        dit.sample_device(*dev, out_dev, **kw)
+        return par.gather_rows(out_dev, cfg.batch, world)
+
+    def job_e2e():
+        return dit.sample(*host, out=out_host, **kw)
+
+    ms = timed(job, 1, 1)
+    ctx.sync(st.cuda_stream)
+    ms_e2e = timed(job_e2e, 1, 0)
+    full = job()
+    assert tuple(full.shape) == (cfg.batch, 64, cfg.latent_tokens) and bool(torch.isfinite(full).all())
+    seq_steps = 2 * cfg.batch * cfg.steps
+    peak = peaks.get("bf16_tflops", 1590.0)
+    tf = seq_steps * 2.264e12 / (ms / 1e3) / 1e12 / world
+    return {"metric": "denoise sequence-steps/sec (DiT, C4 strong scaling)",
+            "value": round(seq_steps / (ms / 1e3), 2), "unit": "seq-steps/s", "ms_per_call": round(ms, 2),
+            "timed_calls": 1, "warmup_calls": 1, "scaling": "strong",
+            "prompt_steps_per_s": round(seq_steps / 2 / (ms / 1e3), 2),
+            "config": {"workload": "sao_q8_16x1024" + ("_%dsteps" % cfg.steps if args.dit_dpm_steps else ""),
+                       "model": "Stable-Audio-Open-1.0-shaped DiT (random-init)", "weights": "q8_0",
+                       "prompts": cfg.batch, "prompts_per_rank": hi - lo, "tokens": cfg.latent_tokens + 1,
+                       "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg, "apg_scale": cfg.apg, "n_gpus": world,
+                       "parallelism": "dp%d (prompt pairs sharded; one all_gather timed)" % world},
+            "dtype": "f16 tensor-core operands (Q8_0 dequantised), fp32 accumulate",
+            "e2e": {"value": round(seq_steps / (ms_e2e / 1e3), 2), "unit": "seq-steps/s",
+                    "h2d_bytes_per_step": sum(t.numel() * 4 for t in host), "d2h_bytes_per_step": out_host.numel() * 4,
+                    "api": "b2d_dit_sample (host buffers, pinned), each rank its shard (no gather)"},
+            "per_gpu_tflops": round(tf, 1), "per_gpu_frac_of_bf16_peak": round(tf / peak, 4)}
 
 
 def make_timer(torch, args, world, st):
@@ -433,13 +623,19 @@ def bench_dit_only(args, torch, b2d, world, rank, local):
         timer = make_timer(torch, args, world, st)
         if args.workload == "sa3":
             res = bench_sa3(args, torch, b2d, ctx, world, rank, timer)
+        elif args.workload == "c1":
+            res = bench_c1(args, torch, b2d, ctx, world, rank, timer, peaks)
+        elif args.workload == "c4":
+            res = bench_c4(args, torch, b2d, ctx, world, rank, timer, peaks)
+        elif args.workload == "c5":
+            res = bench_c5(args, torch, b2d, ctx, world, rank, timer, peaks)
         elif args.workload == "oobleck":
             res = bench_oobleck(args, torch, b2d, ctx, world, rank, timer)
         else:
             res = bench_dit(args, torch, b2d, ctx, world, rank, timer, peaks)
     if rank == 0:
         res.update({"n_gpus": world, "steps": res["timed_calls"], "warmup": res["warmup_calls"],
-                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "higher_is_better": True, "scaling": res.get("scaling", "weak"), "vs_baseline": None,
                     "data": "synthetic (seeded random weights and inputs)", "clocks": clk.summary()})
         print(json.dumps(res))
     ctx.close()
@@ -457,7 +653,7 @@ def bench_ours(args):
     b2d = load_package()
     from oracle import synth  # seeded synthetic weights/inputs (no checkpoints here)
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
-    if args.workload in ("dit", "sa3", "oobleck"):
+    if args.workload in ("dit", "sa3", "oobleck", "c1", "c4", "c5"):
         return bench_dit_only(args, torch, b2d, world, rank, local)
     w = synth.head_weights(cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
@@ -543,10 +739,14 @@ def bench_ours(args):
     dit_res = None
     if args.workload in ("all", "dit"):
         dit_res = bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks)
-    sa3_res = oob_res = None
+    extra = {}
     if args.workload == "all":
-        sa3_res = bench_sa3(args, torch, b2d, ctx, world, rank, timed)
-        oob_res = bench_oobleck(args, torch, b2d, ctx, world, rank, timed)
+        extra["sa3"] = bench_sa3(args, torch, b2d, ctx, world, rank, timed)
+        extra["oobleck"] = bench_oobleck(args, torch, b2d, ctx, world, rank, timed)
+        extra["c1"] = bench_c1(args, torch, b2d, ctx, world, rank, timed, peaks)
+        extra["c5"] = bench_c5(args, torch, b2d, ctx, world, rank, timed, peaks)
+        if not args.no_c4:
+            extra["c4"] = bench_c4(args, torch, b2d, ctx, world, rank, timed, peaks)
     if rank == 0:
         roof = gemm_roofline(b2d, ctx, torch, cfg, peaks)
         flops_call = 2.0 * cfg.frames * cfg.steps * (100 * cfg.hidden ** 2 + 256 * cfg.hidden)
@@ -562,19 +762,16 @@ def bench_ours(args):
                 "roofline": roof,
                 "whole_call_tflops": round(flops_call / (ms / 1e3) / 1e12, 1),
                 "clocks": clk.summary()}
-        if not args.no_cpu_baseline:
-            frames = 128
-            cms, variant = run_cpu_reference(cfg, frames, 2, os.cpu_count() or 1)
-            v = frames / (float(np.mean(cms[1:])) / 1e3)
+        if not args.no_cpu_baseline and world == 1:
+            frames = cfg.frames  # the whole 1024-frame call, as the GPU arm runs it
+            cms, variant = run_cpu_reference(cfg, frames, 4, os.cpu_count() or 1)
+            v = frames / (float(np.median(cms[1:])) / 1e3)
             line["cpu_baseline"] = {"value": round(v, 2), "unit": UNIT, "cores": os.cpu_count(), "kind": "reference",
-                                    "sample": "%d of the 1024 frames, 10 DPM steps + CFG, audio.cpp ggml CPU (%s), "
-                                              "1 warm-up + 1 timed call" % (frames, variant)}
+                                    "sample": "the full %d-frame call, 10 DPM steps + CFG, audio.cpp ggml CPU (%s), "
+                                              "1 warm-up + median of 3 timed calls" % (frames, variant)}
         if dit_res is not None:
             line["dit"] = dit_res
-        if sa3_res is not None:
-            line["sa3"] = sa3_res
-        if oob_res is not None:
-            line["oobleck"] = oob_res
+        line.update(extra)
         print(json.dumps(line))
     ctx.close()
     if world > 1:
@@ -588,9 +785,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="all", choices=["all", "head", "dit", "sa3", "oobleck"],
-                    help="all = head line with the DiT and SA3 results attached; head = VibeVoice head only; "
-                         "dit / sa3 / oobleck = only that path")
+    ap.add_argument("--workload", default="all", choices=["all", "head", "dit", "sa3", "oobleck", "c1", "c4", "c5"],
+                    help="all = head line (C2) with the C3 DiT, SA3, Oobleck, C1, C5 and C4 results attached; "
+                         "head = VibeVoice head only; dit / sa3 / oobleck / c1 / c4 / c5 = only that workload")
+    ap.add_argument("--no-c4", action="store_true", help="leave the C4 leg (16-prompt Q8_0 DiT) out of 'all'")
     ap.add_argument("--dit-steps", type=int, default=3, help="timed DiT sampling calls (each 100 DPM++ steps)")
     ap.add_argument("--dit-dpm-steps", type=int, default=0,
                     help="profiling only: DPM++ steps per DiT call instead of the workload's 100")

@@ -99,6 +99,8 @@ HEAD_CONFIGS = {
     "vv15_q8_1024": HeadConfig(wtype=Q8_0, frames=1024),
     "vv7_q8_8192": HeadConfig(hidden=3584, wtype=Q8_0, frames=8192),
     # C5's 7B width (hidden 3584, F = 10752, adaLN N = 50176) at 32 frames and 3 steps: parity at that shape
+    # C5's per-rank share at 8 GPUs (1024 of the 8192 frames, 7B width, all 10 steps): full-length parity
+    "vv7_q8_1024": HeadConfig(hidden=3584, wtype=Q8_0, frames=1024),
     "vv7_q8_32_3steps": HeadConfig(hidden=3584, wtype=Q8_0, frames=32, steps=3, wseed=7, cseed=8, xseed=9),
     # small parity configs
     "tiny_f16": HeadConfig(hidden=256, wtype=F16, frames=8),
@@ -191,6 +193,10 @@ DIT_CONFIGS = {
     "sao_q8_16x1024": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16))),
     # full-size parity cases (BASELINE C3/C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
     "sao_bf16_1x1024_2steps": DitConfig(steps=2),
+    # C3 in full (100 DPM++ 2M steps), with APG (the reference default) and as plain CFG
+    "sao_bf16_1x1024_noapg": DitConfig(apg=0.0),
+    # C4 at its full latent length: 16 prompts + CFG = 32 sequences x 1025 tokens, Q8_0, 2 steps
+    "sao_q8_16x1024_2steps": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16)), steps=2),
     "sao_q8_1x1024_2steps": DitConfig(wtype=Q8_0, steps=2, prompt_seeds=(5,)),
     # C4's batch (16 prompts + CFG = 32 sequences, Q8_0, full width and depth) at 64 latent frames, 2 steps
     "sao_q8_16x64_2steps": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16)), latent_tokens=64, steps=2),
@@ -486,6 +492,9 @@ OOBLECK_CONFIGS = {
     # upsampling), one 1024-latent generation (47.5 s of 44.1 kHz stereo)
     "oobleck_bench_sao_1x1024": OobleckConfig(channels=128, c_mults=(1, 2, 4, 8, 16), strides=(2, 4, 4, 8, 8),
                                               latent_tokens=1024, wseed=15, seed=16),
+    # parity at the bench's channel / stride shape on a short latent (16 latents -> 32768 frames)
+    "oobleck_sao_shape_1x16": OobleckConfig(channels=128, c_mults=(1, 2, 4, 8, 16), strides=(2, 4, 4, 8, 8),
+                                            latent_tokens=16, wseed=15, seed=17),
 }
 
 OP = "pretransform.model.decoder.layers."

@@ -29,9 +29,10 @@ from oracle import dit, oobleck, ref_runner, sa3, saocond, synth, vibevoice, vvd
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 HEAD_GOLDENS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_frame_f16", "one_step_q8",
-                "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps"]
+                "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps", "vv7_q8_1024"]
 DIT_GOLDENS = ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "tiny_bf16_vddim", "tiny_f16_3msde",
-               "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps"]
+               "sao_bf16_1x1024_2steps", "sao_q8_1x1024_2steps", "sao_q8_16x64_2steps",
+               "sao_q8_16x1024_2steps", "sao_bf16_1x1024", "sao_bf16_1x1024_noapg"]
 SA3_GOLDENS = [n for n in synth.SA3_CONFIGS if "bench" not in n]
 OOBLECK_GOLDENS = [n for n in synth.OOBLECK_CONFIGS if "bench" not in n]
 VVDEC_GOLDENS = [n for n in synth.VVDEC_CONFIGS if "bench" not in n]
