@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_splitk_noalloc", "b2d_gemm_splitk_noalloc_status", "b2d_gemm_splitk_noalloc_selftest_timeout", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
+            "b2d_gemm", "b2d_gemm_stream", "b2d_gemm_splitk_noalloc", "b2d_gemm_splitk_noalloc_status", "b2d_gemm_splitk_noalloc_selftest_timeout", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
             "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
             "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device",
@@ -144,6 +144,7 @@ def lib() -> C.CDLL:
         L.b2d_vv_sample_device.argtypes = [P, P, P, P, I64, I64, F, P, P]
         L.b2d_q8_0_dequantize.argtypes = [P, P, I64, I64, P, P]
         L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
+        L.b2d_gemm_stream.argtypes = [P, I32, P, P, I32, I64, I64, I64, I32, I32, I32, P, P, I64, P, I64, P, I64, P]
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
         L.b2d_gemm_splitk_noalloc_status.argtypes = [P, C.c_char_p, C.c_size_t]
@@ -253,6 +254,17 @@ class Context:
         self.check(lib().b2d_gemm(self._h, int(bf16), C.c_void_p(a_dev), C.c_void_p(b_dev), m, n, k, epilogue, bn,
                                   C.c_void_p(bias or None), C.c_void_p(out or None), ldo, C.c_void_p(resid or None),
                                   ldr, C.c_void_p(gate or None), ldg, C.c_void_p(stream)))
+
+
+    def gemm_stream(self, a_dev: int, w_dev: int, m: int, n: int, k: int, *, w_type: int, bf16: bool = False,
+                    epilogue: int = EPI_F32, bn: int = 0, split: int = 1, bias: int = 0, out: int = 0, ldo: int = 0,
+                    resid: int = 0, ldr: int = 0, gate: int = 0, ldg: int = 0, stream: int = 0) -> None:
+        """Weight-streaming GEMM (M <= 128); w_type = ggml type id of W on the device (1 F16, 30 BF16, 8 Q8_0);
+        bn = 0 plans the tile width and K split itself."""
+        self.check(lib().b2d_gemm_stream(self._h, int(bf16), C.c_void_p(a_dev), C.c_void_p(w_dev), w_type, m, n, k,
+                                         epilogue, bn, split, C.c_void_p(bias or None), C.c_void_p(out or None), ldo,
+                                         C.c_void_p(resid or None), ldr, C.c_void_p(gate or None), ldg,
+                                         C.c_void_p(stream)))
 
 
 WeightSpec = Tuple[str, int, Tuple[int, ...], np.ndarray]  # (name, ggml type, dims, raw payload)

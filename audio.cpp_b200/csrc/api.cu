@@ -25,6 +25,7 @@
 #include "t5_kernels.cuh"
 #include "lm_kernels.cuh"
 #include "gemm.cuh"
+#include "gemm_stream.cuh"
 #include "kernels.cuh"
 
 using namespace b2d;
@@ -84,6 +85,46 @@ struct DevBuf {
     template <typename T>
     T* as() const { return static_cast<T*>(p); }
 };
+
+// ------------------------------------------------------ kernel launches
+// Launches inside a PdlScope carry the programmatic-stream-serialization attribute: the next kernel may start
+// its prologue (and its constant-weight loads) while this one finishes; every kernel launched this way calls
+// pdl_wait before touching data of its predecessors.  Per host thread, so concurrent contexts do not interact.
+thread_local bool tl_pdl = false;
+
+struct PdlScope {
+    bool prev;
+    PdlScope() : prev(tl_pdl) { tl_pdl = true; }
+    ~PdlScope() { tl_pdl = prev; }
+};
+
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+              Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = unsigned(cluster_x);
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    if (tl_pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = unsigned(n);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) fail(B2D_ECUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+}
 
 // ---------------------------------------------------------- TMA descriptors
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -180,8 +221,8 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
         if (ep.gate) tg = make_tmap_f32_box32(ep.gate, M, N, ep.ldg);
         e.tma_resid = 1;
     }
-    gemm_tc_kernel<BN, EPI, CT><<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, to, tg, int(M), int(N), int(K), e);
-    CK(cudaGetLastError());
+    launch_k(gemm_tc_kernel<BN, EPI, CT>, dim3(unsigned(grid)), dim3(192), S::SMEM_BYTES, st, 1, ta, tb, to, tg, int(M),
+             int(N), int(K), e);
 }
 
 // 2-SM (cta_group::2) 256 x 256 pair tiles; B operands need a 128-row TMA box.
@@ -194,9 +235,8 @@ void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb_half, int64
     const int64_t units = ((M + 255) / 256) * (N / BN);
     if (units == 0) return;
     const int64_t pairs = units < num_sms / 2 ? units : num_sms / 2;
-    gemm_tc2_kernel<BN, EPI, CT><<<unsigned(2 * pairs), 192, S::SMEM_BYTES, st>>>(ta, tb_half, int(M), int(N), int(K),
-                                                                                  ep);
-    CK(cudaGetLastError());
+    launch_k(gemm_tc2_kernel<BN, EPI, CT>, dim3(unsigned(2 * pairs)), dim3(192), S::SMEM_BYTES, st, 1, ta, tb_half,
+             int(M), int(N), int(K), ep);
 }
 
 // 2-SM pair tiles of 256 x bn (bn = 256 or 192); tb_half is B's tensor map with a bn / 2-row box.
@@ -330,8 +370,17 @@ std::vector<float> host_f32(const b2d_tensor_view* t, int64_t n) {
 // ------------------------------------------------------------- VibeVoice head
 constexpr int kHeadLatent = 64;
 
+// Launch plan of the weight-streaming GEMM for one shape: column-tile width and the K split (= cluster size).
+struct StreamPlan {
+    int bn = 0, split = 1;
+};
+
 struct HeadWorkspace {
     int64_t batch = 0;  // B; GEMM rows = 2B
+    // rows <= 128: weight-streaming plans of the per-step projections and weight maps with their tile widths
+    StreamPlan plan_ada, plan_gu, plan_down;
+    CUtensorMap tm_ada_s{};
+    std::vector<CUtensorMap> tm_gu_s, tm_down_s;
     DevBuf x, cp, sc, ada, h, ffn, v, noisy, cond, cond_ct, init, xstate, hist0, hist1, out, temb, h1, tsteps, coefs, ptstep, vpart, feat_ct, h1pre, h1_ct;
     int final_splits = 1;
     CUtensorMap tm_noisy, tm_cond, tm_sc, tm_h, tm_ffn, tm_feat, tm_h1;
@@ -356,6 +405,11 @@ struct HeadModel {
     std::vector<DevBuf> w_gu, w_down;
     CUtensorMap tm_in, tm_cond, tm_ada, tm_final, tm_t1, tm_t2;
     std::vector<CUtensorMap> tm_gu, tm_gu128, tm_down256, tm_down192;
+    // Q8_0 checkpoints: the same projections kept as k-block-major Q8_0 planes for the weight-streaming GEMM
+    // (few rows), next to the fp16 copies the tensor-bound GEMMs read.
+    bool q8 = false;
+    DevBuf q_ada, d_ada;
+    std::vector<DevBuf> q_gu, d_gu, q_down, d_down;
     std::unique_ptr<HeadWorkspace> ws;
 };
 
@@ -418,6 +472,146 @@ void check_status_word(b2d_ctx* ctx, cudaStream_t st) {
     }
 }
 
+// Q8_0 [rows, k] weight -> k-block-major planes (q [k/64][n_total][64], d [k/64][n_total][2]) at rows map(r).
+void upload_q8_planar(const b2d_tensor_view* t, int64_t rows, int64_t k, int8_t* q, __half* d, int64_t n_total,
+                      RowMap map, int num_sms, cudaStream_t st) {
+    if (t->ggml_type != B2D_TYPE_Q8_0) fail(B2D_EINVAL, "%s is not Q8_0", t->name);
+    if (t->dims[0] != rows || k % 64) fail(B2D_EINVAL, "Q8_0 plane shape for %s", t->name);
+    const size_t need = type_row_bytes(B2D_TYPE_Q8_0, k) * size_t(rows);
+    if (t->nbytes != need) fail(B2D_EINVAL, "tensor byte size mismatch for %s", t->name);
+    DevBuf staging(need);
+    CK(cudaMemcpyAsync(staging.p, t->data, need, cudaMemcpyHostToDevice, st));
+    repack_q8_0_kernel<<<grid_for(rows * k / 32, 256, num_sms), 256, 0, st>>>(staging.as<uint8_t>(), rows, k, q, d,
+                                                                               n_total, map);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(st));
+}
+
+template <int BN, int WF, int EPI, typename CT>
+int stream_max_clusters(int split) {
+    using S = StreamShape<BN, WF>;
+    set_smem_limit(gemm_stream_kernel<BN, WF, EPI, CT>, int(S::SMEM_BYTES));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(unsigned(split), 1, 1);
+    cfg.blockDim = dim3(S::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(split);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_stream_kernel<BN, WF, EPI, CT>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+template <int WF, int EPI, typename CT>
+int stream_max_clusters_bn(int bn, int split) {
+    switch (bn) {
+        case 64: if constexpr (EPI != EPI_SWIGLU) return stream_max_clusters<64, WF, EPI, CT>(split); break;
+        case 128: if constexpr (EPI != EPI_SWIGLU) return stream_max_clusters<128, WF, EPI, CT>(split); break;
+        case 192: if constexpr (EPI != EPI_SWIGLU) return stream_max_clusters<192, WF, EPI, CT>(split); break;
+        default: return stream_max_clusters<256, WF, EPI, CT>(split);
+    }
+    return 0;
+}
+
+// Picks (bn, split) so that the n_tiles x split CTAs run in one wave (every cluster co-resident) and keep as many
+// SMs streaming as possible; ties go to the smaller split (less reduction traffic), then the wider tile.
+template <int WF, int EPI, typename CT>
+StreamPlan stream_plan_t(int num_sms, int64_t N, int64_t K) {
+    StreamPlan best;
+    int64_t best_ctas = -1;
+    const int64_t kb = K / 64;
+    const int bns[4] = {256, 192, 128, 64};
+    for (int bn : bns) {
+        if (EPI == EPI_SWIGLU && bn != 256) continue;
+        if (N % bn) continue;
+        const int64_t tiles = N / bn;
+        for (int split : {1, 2, 3, 4, 6, 8}) {
+            if (split > kb) break;
+            const int64_t ctas = tiles * split;
+            if (ctas > num_sms) break;
+            const int maxc = stream_max_clusters_bn<WF, EPI, CT>(bn, split);
+            if (maxc < tiles) continue;
+            if (ctas > best_ctas || (ctas == best_ctas && split < best.split)) {
+                best_ctas = ctas;
+                best.bn = bn;
+                best.split = split;
+            }
+        }
+    }
+    if (best.bn == 0) {  // nothing fits one wave: the widest tile without a split
+        for (int bn : bns)
+            if (N % bn == 0 && (EPI != EPI_SWIGLU || bn == 256)) {
+                best.bn = bn;
+                break;
+            }
+    }
+    return best;
+}
+
+template <typename CT>
+StreamPlan stream_plan(b2d_ctx* ctx, bool q8, int epi, int64_t N, int64_t K) {
+    switch (epi * 2 + (q8 ? 1 : 0)) {
+        case EPI_F32 * 2: return stream_plan_t<WF_16, EPI_F32, CT>(ctx->num_sms, N, K);
+        case EPI_F32 * 2 + 1: return stream_plan_t<WF_Q8, EPI_F32, CT>(ctx->num_sms, N, K);
+        case EPI_CT * 2: return stream_plan_t<WF_16, EPI_CT, CT>(ctx->num_sms, N, K);
+        case EPI_CT * 2 + 1: return stream_plan_t<WF_Q8, EPI_CT, CT>(ctx->num_sms, N, K);
+        case EPI_SWIGLU * 2: return stream_plan_t<WF_16, EPI_SWIGLU, CT>(ctx->num_sms, N, K);
+        case EPI_SWIGLU * 2 + 1: return stream_plan_t<WF_Q8, EPI_SWIGLU, CT>(ctx->num_sms, N, K);
+        case EPI_RESID * 2: return stream_plan_t<WF_16, EPI_RESID, CT>(ctx->num_sms, N, K);
+        default: return stream_plan_t<WF_Q8, EPI_RESID, CT>(ctx->num_sms, N, K);
+    }
+}
+
+template <int BN, int WF, int EPI, typename CT>
+void launch_stream_t(const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* q, const __half* d, int64_t M,
+                     int64_t N, int64_t K, int split, const EpiParams& ep, cudaStream_t st) {
+    using S = StreamShape<BN, WF>;
+    set_smem_limit(gemm_stream_kernel<BN, WF, EPI, CT>, int(S::SMEM_BYTES));
+    StreamArgs a;
+    a.M = int(M);
+    a.N = int(N);
+    a.K = int(K);
+    a.k_blocks = int(K / 64);
+    a.q8 = q;
+    a.q8d = d;
+    launch_k(gemm_stream_kernel<BN, WF, EPI, CT>, dim3(unsigned((N / BN) * split)), dim3(S::THREADS), S::SMEM_BYTES, st,
+             split, ta, tb, a, ep);
+}
+
+// C = A W^T for M <= 128 rows with the weight-streaming kernel and a plan from stream_plan; W either 16-bit
+// through `tb` (box rows = plan.bn) or Q8_0 planes (q, d).  Outputs need 16-byte aligned rows.
+template <typename CT>
+void launch_stream(StreamPlan plan, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* q,
+                   const __half* d, int64_t M, int64_t N, int64_t K, const EpiParams& ep, cudaStream_t st) {
+    if (M > 128 || M <= 0) fail(B2D_EINVAL, "weight-streaming GEMM takes 1..128 rows (got %lld)", (long long)M);
+    const int bn = plan.bn;
+    if (bn == 0 || N % bn || K % 64 || plan.split < 1 || plan.split > K / 64)
+        fail(B2D_EINVAL, "weight-streaming GEMM shape %lld x %lld (tile %d, split %d)", (long long)N, (long long)K, bn,
+             plan.split);
+    if (ep.splits > 1 || ep.seg_rows || ep.rope_cos) fail(B2D_EINVAL, "weight-streaming GEMM epilogue options");
+    const bool wq = q != nullptr;
+#define B2D_S(BNv, EPIv)                                                                                     \
+    if (bn == BNv && epi == EPIv) {                                                                          \
+        if (wq) launch_stream_t<BNv, WF_Q8, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st);            \
+        else launch_stream_t<BNv, WF_16, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st);               \
+        return;                                                                                              \
+    }
+    B2D_S(256, EPI_F32) B2D_S(256, EPI_SWIGLU) B2D_S(256, EPI_RESID) B2D_S(256, EPI_CT)
+    B2D_S(192, EPI_F32) B2D_S(192, EPI_RESID) B2D_S(192, EPI_CT)
+    B2D_S(128, EPI_F32) B2D_S(128, EPI_RESID) B2D_S(128, EPI_CT)
+    B2D_S(64, EPI_F32) B2D_S(64, EPI_RESID) B2D_S(64, EPI_CT)
+#undef B2D_S
+    fail(B2D_EINVAL, "unsupported weight-streaming GEMM tile %d / epilogue %d", bn, epi);
+}
+
 // ------------------------------------------------------------ head: load
 template <typename CT>
 void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
@@ -463,6 +657,41 @@ void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
     }
     upload_weight<CT>(need("final_layer.adaLN_modulation.1.weight"), 2 * H, H, m.w_ada.as<CT>(),
                       RowMap{2 * H, 0, 3 * H * L}, ctx->num_sms, st);
+    // Q8_0 checkpoints also keep the per-step projections as Q8_0 planes (same row order as the fp16 copies)
+    m.q8 = need("layers.0.ffn.gate_proj.weight")->ggml_type == B2D_TYPE_Q8_0 && H % 64 == 0 && F % 64 == 0;
+    for (int64_t l = 0; m.q8 && l < L; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        for (const char* nm : {"adaLN_modulation.1.weight", "ffn.gate_proj.weight", "ffn.up_proj.weight",
+                               "ffn.down_proj.weight"})
+            if (need(p + nm)->ggml_type != B2D_TYPE_Q8_0) m.q8 = false;
+    }
+    if (need("final_layer.adaLN_modulation.1.weight")->ggml_type != B2D_TYPE_Q8_0) m.q8 = false;
+    if (m.q8) {
+        m.q_ada.alloc(size_t(m.NADA) * H);
+        m.d_ada.alloc(size_t(m.NADA) * (H / 32) * 2);
+        m.q_gu.resize(size_t(L));
+        m.d_gu.resize(size_t(L));
+        m.q_down.resize(size_t(L));
+        m.d_down.resize(size_t(L));
+        for (int64_t l = 0; l < L; ++l) {
+            const std::string p = "layers." + std::to_string(l) + ".";
+            const size_t li = size_t(l);
+            upload_q8_planar(need(p + "adaLN_modulation.1.weight"), 3 * H, H, m.q_ada.as<int8_t>(),
+                             m.d_ada.as<__half>(), m.NADA, RowMap{3 * H, 0, 3 * H * l}, ctx->num_sms, st);
+            m.q_gu[li].alloc(size_t(2 * F) * H);
+            m.d_gu[li].alloc(size_t(2 * F) * (H / 32) * 2);
+            upload_q8_planar(need(p + "ffn.gate_proj.weight"), F, H, m.q_gu[li].as<int8_t>(), m.d_gu[li].as<__half>(),
+                             2 * F, RowMap{128, 256, 0}, ctx->num_sms, st);
+            upload_q8_planar(need(p + "ffn.up_proj.weight"), F, H, m.q_gu[li].as<int8_t>(), m.d_gu[li].as<__half>(),
+                             2 * F, RowMap{128, 256, 128}, ctx->num_sms, st);
+            m.q_down[li].alloc(size_t(H) * F);
+            m.d_down[li].alloc(size_t(H) * (F / 32) * 2);
+            upload_q8_planar(need(p + "ffn.down_proj.weight"), H, F, m.q_down[li].as<int8_t>(),
+                             m.d_down[li].as<__half>(), H, RowMap{H, 0, 0}, ctx->num_sms, st);
+        }
+        upload_q8_planar(need("final_layer.adaLN_modulation.1.weight"), 2 * H, H, m.q_ada.as<int8_t>(),
+                         m.d_ada.as<__half>(), m.NADA, RowMap{2 * H, 0, 3 * H * L}, ctx->num_sms, st);
+    }
     m.w_final.alloc(size_t(kHeadLatent) * H * e);
     upload_weight<CT>(need("final_layer.linear.weight"), kHeadLatent, H, m.w_final.as<CT>(), plain(kHeadLatent),
                       ctx->num_sms, st);
@@ -496,6 +725,18 @@ HeadWorkspace& head_workspace(b2d_ctx* ctx, HeadModel& m, int64_t batch) {
     auto ws = std::make_unique<HeadWorkspace>();
     ws->batch = batch;
     const int64_t R = 2 * batch, H = m.H, F = m.F;
+    if (R <= 128) {  // weight-streaming plans of the per-step projections (planned outside any capture)
+        ws->plan_ada = stream_plan<CT>(ctx, m.q8, EPI_F32, m.NADA, H);
+        ws->plan_gu = stream_plan<CT>(ctx, m.q8, EPI_SWIGLU, 2 * F, H);
+        ws->plan_down = stream_plan<CT>(ctx, m.q8, EPI_RESID, H, F);
+        if (!m.q8) {
+            ws->tm_ada_s = make_tmap(m.w_ada.p, m.bf16, m.NADA, H, uint32_t(ws->plan_ada.bn));
+            for (size_t l = 0; l < m.w_gu.size(); ++l) {
+                ws->tm_gu_s.push_back(make_tmap(m.w_gu[l].p, m.bf16, 2 * F, H, uint32_t(ws->plan_gu.bn)));
+                ws->tm_down_s.push_back(make_tmap(m.w_down[l].p, m.bf16, H, F, uint32_t(ws->plan_down.bn)));
+            }
+        }
+    }
     const size_t e = sizeof(CT);
     ws->x.alloc(size_t(R) * H * 4);
     ws->cp.alloc(size_t(R) * H * 4);
@@ -552,12 +793,14 @@ void launch_rms_modulate(const float* x, int64_t ldx, const float* w, const floa
                          int64_t ldm, float eps, int64_t H, int64_t R, CT* out, int64_t ldo, cudaStream_t st) {
     const unsigned grid = unsigned((R + 7) / 8);
     if (H <= 2048)
-        rms_modulate_warp_kernel<CT, 16><<<grid, 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), R, out, ldo);
+        launch_k(rms_modulate_warp_kernel<CT, 16>, dim3(grid), dim3(256), 0, st, 1, x, ldx, w, shift, scale, ldm, eps,
+                 int(H), R, out, ldo);
     else if (H <= 4096)
-        rms_modulate_warp_kernel<CT, 32><<<grid, 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), R, out, ldo);
+        launch_k(rms_modulate_warp_kernel<CT, 32>, dim3(grid), dim3(256), 0, st, 1, x, ldx, w, shift, scale, ldm, eps,
+                 int(H), R, out, ldo);
     else
-        rms_modulate_kernel<CT, 256><<<unsigned(R), 256, 0, st>>>(x, ldx, w, shift, scale, ldm, eps, int(H), out, ldo);
-    CK(cudaGetLastError());
+        launch_k(rms_modulate_kernel<CT, 256>, dim3(unsigned(R)), dim3(256), 0, st, 1, x, ldx, w, shift, scale, ldm,
+                 eps, int(H), out, ldo);
 }
 
 template <typename CT>
@@ -572,15 +815,22 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
     ep.ldo = H;
     launch_gemm<CT>(256, EPI_F32, ws.tm_noisy, m.tm_in, R, H, kHeadLatent, ep, sms, st);
     // sc = silu(cond_proj + t_emb)
-    silu_cond_kernel<CT><<<grid_for(R * H / 4, 256, sms), 256, 0, st>>>(
-        ws.cp.as<float>(), ws.temb.as<float>() + int64_t(temb_row) * H, R, int(H), ws.sc.as<CT>());
-    CK(cudaGetLastError());
+    launch_k(silu_cond_kernel<CT>, dim3(unsigned(grid_for(R * H / 4, 256, sms))), dim3(256), 0, st, 1,
+             (const float*)ws.cp.as<float>(), (const float*)(ws.temb.as<float>() + int64_t(temb_row) * H), R, int(H),
+             ws.sc.as<CT>());
     // every adaLN modulation of every layer in one GEMM: ada = sc * W_ada^T  [R, NADA]
     ep = EpiParams{};
     ep.status = status;
     ep.out = ws.ada.p;
     ep.ldo = m.NADA;
-    launch_gemm<CT>(256, EPI_F32, ws.tm_sc, m.tm_ada, R, m.NADA, H, ep, sms, st);
+    // Up to 128 rows the per-step projections stream their weights (HBM-bound); above, tensor-bound tiles.
+    const bool stream = R <= 128 && m.NADA % 256 == 0 && H % 256 == 0 && (2 * F) % 256 == 0 && m.NADA % 4 == 0;
+    const bool q8s = stream && m.q8;
+    if (stream)
+        launch_stream<CT>(ws.plan_ada, EPI_F32, ws.tm_sc, ws.tm_ada_s, q8s ? m.q_ada.as<int8_t>() : nullptr,
+                          q8s ? m.d_ada.as<__half>() : nullptr, R, m.NADA, H, ep, st);
+    else
+        launch_gemm<CT>(256, EPI_F32, ws.tm_sc, m.tm_ada, R, m.NADA, H, ep, sms, st);
     const float* ada = ws.ada.as<float>();
     for (int64_t l = 0; l < L; ++l) {
         const float* shift = ada + 3 * H * l;
@@ -590,8 +840,13 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         ep.status = status;
         ep.out = ws.ffn.p;
         ep.ldo = F;
-        // SwiGLU GEMMs run on 2-SM 256 x 256 pair tiles (measured faster at every head shape)
-        launch_gemm_pair<CT>(EPI_SWIGLU, ws.tm_h, m.tm_gu128[size_t(l)], R, 2 * F, H, ep, sms, st);
+        // SwiGLU GEMMs run on 2-SM 256 x 256 pair tiles (measured faster at every tensor-bound head shape)
+        if (stream)
+            launch_stream<CT>(ws.plan_gu, EPI_SWIGLU, ws.tm_h, q8s ? ws.tm_ada_s : ws.tm_gu_s[size_t(l)],
+                              q8s ? m.q_gu[size_t(l)].as<int8_t>() : nullptr,
+                              q8s ? m.d_gu[size_t(l)].as<__half>() : nullptr, R, 2 * F, H, ep, st);
+        else
+            launch_gemm_pair<CT>(EPI_SWIGLU, ws.tm_h, m.tm_gu128[size_t(l)], R, 2 * F, H, ep, sms, st);
         ep = EpiParams{};
         ep.status = status;
         ep.resid = ws.x.as<float>();
@@ -601,7 +856,11 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         // 192-wide tiles when they fill the SMs better (H = 1536: 8 x 16 = 128 tiles vs 96)
         const int64_t mt = (R + 127) / 128;
         const bool use192 = !m.tm_down192.empty() && waves_eff(mt * (H / 192), sms) > waves_eff(mt * (H / 256), sms);
-        if (use192)
+        if (stream)
+            launch_stream<CT>(ws.plan_down, EPI_RESID, ws.tm_ffn, q8s ? ws.tm_ada_s : ws.tm_down_s[size_t(l)],
+                              q8s ? m.q_down[size_t(l)].as<int8_t>() : nullptr,
+                              q8s ? m.d_down[size_t(l)].as<__half>() : nullptr, R, H, F, ep, st);
+        else if (use192)
             launch_gemm<CT>(192, EPI_RESID, ws.tm_ffn, m.tm_down192[size_t(l)], R, H, F, ep, sms, st);
         else
             launch_gemm<CT>(256, EPI_RESID, ws.tm_ffn, m.tm_down256[size_t(l)], R, H, F, ep, sms, st);
@@ -661,15 +920,15 @@ void head_sample_body(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int S, floa
     vv_init_kernel<CT><<<grid_for(n_half, 256, sms), 256, 0, st>>>(ws.init.as<float>(), ws.xstate.as<float>(),
                                                                      ws.noisy.as<CT>(), n_half);
     CK(cudaGetLastError());
+    PdlScope pdl;  // the step loop's kernels overlap each other's launch and prologue
     for (int s = 0; s < S; ++s) {
         head_forward<CT>(ctx, m, ws, s, st);
         float* hp = (s & 1) ? ws.hist0.as<float>() : ws.hist1.as<float>();
         float* hc = (s & 1) ? ws.hist1.as<float>() : ws.hist0.as<float>();
-        vv_cfg_dpm_kernel<CT><<<grid_for(n_half, 256, sms), 256, 0, st>>>(
-            ws.vpart.as<float>(), ws.final_splits, 2 * n_half, ws.xstate.as<float>(), hp, hc, ws.noisy.as<CT>(),
-            ws.out.as<float>(), n_half,
-            ws.coefs.as<VvStepCoef>(), s, cfg, ctx->status.as<int>());
-        CK(cudaGetLastError());
+        launch_k(vv_cfg_dpm_kernel<CT>, dim3(unsigned(grid_for(n_half, 256, sms))), dim3(256), 0, st, 1,
+                 (const float*)ws.vpart.as<float>(), ws.final_splits, 2 * n_half, ws.xstate.as<float>(),
+                 (const float*)hp, hc, ws.noisy.as<CT>(), ws.out.as<float>(), n_half,
+                 (const VvStepCoef*)ws.coefs.as<VvStepCoef>(), s, cfg, ctx->status.as<int>());
     }
 }
 
@@ -972,6 +1231,62 @@ b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* b
         } else {
             launch_gemm<__half>(bn, epilogue, ta, tb, m, n, k, ep, ctx->num_sms, st);
         }
+    });
+}
+
+b2d_status b2d_gemm_stream(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* w_dev, int32_t w_type,
+                           int64_t m, int64_t n, int64_t k, int32_t epilogue, int32_t bn, int32_t split,
+                           const float* bias_dev,
+                           void* out_dev, int64_t ldo, float* resid_dev, int64_t ldr, const float* gate_dev,
+                           int64_t ldg, void* stream) {
+    return guarded(ctx, [&] {
+        if (m <= 0 || n <= 0 || k <= 0 || !a_dev || !w_dev) fail(B2D_EINVAL, "GEMM dimensions must be positive");
+        if (epilogue == EPI_RESID ? !resid_dev : !out_dev) fail(B2D_EINVAL, "GEMM output is null");
+        const bool q8 = w_type == B2D_TYPE_Q8_0;
+        if (!q8 && w_type != (bf16 ? B2D_TYPE_BF16 : B2D_TYPE_F16)) fail(B2D_EINVAL, "weight type");
+        if (q8 && bf16) fail(B2D_EINVAL, "Q8_0 weights stream as fp16 operands");
+        const bool f32out = epilogue == EPI_F32 || epilogue == EPI_RESID;
+        if ((f32out && epilogue == EPI_F32 && (ldo % 4 || reinterpret_cast<uintptr_t>(out_dev) % 16)) ||
+            (epilogue == EPI_RESID && (ldr % 4 || reinterpret_cast<uintptr_t>(resid_dev) % 16 ||
+                                       (gate_dev && (ldg % 4 || reinterpret_cast<uintptr_t>(gate_dev) % 16)))) ||
+            ((epilogue == EPI_CT || epilogue == EPI_SWIGLU) && (ldo % 8 || reinterpret_cast<uintptr_t>(out_dev) % 16)))
+            fail(B2D_EINVAL, "weight-streaming GEMM outputs need 16-byte aligned rows");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        StreamPlan plan;
+        if (bn == 0) {
+            plan = bf16 ? stream_plan<__nv_bfloat16>(ctx, q8, epilogue, n, k) : stream_plan<__half>(ctx, q8, epilogue, n, k);
+        } else {
+            plan.bn = bn;
+            plan.split = split < 1 ? 1 : split;
+        }
+        const CUtensorMap ta = make_tmap(a_dev, bf16 != 0, uint64_t(m), uint64_t(k), 128);
+        CUtensorMap tb{};
+        DevBuf qbuf, dbuf;
+        if (q8) {
+            if (k % 64) fail(B2D_EINVAL, "K %% 64");
+            qbuf.alloc(size_t(n) * k);
+            dbuf.alloc(size_t(n) * (k / 32) * 2);
+            repack_q8_0_kernel<<<grid_for(n * k / 32, 256, ctx->num_sms), 256, 0, st>>>(
+                static_cast<const uint8_t*>(w_dev), n, k, qbuf.as<int8_t>(), dbuf.as<__half>(), n, RowMap{n, 0, 0});
+            CK(cudaGetLastError());
+        } else {
+            tb = make_tmap(w_dev, bf16 != 0, uint64_t(n), uint64_t(k), uint32_t(plan.bn));
+        }
+        EpiParams ep;
+        ep.out = out_dev;
+        ep.ldo = ldo;
+        ep.bias = bias_dev;
+        ep.resid = resid_dev;
+        ep.ldr = ldr;
+        ep.gate = gate_dev;
+        ep.ldg = ldg;
+        ep.status = ctx->status.as<int>();
+        if (bf16)
+            launch_stream<__nv_bfloat16>(plan, epilogue, ta, tb, nullptr, nullptr, m, n, k, ep, st);
+        else
+            launch_stream<__half>(plan, epilogue, ta, tb, q8 ? qbuf.as<int8_t>() : nullptr,
+                                  q8 ? dbuf.as<__half>() : nullptr, m, n, k, ep, st);
+        if (q8) CK(cudaStreamSynchronize(st));  // the planes are freed on return
     });
 }
 

@@ -414,9 +414,11 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {
+            pdl_wait();
             int stage = 0;
             uint32_t phase = 0;
             for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
@@ -482,6 +484,7 @@ __global__ void __launch_bounds__(192, 1)
         // instruction reads/writes one contiguous 32-column row segment (coalesced, and the
         // residual read-modify-write issues all 32 rows' loads before any store instead of serialising).
         const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
+        pdl_wait();
         if constexpr (S::RESID_TMA) {
             if (ep.tma_resid) {
                 uint8_t* epi = smem + size_t(STAGES) * S::STAGE_BYTES;
@@ -591,9 +594,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {
+            pdl_wait();
             int stage = 0;
             uint32_t phase = 0;
             for (int u = cluster; u < num_units; u += nclusters) {
@@ -651,6 +656,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int quarter = warp & 3;
         float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
         const uint32_t tempty_leader[2] = {map_to_cta(smem_u32(&tempty[0]), 0), map_to_cta(smem_u32(&tempty[1]), 0)};
+        pdl_wait();
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = cluster; u < num_units; u += nclusters) {

@@ -63,6 +63,24 @@ __global__ void dequant_q8_0_kernel(const uint8_t* __restrict__ src, int64_t row
     }
 }
 
+// Q8_0 blocks of a [rows, k] weight -> the k-block-major planar form the weight-streaming GEMM reads:
+// quants q[k/64][n_total][64] (int8) and scales d[k/64][n_total][2] (the fp16 scale bits of the two 32-blocks),
+// destination row map(r).  A lossless rearrangement of the checkpoint's bytes.
+__global__ void repack_q8_0_kernel(const uint8_t* __restrict__ src, int64_t rows, int64_t k, int8_t* __restrict__ q,
+                                   __half* __restrict__ d, int64_t n_total, RowMap map) {
+    const int64_t nblk_row = k / 32;
+    const int64_t total = rows * nblk_row;
+    for (int64_t b = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; b < total; b += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = b / nblk_row, kb = b % nblk_row;
+        const uint8_t* blk = src + b * 34;
+        const int64_t n = map(r), k64 = kb / 2, half = kb % 2;
+        d[(k64 * n_total + n) * 2 + half] = __ushort_as_half(uint16_t(blk[0]) | (uint16_t(blk[1]) << 8));
+        int8_t* o = q + (k64 * n_total + n) * 64 + half * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = int8_t(blk[2 + j]);
+    }
+}
+
 template <typename InT, typename OutT>
 __global__ void convert_rows_kernel(const InT* __restrict__ src, int64_t rows, int64_t k, OutT* __restrict__ dst,
                                     int64_t ldd, RowMap map) {
@@ -87,6 +105,8 @@ __global__ void __launch_bounds__(THREADS) rms_modulate_kernel(const float* __re
                                                                const float* __restrict__ w, const float* __restrict__ shift,
                                                                const float* __restrict__ scale, int64_t ldm, float eps,
                                                                int H, CT* __restrict__ out, int64_t ldo) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const float4* x4 = reinterpret_cast<const float4*>(x + row * ldx);
     const int n4 = H / 4;
@@ -130,6 +150,8 @@ __global__ void __launch_bounds__(256) rms_modulate_warp_kernel(const float* __r
                                                                 const float* __restrict__ shift,
                                                                 const float* __restrict__ scale, int64_t ldm, float eps,
                                                                 int H, int64_t rows, CT* __restrict__ out, int64_t ldo) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = int64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -167,6 +189,8 @@ __global__ void __launch_bounds__(256) rms_modulate_warp_kernel(const float* __r
 template <typename CT>
 __global__ void silu_cond_kernel(const float* __restrict__ cp, const float* __restrict__ temb, int64_t rows, int H,
                                  CT* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t n4 = rows * H / 4;
     const int h4 = H / 4;
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
@@ -231,6 +255,8 @@ __global__ void vv_cfg_dpm_kernel(const float* __restrict__ v, int splits, int64
                                   float* __restrict__ hist_cur, CT* __restrict__ noisy, float* __restrict__ out_latents,
                                   int64_t n_half, const VvStepCoef* __restrict__ coefs, int step, float cfg,
                                   int* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
     const VvStepCoef c = coefs[step];
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n_half; i += int64_t(gridDim.x) * blockDim.x) {
         float vc = 0.f, vu = 0.f;

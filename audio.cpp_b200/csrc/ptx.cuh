@@ -70,6 +70,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     return false;
 }
 
+// Programmatic dependent launch.  pdl_wait: block until the grids this one depends on have completed and
+// their memory is visible (returns at once for a kernel launched without a programmatic dependency).
+// pdl_trigger: let the next kernel in the stream start launching its CTAs (they then run their own
+// prologue and whatever precedes their pdl_wait -- here only loads of constant weights).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar, int32_t x, int32_t y) {
     asm volatile(
@@ -96,6 +103,16 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
                      reinterpret_cast<uint64_t>(tmap)),
                  "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
                  : "memory");
+}
+
+// Plain (non-tensor) bulk copy global -> shared, completion counted on `bar`: both addresses 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // 2-D tiled store from shared memory (bulk group); rows / columns outside the map's extent are not written.
@@ -244,6 +261,22 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
+// 16-byte load from shared memory of any CTA of the cluster (address from map_to_cta).
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
 }
 
 // Address of the same shared variable in CTA `rank` of this cluster.

@@ -409,6 +409,21 @@ B2D_API b2d_status b2d_gemm(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const
                     int64_t k, int32_t epilogue, int32_t bn, const float* bias_dev, void* out_dev, int64_t ldo,
                     float* resid_dev, int64_t ldr, const float* gate_dev, int64_t ldg, void* stream);
 
+/* The weight-streaming GEMM the VibeVoice head uses when a call has at most 128 rows (HBM-bound: every SM
+ * streams weights; each column tile's K range is split over the CTAs of a thread-block cluster whose partial
+ * sums are added on chip in a fixed order).  A [M <= 128, K] device fp16 / bf16 (bf16 != 0); W [N, K] on the device either
+ * in the same 16-bit type (w_type B2D_TYPE_F16 / B2D_TYPE_BF16) or as ggml Q8_0 blocks (B2D_TYPE_Q8_0,
+ * fp16 operands: each block is expanded in shared memory to fp16(q * d) inside the main loop).
+ * bn = 0 picks the column-tile width and K split (the cluster size that sums the split partials on chip) for
+ * the shape; else bn in {64, 128, 192, 256} (SwiGLU: 256) and split in 1..8 CTAs per column tile
+ * (K / 64 >= split).  K % 64 == 0, N % bn == 0; outputs / residual / gate need 16-byte aligned rows.
+ * Kernel-level entry for tests and benchmarks; no counterpart in the reference (it stands in for the
+ * ggml-cuda GEMV paths behind ggml_mul_mat for few rows). */
+B2D_API b2d_status b2d_gemm_stream(b2d_ctx* ctx, int32_t bf16, const void* a_dev, const void* w_dev, int32_t w_type,
+                                   int64_t m, int64_t n, int64_t k, int32_t epilogue, int32_t bn, int32_t split,
+                                   const float* bias_dev, void* out_dev, int64_t ldo, float* resid_dev, int64_t ldr,
+                                   const float* gate_dev, int64_t ldg, void* stream);
+
 /* torch-CUDA-compatible normals on the device (src/framework/sampling/torch_random.cpp):
  * layout 0 = generate_torch_cuda_randn(count, seed) starting at element `offset`;
  * layout 1 = generate_torch_cuda_tensor_iterator_randn(count, seed, offset_blocks = offset, policy).

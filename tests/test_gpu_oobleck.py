@@ -19,7 +19,7 @@ def make(b2d, ctx, cfg):
                               weights=weight_specs(synth.oobleck_weights(cfg)))
 
 
-@pytest.mark.parametrize("name", ["oobleck_tiny", "oobleck_tiny_b2_odd"])
+@pytest.mark.parametrize("name", ["oobleck_tiny", "oobleck_tiny_b2_odd", "oobleck_sao_shape_1x16"])
 def test_oobleck_decode_matches_reference(b2d, ctx, name):
     from oracle import oobleck
     cfg = synth.OOBLECK_CONFIGS[name]
