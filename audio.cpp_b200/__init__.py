@@ -29,7 +29,7 @@ STATUS = {0: "ok", -1: "EINVAL", -2: "ECUDA", -3: "ENOMEM", -4: "ESTATE", -5: "E
 
 EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_version", "b2d_vv_schedule",
             "b2d_vv_head_load", "b2d_vv_predict", "b2d_vv_sample", "b2d_vv_sample_device", "b2d_q8_0_dequantize",
-            "b2d_gemm", "b2d_gemm_stream", "b2d_gemm_splitk_noalloc", "b2d_gemm_splitk_noalloc_status", "b2d_gemm_splitk_noalloc_selftest_timeout", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
+            "b2d_storage_resolve", "b2d_tensor_bytes", "b2d_tensor_convert", "b2d_gemm", "b2d_gemm_stream", "b2d_gemm_splitk_noalloc", "b2d_gemm_splitk_noalloc_status", "b2d_gemm_splitk_noalloc_selftest_timeout", "b2d_dit_load", "b2d_dit_sample", "b2d_dit_sample_device", "b2d_attention", "b2d_torch_randn", "b2d_selftest_wait_timeout",
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
             "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
             "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device",
@@ -144,6 +144,11 @@ def lib() -> C.CDLL:
         L.b2d_vv_sample_device.argtypes = [P, P, P, P, I64, I64, F, P, P]
         L.b2d_q8_0_dequantize.argtypes = [P, P, I64, I64, P, P]
         L.b2d_gemm.argtypes = [P, I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, I64, P, I64, P]
+        L.b2d_storage_resolve.argtypes = [I32, C.POINTER(TensorView)]
+        L.b2d_storage_resolve.restype = I32
+        L.b2d_tensor_bytes.argtypes = [I32, C.POINTER(I64), I32]
+        L.b2d_tensor_bytes.restype = C.c_size_t
+        L.b2d_tensor_convert.argtypes = [C.POINTER(TensorView), I32, P, C.c_size_t]
         L.b2d_gemm_stream.argtypes = [P, I32, P, P, I32, I64, I64, I64, I32, I32, I32, P, P, I64, P, I64, P, I64, P]
         L.b2d_gemm_splitk_noalloc.argtypes = [I32, P, P, I64, I64, I64, I32, I32, P, P, I64, P, C.c_char_p,
                                               C.c_size_t]
@@ -172,6 +177,32 @@ def lib() -> C.CDLL:
         L.b2d_vvlm_step.argtypes = [P, P, P, P, P]
         _lib = L
     return _lib
+
+
+STORAGE_NATIVE, STORAGE_F32, STORAGE_F16, STORAGE_BF16, STORAGE_Q8_0 = 0, 1, 2, 3, 13
+
+
+def convert_tensor(ggml_type: int, dims, payload: np.ndarray, storage: int):
+    """The reference weight store's storage-type selection + conversion of one checkpoint tensor (host).
+    Returns (ggml_type, payload bytes as uint8)."""
+    payload = np.ascontiguousarray(payload)
+    v = TensorView()
+    v.name = b"t"
+    v.ggml_type = ggml_type
+    v.ndim = len(dims)
+    for j, d in enumerate(dims):
+        v.dims[j] = d
+    v.data = payload.ctypes.data
+    v.nbytes = payload.nbytes
+    target = lib().b2d_storage_resolve(storage, C.byref(v))
+    if target < 0:
+        raise B2DError(-1, "unsupported storage type %d" % storage)
+    nbytes = lib().b2d_tensor_bytes(target, v.dims, v.ndim)
+    out = np.empty(nbytes, np.uint8)
+    st = lib().b2d_tensor_convert(C.byref(v), target, out.ctypes.data, nbytes)
+    if st != 0:
+        raise B2DError(st, "tensor conversion failed")
+    return target, out
 
 
 def version() -> str:

@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "libb200diff.so")
 SOURCES = [os.path.join(HERE, "csrc", "api.cu"), os.path.join(HERE, "csrc", "noalloc.cu"),
-           os.path.join(HERE, "csrc", "schedule.cpp")]
+           os.path.join(HERE, "csrc", "schedule.cpp"), os.path.join(HERE, "csrc", "storage.cpp")]
 DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))] + [
     os.path.join(os.path.dirname(HERE), "include", "b200diff.h")]
 

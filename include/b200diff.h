@@ -68,6 +68,24 @@ typedef struct {
     size_t nbytes;
 } b2d_tensor_view;
 
+/* ------------------------------------------------- weight storage types */
+/* audio.cpp's assets::TensorStorageType (include/engine/framework/assets/tensor_source.h:19-34), same values;
+ * this path computes with the Native / F32 / F16 / BF16 / Q8_0 members. */
+enum { B2D_STORAGE_NATIVE = 0, B2D_STORAGE_F32 = 1, B2D_STORAGE_F16 = 2, B2D_STORAGE_BF16 = 3, B2D_STORAGE_Q8_0 = 13 };
+
+/* ggml type a checkpoint tensor is kept in under a storage request, as the reference's weight store
+ * resolves it (include/engine/framework/core/backend_weight_store.h:237-290): Native keeps the stored type; a
+ * Q8_0 request falls back to F32 for tensors of rank < 2 or whose last dimension is not a multiple of 32.
+ * -1 for storage types this path does not support.  Host only. */
+B2D_API int32_t b2d_storage_resolve(int32_t storage_type, const b2d_tensor_view* tensor);
+/* Bytes of a tensor of `dims` in ggml type F32 / F16 / BF16 / Q8_0 (0 when not representable). */
+B2D_API size_t b2d_tensor_bytes(int32_t ggml_type, const int64_t* dims, int32_t ndim);
+/* Quantize-on-load / re-encoding (src/framework/assets/tensor_source.cpp:150-200): decodes `tensor` to fp32
+ * and encodes it as `ggml_type` into `out` (exactly b2d_tensor_bytes bytes): F16 round-to-nearest-even,
+ * BF16 with ggml's rounding, Q8_0 as quantize_row_q8_0_ref (d = amax / 127, q = roundf(x / d), d as fp16).
+ * Host only; the same bytes the reference's weight store produces. */
+B2D_API b2d_status b2d_tensor_convert(const b2d_tensor_view* tensor, int32_t ggml_type, void* out, size_t out_bytes);
+
 /* ---------------------------------------------------------------- context */
 /* Replaces core::init_backend for these graphs (src/framework/core/backend.cpp:94-144). */
 B2D_API b2d_status b2d_create(int device, b2d_ctx** out);

@@ -95,14 +95,19 @@ def q8_golden() -> None:
     print("q8 ok")
 
 
+# Full-length runs whose fp32-activation restatement would take hours of numpy: the fixture holds the
+# reference's latents only (the tests then hold the GPU to the reference alone).
+NO_EXACT = {"sao_bf16_1x1024", "sao_bf16_1x1024_noapg"}
+
+
 def dit_golden(name: str) -> None:
     cfg = synth.DIT_CONFIGS[name]
     w, inp = synth.dit_weights(cfg), synth.dit_inputs(cfg)
-    out = ref_runner.run("dit", inp, w)
-    exact = dit.sample(dit.Dit(w, cfg, act="exact"), cfg, inp)  # fp32-activation restatement
-    B.write(os.path.join(HERE, "dit_%s.b2db" % name),
-            {"latents": out["latents"], "exact_latents": B.f32(exact),
-             "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    out = ref_runner.run("dit", inp, w, timeout=4 * 3600)
+    fixture = {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))}
+    if name not in NO_EXACT:
+        fixture["exact_latents"] = B.f32(dit.sample(dit.Dit(w, cfg, act="exact"), cfg, inp))  # fp32 activations
+    B.write(os.path.join(HERE, "dit_%s.b2db" % name), fixture)
     print("dit", name, "ok", out["latents"].dims)
 
 

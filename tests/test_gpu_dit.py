@@ -60,6 +60,10 @@ def make_dit(b2d, ctx, name):
     return _dits[name]
 
 
+# Full 100-step C3 runs against the reference's latents (no fp32-activation restatement at this length).
+FULL_LENGTH_TOL = {"sao_bf16_1x1024": 5e-2, "sao_bf16_1x1024_noapg": 5e-2}
+
+
 def run(cfg, dit, inp):
     return dit.sample(inp["noise"].array(), inp["padding_mask"].array(), inp["cross_positive"].array(),
                       inp["cross_negative"].array(), inp["global"].array(), steps=cfg.steps,
@@ -77,15 +81,20 @@ def test_dit_sample_matches_reference(b2d, ctx, name):
     inp = synth.dit_inputs(cfg)
     out = run(cfg, dit, inp)
     g = golden("dit_" + name)
-    ref, exact = g["latents"].array(), g["exact_latents"].array()
+    ref = g["latents"].array()
     assert np.isfinite(out).all()
-    spread = rel_l2(exact, ref)
     err = rel_l2(out, ref)
-    err_exact = rel_l2(out, exact)
-    print("%s: vs ref %.3g (spread %.3g), vs exact %.3g" % (name, err, spread, err_exact))
-    assert err < max(2e-2, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
-    assert err_exact < max(2e-2 if cfg.wtype == synth.BF16 else 1e-2, 1.5 * spread), \
-        "rel-L2 %.3g vs exact oracle (spread %.3g)" % (err_exact, spread)
+    if "exact_latents" in g:
+        exact = g["exact_latents"].array()
+        spread = rel_l2(exact, ref)
+        err_exact = rel_l2(out, exact)
+        print("%s: vs ref %.3g (spread %.3g), vs exact %.3g" % (name, err, spread, err_exact))
+        assert err < max(2e-2, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
+        assert err_exact < max(2e-2 if cfg.wtype == synth.BF16 else 1e-2, 1.5 * spread), \
+            "rel-L2 %.3g vs exact oracle (spread %.3g)" % (err_exact, spread)
+    else:  # full-length fixtures carry the reference's latents only
+        print("%s: vs ref %.3g" % (name, err))
+        assert err < FULL_LENGTH_TOL[name], "rel-L2 %.3g vs reference" % err
     out2 = run(cfg, dit, inp)
     assert np.array_equal(out, out2)
     # rng_offset_blocks out-parameter: one TensorIterator draw per step with a non-zero next sigma
