@@ -301,8 +301,13 @@ int cmd_vv(const std::string & w, const std::string & in_path, const std::string
     const Bundle in = read_bundle(in_path);
     auto assets = head_assets(w, in);
     const auto & cfg = assets->config.diffusion_head;
+    // optional "storage_type": assets::TensorStorageType value for the weight store (quantize-on-load)
+    const auto storage = in.count("storage_type")
+                             ? static_cast<engine::assets::TensorStorageType>(i64_scalar(in, "storage_type"))
+                             : engine::assets::TensorStorageType::Native;
     engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime head(
-        assets, engine::core::BackendType::Cpu, 0, threads);
+        assets, engine::core::BackendType::Cpu, 0, threads, 64ull * 1024ull * 1024ull, 64ull * 1024ull * 1024ull,
+        storage);
     engine::models::vibevoice::VibeVoiceDPMSolverScheduler sched(cfg);
     engine::models::vibevoice::VibeVoiceSpeechDiffusionInput input;
     input.positive_condition = f32s(in, "positive_condition");
@@ -382,7 +387,10 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     const float rho = f32_scalar(in, "rho");
 
     engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
-    sa::foundation::FoundationRfDitRuntime dit(exec, assets, engine::assets::TensorStorageType::Native);
+    const auto storage = in.count("storage_type")
+                             ? static_cast<engine::assets::TensorStorageType>(i64_scalar(in, "storage_type"))
+                             : engine::assets::TensorStorageType::Native;
+    sa::foundation::FoundationRfDitRuntime dit(exec, assets, storage);
     engine::sampling::TorchCudaSamplingPolicy policy;
     if (in.count("rng_sms")) policy.multiprocessor_count = i64_scalar(in, "rng_sms");
     if (in.count("rng_max_threads")) policy.max_threads_per_multiprocessor = i64_scalar(in, "rng_max_threads");

@@ -55,9 +55,17 @@ def variant() -> Optional[str]:
     return None if b is None else os.path.basename(b).split("_")[-1]
 
 
+def dropin_binary() -> Optional[str]:
+    """The harness linked with the B200 drop-in translation units instead of the reference's diffusion head,
+    sampler and foundation DiT (oracle/ref/Makefile target ``dropin``); needs a B200 to run."""
+    path = os.path.join(REF_DIR, "b2d_ref_dropin")
+    return path if os.path.exists(path) else None
+
+
 def run(cmd: str, inputs: Dict[str, B.Tensor], weights: Optional[Dict[str, B.Tensor]] = None,
-        threads: int = 0, reps: int = 1, weights_path: Optional[str] = None, timeout: float = 3600) -> Dict[str, B.Tensor]:
-    exe = binary()
+        threads: int = 0, reps: int = 1, weights_path: Optional[str] = None, timeout: float = 3600,
+        exe: Optional[str] = None) -> Dict[str, B.Tensor]:
+    exe = exe or binary()
     if exe is None:
         raise RuntimeError("reference CPU build not found under oracle/_ref (run oracle/ref/Makefile)")
     threads = threads or os.cpu_count() or 1

@@ -68,6 +68,17 @@ def head_golden(name: str) -> None:
     print("head", name, "ok", out["latents"].dims)
 
 
+def head_storage_golden(name: str, storage: int, tag: str) -> None:
+    """The head loaded with a weight storage type (quantize-on-load in the reference's weight store)."""
+    cfg = synth.HEAD_CONFIGS[name]
+    w, inp = synth.head_weights(cfg), synth.head_inputs(cfg)
+    inp["storage_type"] = B.i64(storage)
+    out = ref_runner.run("vv", inp, w)
+    B.write(os.path.join(HERE, "head_%s_as_%s.b2db" % (name, tag)),
+            {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("head", name, "as", tag, "ok")
+
+
 def sched_golden() -> None:
     rng = np.random.default_rng(7)
     for steps in (1, 2, 10, 20):
@@ -175,6 +186,8 @@ def main(argv) -> None:
             q8_golden()
         elif n == "sched":
             sched_golden()
+        elif n.startswith("headq8:"):  # storage type Q8_0 (assets::TensorStorageType::Q8_0 = 13)
+            head_storage_golden(n[7:], 13, "q8")
         elif n.startswith("head:"):
             head_golden(n[5:])
         elif n.startswith("dit:"):
