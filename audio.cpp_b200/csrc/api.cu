@@ -787,12 +787,16 @@ HeadWorkspace& head_workspace(b2d_ctx* ctx, HeadModel& m, int64_t batch) {
 
 // One evaluation of the head on ws.noisy / ws.cp (cond_proj already applied) with
 // the time embedding row temb_row -> ws.v.  diffusion_head.cpp:495-523.
-// RMSNorm + modulate of R rows: the warp-per-row kernel up to H = 4096, the CTA-per-row one above.
+// RMSNorm + modulate of R rows: one CTA per row (H a multiple of 256, up to 8192), else the warp-per-row kernel up
+// to H = 4096 and the looping CTA-per-row one above.
 template <typename CT>
 void launch_rms_modulate(const float* x, int64_t ldx, const float* w, const float* shift, const float* scale,
                          int64_t ldm, float eps, int64_t H, int64_t R, CT* out, int64_t ldo, cudaStream_t st) {
     const unsigned grid = unsigned((R + 7) / 8);
-    if (H <= 2048)
+    if (H % 256 == 0 && H <= 8192 && ldx % 4 == 0 && ldm % 4 == 0 && ldo % 8 == 0)  // CTA per row, 8 values per thread
+        launch_k(rms_modulate_row_kernel<CT>, dim3(unsigned(R)), dim3(unsigned(H / 8)), 0, st, 1, x, ldx, w, shift,
+                 scale, ldm, eps, int(H), out, ldo);
+    else if (H <= 2048)
         launch_k(rms_modulate_warp_kernel<CT, 16>, dim3(grid), dim3(256), 0, st, 1, x, ldx, w, shift, scale, ldm, eps,
                  int(H), R, out, ldo);
     else if (H <= 4096)

@@ -142,6 +142,52 @@ __global__ void __launch_bounds__(THREADS) rms_modulate_kernel(const float* __re
     }
 }
 
+// Block-wide sum over blockDim.x (a multiple of 32, at most 1024) threads; every thread gets the total.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();  // red may still be read by a previous reduction
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = (threadIdx.x & 31) < nw ? red[threadIdx.x & 31] : 0.f;
+    return warp_sum(t);
+}
+
+// Same computation, one CTA per row with 8 values per thread (blockDim = H / 8): every operand of the row --
+// x, shift, scale and the norm weight -- is requested before the reduction, so a row costs one memory
+// latency, and a few thousand rows keep every SM busy.
+template <typename CT>
+__global__ void __launch_bounds__(1024) rms_modulate_row_kernel(const float* __restrict__ x, int64_t ldx,
+                                                                const float* __restrict__ w,
+                                                                const float* __restrict__ shift,
+                                                                const float* __restrict__ scale, int64_t ldm,
+                                                                float eps, int H, CT* __restrict__ out, int64_t ldo) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float red[32];
+    const int64_t row = blockIdx.x;
+    const int i0 = threadIdx.x * 2;  // float4 index
+    const float4* x4 = reinterpret_cast<const float4*>(x + row * ldx) + i0;
+    const float4* s4 = reinterpret_cast<const float4*>(shift + row * ldm) + i0;
+    const float4* c4 = reinterpret_cast<const float4*>(scale + row * ldm) + i0;
+    const float4 v0 = x4[0], v1 = x4[1];
+    const float4 sh0 = s4[0], sh1 = s4[1], sc0 = c4[0], sc1 = c4[1];
+    float4 w0 = make_float4(1.f, 1.f, 1.f, 1.f), w1 = w0;
+    if (w) {
+        w0 = __ldg(reinterpret_cast<const float4*>(w) + i0);
+        w1 = __ldg(reinterpret_cast<const float4*>(w) + i0 + 1);
+    }
+    const float ss = v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w + v1.x * v1.x + v1.y * v1.y +
+                     v1.z * v1.z + v1.w * v1.w;
+    const float inv = 1.0f / sqrtf(block_sum(ss, red) / float(H) + eps);
+    uint4 o;
+    o.x = CtTraits<CT>::pack2(v0.x * inv * w0.x * (1.f + sc0.x) + sh0.x, v0.y * inv * w0.y * (1.f + sc0.y) + sh0.y);
+    o.y = CtTraits<CT>::pack2(v0.z * inv * w0.z * (1.f + sc0.z) + sh0.z, v0.w * inv * w0.w * (1.f + sc0.w) + sh0.w);
+    o.z = CtTraits<CT>::pack2(v1.x * inv * w1.x * (1.f + sc1.x) + sh1.x, v1.y * inv * w1.y * (1.f + sc1.y) + sh1.y);
+    o.w = CtTraits<CT>::pack2(v1.z * inv * w1.z * (1.f + sc1.z) + sh1.z, v1.w * inv * w1.w * (1.f + sc1.w) + sh1.w);
+    reinterpret_cast<uint4*>(out + row * ldo)[threadIdx.x] = o;
+}
+
 // Same computation, one warp per row with the row held in registers (x read once, reductions by
 // shuffles only): rows of H <= 128 * MAXV floats; 8 rows per 256-thread CTA.
 template <typename CT, int MAXV>

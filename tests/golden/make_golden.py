@@ -122,6 +122,20 @@ def dit_golden(name: str) -> None:
     print("dit", name, "ok", out["latents"].dims)
 
 
+def dit_f32_golden(name: str) -> None:
+    """The same seeded BF16 weights handed to the reference as F32 tensors (exact values): the reference then
+    computes without rounding activations to bf16 before its matmuls.  Its distance to the BF16 run is the
+    reference's own activation-rounding spread at full length, which the stiff CFG-7 trajectory amplifies."""
+    cfg = synth.DIT_CONFIGS[name]
+    w, inp = synth.dit_weights(cfg), synth.dit_inputs(cfg)
+    w32 = {n: (B.Tensor(B.F32, t.dims, synth.decode_weight(t).reshape(-1).astype(np.float32))
+               if t.dtype == B.BF16 else t) for n, t in w.items()}
+    out = ref_runner.run("dit", inp, w32, timeout=6 * 3600)
+    B.write(os.path.join(HERE, "dit_%s_f32w.b2db" % name),
+            {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w32, inp))})
+    print("dit", name, "as f32 ok")
+
+
 def sa3_golden(name: str) -> None:
     """Stable Audio 3 DiT (StableAudioRfDitRuntime::sample) on a tiny seeded configuration."""
     cfg = synth.SA3_CONFIGS[name]
@@ -190,6 +204,8 @@ def main(argv) -> None:
             head_storage_golden(n[7:], 13, "q8")
         elif n.startswith("head:"):
             head_golden(n[5:])
+        elif n.startswith("ditf32:"):
+            dit_f32_golden(n[7:])
         elif n.startswith("dit:"):
             dit_golden(n[4:])
         elif n.startswith("sa3:"):
