@@ -74,7 +74,7 @@ def run(cfg, dit, inp):
 
 @pytest.mark.parametrize("name", ["tiny_bf16", "tiny_q8_b2_noapg", "tiny_f16_ragged", "sao_bf16_1x1024_2steps",
                                   "sao_q8_1x1024_2steps", "tiny_bf16_vddim", "tiny_f16_3msde",
-                                  "sao_q8_16x64_2steps", "sao_q8_16x1024_2steps", "sao_bf16_1x1024"])
+                                  "sao_q8_16x64_2steps", "sao_q8_16x1024_2steps"])
 def test_dit_sample_matches_reference(b2d, ctx, name):
     cfg, dit = make_dit(b2d, ctx, name)
     inp = synth.dit_inputs(cfg)
