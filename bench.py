@@ -169,12 +169,14 @@ def gemm_roofline(b2d, ctx, torch, cfg, peaks):
             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst, cuBLAS)" if "bf16_tflops" in peaks
             else "fallback 1590", "launch_us": round(dt * 1e6, 2), "flop_per_launch": flops,
             # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this GEMM shape (ncu, 1-SM kernel):
-            # = the algorithmic A + B bytes, no re-reads (profiles/gemm_swiglu_vv15_q8_1024.md)
+            # = the algorithmic A + B bytes, no re-reads
             "traffic": 34637056 + 26368, "traffic_unit": "bytes/launch"}
 
 
 DIT_WORKLOAD = "sao_bf16_1x1024"
-RESID_TRAFFIC_DIT = None  # filled from the ncu capture of the three residual-GEMM launches
+# dram__bytes_read.sum + dram__bytes_write.sum of one out-projection launch of that GEMM (ncu, one launch;
+# on the C3 workload): A 6.3 MB + W 4.7 MB + residual 12.6 MB read, i.e. no re-reads
+RESID_TRAFFIC_DIT = 23680000
 
 
 def gemm_time(b2d, ctx, torch, M, N, K, epilogue, bn=256, bf16=False, reps=30):
@@ -262,9 +264,8 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
                            "unit": "TFLOP/s", "frac": round(fl / t / 1e12 / peak, 4),
                            "launch_us": {"out_proj": round(t_o * 1e6, 2), "ff_out": round(t_f * 1e6, 2)},
                            "flop_per_layer": fl,
-                           # dram__bytes_read.sum + dram__bytes_write.sum summed over the three launches (ncu,
-                           # profiles/gemm_resid_sao_bf16_1x1024.md)
-                           "traffic": RESID_TRAFFIC_DIT, "traffic_unit": "bytes per layer (3 launches)"}
+                           "traffic": RESID_TRAFFIC_DIT,
+                           "traffic_unit": "bytes per out-projection launch (ncu); algorithmic 23.6 MB"}
         t_ff = gemm_time(b2d, ctx, torch, R, 8 * d, d, b2d.EPI_SWIGLU, bn=512, bf16=True)
         fl_ff = 2.0 * R * 8 * d * d
         res["ffn_in_gemm"] = {"kernel": "gemm_tc2_kernel<SWIGLU,bf16> 2-SM (FFN in, %dx%dx%d)" % (R, 8 * d, d),

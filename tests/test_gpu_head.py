@@ -33,6 +33,12 @@ def make_head(b2d, ctx, name):
     return _heads[name]
 
 
+# rel-L2 of the GPU latents against the fp32-activation restatement, measured on B200 (deterministic: the same
+# kernels and reduction orders every run), and the bound each case is held to (about 1.5x the measurement)
+MEASURED_VS_EXACT = {"tiny_f16": 5.3e-5, "tiny_q8": 1.44e-4, "tiny_bf16": 4.3e-4, "small_q8_ragged": 2.19e-4,
+                     "one_frame_f16": 8.7e-5, "one_step_q8": 4.35e-4, "vv15_f16_64": 6.2e-4, "vv15_q8_1024": 1.16e-3,
+                     "vv7_q8_32_3steps": 1.48e-3, "vv7_q8_1024": 1.42e-3}
+
 GOLDEN_HEADS = ["tiny_f16", "tiny_q8", "tiny_bf16", "small_q8_ragged", "one_frame_f16", "one_step_q8",
                 "vv15_f16_64", "vv15_q8_1024", "vv7_q8_32_3steps", "vv7_q8_1024"]
 
@@ -51,7 +57,7 @@ def test_sample_matches_reference(b2d, ctx, name):
     print("%s: vs ref %.3g (spread %.3g), vs exact %.3g" % (name, err, spread, rel_l2(out, exact)))
     assert err < max(LATENT_TOL, 1.5 * spread), "rel-L2 %.3g vs reference (spread %.3g)" % (err, spread)
     err_exact = rel_l2(out, exact)
-    assert err_exact < (1e-2 if cfg.wtype == synth.BF16 else 3e-3), "rel-L2 %.3g vs exact oracle" % err_exact
+    assert err_exact < 1.5 * MEASURED_VS_EXACT[name], "rel-L2 %.3g vs exact oracle" % err_exact
     # graph replay gives identical results
     out2 = head.sample(inp["positive_condition"].array(), inp["negative_condition"].array(),
                        inp["initial_speech"].array(), cfg.steps, cfg.cfg)
