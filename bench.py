@@ -59,6 +59,35 @@ def dist_setup():
     return world, rank, local
 
 
+def node_shared(fn, cfg):
+    """fn(cfg) computed once per node: with several ranks, local rank 0 synthesises the seeded weights and the
+    other ranks of the node read its pickle (the DiT's 1.1 GB of Q8_0 weights take about a minute of numpy per
+    synthesis, which eight ranks would otherwise repeat side by side).  Outside the timed region."""
+    world, _, local = dist_setup()
+    if world == 1:
+        return fn(cfg)
+    import pickle
+    import tempfile
+    import torch.distributed as dist
+    import zlib
+    tag = "%s_%08x" % (fn.__name__, zlib.crc32(repr(cfg).encode()))
+    path = os.path.join(tempfile.gettempdir(), "b2d_bench_%d_%s.pkl" % (os.getppid(), tag))
+    val = None
+    if local == 0:
+        val = fn(cfg)
+        with open(path + ".tmp", "wb") as f:
+            pickle.dump(val, f, protocol=5)
+        os.replace(path + ".tmp", path)
+    dist.barrier()
+    if local != 0:
+        with open(path, "rb") as f:
+            val = pickle.load(f)
+    dist.barrier()
+    if local == 0:
+        os.remove(path)
+    return val
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
 
@@ -213,7 +242,7 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     cfg = synth.DitConfig(**{**cfg.__dict__, "prompt_seeds": (rank,)})
     if args.dit_dpm_steps:  # profiling only: shorter schedules (the reported config says so)
         cfg = synth.DitConfig(**{**cfg.__dict__, "steps": args.dit_dpm_steps})
-    w = synth.dit_weights(cfg)
+    w = node_shared(synth.dit_weights, cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
                              cfg.io_channels, cfg.prompt_max_length,
@@ -296,7 +325,7 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
     if args.small:  # profiling only: a shape an ncu capture finishes (the reported config says so)
         cfg = synth.Sa3Config(**{**cfg.__dict__, "latent_tokens": 448, "steps": 2})
     cfg = synth.Sa3Config(**{**cfg.__dict__, "prompt_seeds": (rank,)})
-    w = synth.sa3_weights(cfg)
+    w = node_shared(synth.sa3_weights, cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     model = b2d.StableAudio3DiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_dim, cfg.global_cond_dim,
                                 cfg.local_add_cond_dim, cfg.num_memory_tokens, cfg.prompt_max_length,
@@ -361,7 +390,7 @@ def bench_oobleck(args, torch, b2d, ctx, world, rank, timed):
     cfg = synth.OOBLECK_CONFIGS[OOBLECK_WORKLOAD]
     if args.small:  # profiling only: 128 latents (262,144 frames), activations still larger than L2
         cfg = synth.OobleckConfig(**{**cfg.__dict__, "latent_tokens": 128})
-    w = synth.oobleck_weights(cfg)
+    w = node_shared(synth.oobleck_weights, cfg)
     dec = b2d.OobleckDecoder(ctx, cfg.latent_dim, cfg.channels, cfg.c_mults, cfg.strides, cfg.audio_channels,
                              weights=[(n, 0, t.dims, t.data) for n, t in w.items()])
     lat = synth.oobleck_inputs(synth.OobleckConfig(**{**cfg.__dict__, "seed": cfg.seed + rank}))["latents"].array()
@@ -436,7 +465,7 @@ def bench_c1(args, torch, b2d, ctx, world, rank, timed, peaks):
     judged on weight bytes per call against the measured HBM copy bandwidth.  Per rank its own 64 frames."""
     from oracle import synth
     cfg = synth.HEAD_CONFIGS["vv15_f16_64"]
-    w = synth.head_weights(cfg)
+    w = node_shared(synth.head_weights, cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
     head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
                                       weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
@@ -479,7 +508,7 @@ def bench_c5(args, torch, b2d, ctx, world, rank, timed, peaks):
     from oracle import synth
     par = _parallel_module()
     cfg = synth.HEAD_CONFIGS["vv7_q8_8192"]
-    w = synth.head_weights(cfg)
+    w = node_shared(synth.head_weights, cfg)
     head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
                                       weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
     del w
@@ -533,7 +562,7 @@ def bench_c4(args, torch, b2d, ctx, world, rank, timed, peaks):
     cfg = synth.DIT_CONFIGS["sao_q8_16x1024"]
     if args.dit_dpm_steps:
         cfg = synth.DitConfig(**{**cfg.__dict__, "steps": args.dit_dpm_steps})
-    w = synth.dit_weights(cfg)
+    w = node_shared(synth.dit_weights, cfg)
     dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
                              cfg.io_channels, cfg.prompt_max_length,
                              weights=[(n, GT[t.dtype], t.dims, t.data) for n, t in w.items()])
@@ -656,7 +685,7 @@ def bench_ours(args):
     cfg = synth.HEAD_CONFIGS[WORKLOAD]
     if args.workload in ("dit", "sa3", "oobleck", "c1", "c4", "c5"):
         return bench_dit_only(args, torch, b2d, world, rank, local)
-    w = synth.head_weights(cfg)
+    w = node_shared(synth.head_weights, cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     ctx = b2d.Context(local)

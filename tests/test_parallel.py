@@ -115,3 +115,45 @@ def test_prompt_shards_carry_the_batched_noise_slice():
             assert np.array_equal(local, noise[lo:hi])
             covered += list(range(lo, hi))
         assert covered == list(range(batch))
+
+
+def _shared_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import importlib.util
+    import torch.distributed as dist
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("b2d_bench", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import synth
+        cfg = synth.HEAD_CONFIGS["tiny_q8"]
+        calls = []
+
+        def make(c):
+            calls.append(rank)
+            return synth.head_weights(c)
+
+        w = bench.node_shared(make, cfg)
+        ref = synth.head_weights(cfg)
+        same = sorted(w) == sorted(ref) and all(np.array_equal(w[k].data, ref[k].data) for k in ref)
+        q.put((rank, same, len(calls)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_weights_synthesised_once_per_node():
+    """bench.py's ranks on one node share one synthesis of the seeded weights: only local rank 0 runs it and
+    every rank ends with the same bytes."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shared_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == [(0, True, 1), (1, True, 0)]
