@@ -59,6 +59,14 @@ def dist_setup():
     return world, rank, local
 
 
+def _host_barrier(dist):
+    """A barrier the host leaves only after every rank entered it (an NCCL barrier returns once it is queued)."""
+    dist.barrier()
+    import torch
+    if torch.cuda.is_available() and dist.get_backend() == "nccl":
+        torch.cuda.synchronize()
+
+
 def node_shared(fn, cfg):
     """fn(cfg) computed once per node: with several ranks, local rank 0 synthesises the seeded weights and the
     other ranks of the node read its pickle (the DiT's 1.1 GB of Q8_0 weights take about a minute of numpy per
@@ -78,11 +86,11 @@ def node_shared(fn, cfg):
         with open(path + ".tmp", "wb") as f:
             pickle.dump(val, f, protocol=5)
         os.replace(path + ".tmp", path)
-    dist.barrier()
+    _host_barrier(dist)
     if local != 0:
         with open(path, "rb") as f:
             val = pickle.load(f)
-    dist.barrier()
+    _host_barrier(dist)
     if local == 0:
         os.remove(path)
     return val
