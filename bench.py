@@ -59,40 +59,44 @@ def dist_setup():
     return world, rank, local
 
 
-def _host_barrier(dist):
-    """A barrier the host leaves only after every rank entered it (an NCCL barrier returns once it is queued)."""
-    dist.barrier()
-    import torch
-    if torch.cuda.is_available() and dist.get_backend() == "nccl":
-        torch.cuda.synchronize()
+def _wait_for(path, what, limit_s=1800.0):
+    t0 = time.time()
+    while not os.path.exists(path):
+        if time.time() - t0 > limit_s:
+            raise TimeoutError("bench: gave up waiting for " + what)
+        time.sleep(0.2)
 
 
 def node_shared(fn, cfg):
     """fn(cfg) computed once per node: with several ranks, local rank 0 synthesises the seeded weights and the
     other ranks of the node read its pickle (the DiT's 1.1 GB of Q8_0 weights take about a minute of numpy per
-    synthesis, which eight ranks would otherwise repeat side by side).  Outside the timed region."""
+    synthesis, which eight ranks would otherwise repeat side by side).  The hand-off is through files only (the
+    file appears by an atomic rename; each reader leaves a marker; the writer removes all once every local rank
+    has read), so it does not depend on when a device-side barrier returns.  Outside the timed region."""
     world, _, local = dist_setup()
     if world == 1:
         return fn(cfg)
     import pickle
     import tempfile
-    import torch.distributed as dist
     import zlib
+    nlocal = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     tag = "%s_%08x" % (fn.__name__, zlib.crc32(repr(cfg).encode()))
     path = os.path.join(tempfile.gettempdir(), "b2d_bench_%d_%s.pkl" % (os.getppid(), tag))
-    val = None
     if local == 0:
         val = fn(cfg)
         with open(path + ".tmp", "wb") as f:
             pickle.dump(val, f, protocol=5)
         os.replace(path + ".tmp", path)
-    _host_barrier(dist)
-    if local != 0:
-        with open(path, "rb") as f:
-            val = pickle.load(f)
-    _host_barrier(dist)
-    if local == 0:
+        for r in range(1, nlocal):
+            _wait_for("%s.read%d" % (path, r), "local rank %d to read %s" % (r, path))
+        for r in range(1, nlocal):
+            os.remove("%s.read%d" % (path, r))
         os.remove(path)
+        return val
+    _wait_for(path, path)
+    with open(path, "rb") as f:
+        val = pickle.load(f)
+    open("%s.read%d" % (path, local), "w").close()
     return val
 
 
