@@ -28,6 +28,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "latent frames/sec (VibeVoice diffusion head)"
 UNIT = "frames/s"
+T_START = time.time()
 WORKLOAD = "vv15_q8_1024"
 
 
@@ -59,21 +60,31 @@ def dist_setup():
     return world, rank, local
 
 
-def _wait_for(path, what, limit_s=1800.0):
+def _wait_for(path, limit_s):
     t0 = time.time()
     while not os.path.exists(path):
         if time.time() - t0 > limit_s:
-            raise TimeoutError("bench: gave up waiting for " + what)
+            return False
         time.sleep(0.2)
+    return True
 
 
-def node_shared(fn, cfg):
+def log(msg):
+    """Progress on stderr (stdout carries only the JSON line)."""
+    print("[bench rank %s %.0fs] %s" % (os.environ.get("RANK", "0"), time.time() - T_START, msg), file=sys.stderr,
+          flush=True)
+
+
+def node_shared(fn, cfg, wait_s=600.0):
     """fn(cfg) computed once per node: with several ranks, local rank 0 synthesises the seeded weights and the
     other ranks of the node read its pickle (the DiT's 1.1 GB of Q8_0 weights take about a minute of numpy per
     synthesis, which eight ranks would otherwise repeat side by side).  The hand-off is through files only (the
-    file appears by an atomic rename; each reader leaves a marker; the writer removes all once every local rank
-    has read), so it does not depend on when a device-side barrier returns.  Outside the timed region."""
+    file appears by an atomic rename; each reader leaves a marker; the writer removes both once every local rank
+    has read), so it does not depend on when a device-side barrier returns.  Every rank must pass the same
+    `cfg`; should a rank not find the file within `wait_s` seconds it synthesises the weights itself (and the writer
+    stops waiting for it), so a mismatch costs time, never a hang.  Outside the timed region."""
     world, _, local = dist_setup()
+    log("weights: %s" % fn.__name__)
     if world == 1:
         return fn(cfg)
     import pickle
@@ -87,13 +98,16 @@ def node_shared(fn, cfg):
         with open(path + ".tmp", "wb") as f:
             pickle.dump(val, f, protocol=5)
         os.replace(path + ".tmp", path)
-        for r in range(1, nlocal):
-            _wait_for("%s.read%d" % (path, r), "local rank %d to read %s" % (r, path))
-        for r in range(1, nlocal):
-            os.remove("%s.read%d" % (path, r))
-        os.remove(path)
+        if all(_wait_for("%s.read%d" % (path, r), wait_s) for r in range(1, nlocal)):
+            for r in range(1, nlocal):
+                os.remove("%s.read%d" % (path, r))
+            os.remove(path)
+        else:
+            print("bench: a local rank did not read %s; left in place" % path, file=sys.stderr, flush=True)
         return val
-    _wait_for(path, path)
+    if not _wait_for(path, wait_s):
+        print("bench: %s did not appear; synthesising on this rank" % path, file=sys.stderr, flush=True)
+        return fn(cfg)
     with open(path, "rb") as f:
         val = pickle.load(f)
     open("%s.read%d" % (path, local), "w").close()
@@ -251,10 +265,10 @@ def bench_dit(args, torch, b2d, ctx, world, rank, timed, peaks):
     CFG 7, APG 1.  Per rank its own prompt (weak scaling).  Metric: sequence-steps/s over all ranks."""
     from oracle import synth
     cfg = synth.DIT_CONFIGS[DIT_WORKLOAD]
+    w = node_shared(synth.dit_weights, cfg)  # the same weights on every rank
     cfg = synth.DitConfig(**{**cfg.__dict__, "prompt_seeds": (rank,)})
     if args.dit_dpm_steps:  # profiling only: shorter schedules (the reported config says so)
         cfg = synth.DitConfig(**{**cfg.__dict__, "steps": args.dit_dpm_steps})
-    w = node_shared(synth.dit_weights, cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     dit = b2d.StableAudioDiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_token_dim, cfg.global_cond_dim,
                              cfg.io_channels, cfg.prompt_max_length,
@@ -336,8 +350,8 @@ def bench_sa3(args, torch, b2d, ctx, world, rank, timed):
     cfg = synth.SA3_CONFIGS[SA3_WORKLOAD]
     if args.small:  # profiling only: a shape an ncu capture finishes (the reported config says so)
         cfg = synth.Sa3Config(**{**cfg.__dict__, "latent_tokens": 448, "steps": 2})
+    w = node_shared(synth.sa3_weights, cfg)  # the same weights on every rank
     cfg = synth.Sa3Config(**{**cfg.__dict__, "prompt_seeds": (rank,)})
-    w = node_shared(synth.sa3_weights, cfg)
     gt = {0: 0, 1: 1, 3: 8, 2: 30}
     model = b2d.StableAudio3DiT(ctx, cfg.embed_dim, cfg.depth, cfg.num_heads, cfg.cond_dim, cfg.global_cond_dim,
                                 cfg.local_add_cond_dim, cfg.num_memory_tokens, cfg.prompt_max_length,

@@ -157,3 +157,36 @@ def test_bench_weights_synthesised_once_per_node():
     for p in procs:
         p.join(timeout=60)
     assert res == [(0, True, 1), (1, True, 0)]
+
+
+def _mismatch_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import importlib.util
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("b2d_bench", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    from oracle import synth
+    cfg = synth.HEAD_CONFIGS["tiny_q8" if rank == 0 else "tiny_f16"]  # ranks disagree: no shared file
+    w = bench.node_shared(synth.head_weights, cfg, wait_s=2.0)
+    ref = synth.head_weights(cfg)
+    q.put((rank, all(np.array_equal(w[k].data, ref[k].data) for k in ref)))
+
+
+def test_bench_weight_sharing_never_hangs_on_a_mismatch():
+    """Ranks that pass different configs each end with their own weights after the wait limit, not a hang."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mismatch_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == [(0, True), (1, True)]
+    import glob
+    import tempfile
+    for f in glob.glob(os.path.join(tempfile.gettempdir(), "b2d_bench_%d_*" % os.getpid())):
+        os.remove(f)  # the writer leaves its file when a reader never came
