@@ -4,11 +4,10 @@
 // weight: 128 FLOP per byte, against a ridge of about 260), so it is bound by the HBM weight stream and every
 // SM must pull weights at once, whatever N is.  The grid is n_tiles x S CTAs: each column tile of BN weight
 // rows is split over the K dimension into S contiguous ranges, computed by the S CTAs of one thread-block
-// cluster.  Each CTA accumulates its K range in TMEM; CTA r owns rows [r 128 / S, (r + 1) 128 / S) of the
-// tile, and every CTA sends each accumulator row from TMEM to its owner's shared memory with asynchronous
-// distributed-shared-memory stores (st.async, bytes counted on the owner's mbarrier: nobody waits on a remote
-// load).  The owner adds the S partial rows in rank order (fixed order: results do not depend on timing),
-// applies the epilogue and writes the output with row-contiguous 16-byte stores.  No partial sum leaves the chip.
+// cluster.  Each CTA accumulates its K range in TMEM, copies the 128 x BN fp32 partial into its own shared
+// memory, and after a cluster barrier CTA r sums rows [r 128 / S, (r + 1) 128 / S) of all S partials in rank
+// order through distributed shared memory (fixed order: results do not depend on timing), applies the
+// epilogue and writes the output with row-contiguous 16-byte stores.  No partial sum leaves the chip.
 //
 // Weights come either as 16-bit [N, K] matrices (TMA, 128-byte swizzle) or as Q8_0 blocks
 // (ggml-common.h block_q8_0: 32 int8 quants + an fp16 scale d, value = q * d), stored k-block-major:
@@ -18,9 +17,8 @@
 // (ggml-quants.c) produces, rounded once to fp16 -- in the swizzled K-major layout the MMA reads.
 //
 // CTA: warp 0 issues the weight loads (and, for 16-bit weights, the activation loads), warp 1 owns TMEM and
-// issues tcgen05.mma (M = 128, N = BN, K = 16) from one lane, warps 2-5 (one TMEM lane quarter each) send the
-// accumulator rows to their owners, warps 6-9 (Q8_0 only) dequantise and load the activations; all warps take
-// part in the reduction.
+// issues tcgen05.mma (M = 128, N = BN, K = 16) from one lane, warps 2-5 move the accumulator to shared
+// memory, warps 6-9 (Q8_0 only) dequantise and load the activations; all warps take part in the reduction.
 #pragma once
 
 #include "gemm.cuh"
@@ -38,8 +36,8 @@ struct StreamShape {
     static constexpr uint32_t Q_BYTES = BN * 64;  // int8 quants of one k-block
     static constexpr uint32_t D_BYTES = BN * 4;   // two fp16 scales per row
     static constexpr uint32_t RAW_BYTES = Q_BYTES + D_BYTES;
-    // partial rows received from the cluster: up to 128 + 7 slot rows of BN fp32 (reuses the operand ring)
-    static constexpr uint32_t ACC_BYTES = (128 + 8) * BN * 4;
+    static constexpr int LDS = BN + 4;            // fp32 row stride of the accumulator copy (bank spread)
+    static constexpr uint32_t ACC_BYTES = 128 * LDS * 4;
     // 16-bit weights: a deep operand ring (the weight stream needs ~64 KB in flight per SM); Q8_0: a short
     // operand ring fed by the dequantisers and a deep ring of raw blocks.
     static constexpr int STAGES = WF == WF_Q8 ? 3 : (BN == 64 ? 8 : BN == 128 ? 6 : BN == 192 ? 5 : 4);
@@ -108,15 +106,14 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* raw = smem + S::OPER_BYTES;
-    float* accs = reinterpret_cast<float*>(smem);  // received partial rows (reuse the operand ring at the end)
+    float* accs = reinterpret_cast<float*>(smem);  // the accumulator copy reuses the operand ring at the end
     uint64_t* full = reinterpret_cast<uint64_t*>(raw + size_t(WF == WF_Q8 ? S::RAW_STAGES : 0) * S::RAW_BYTES);
     uint64_t* bfull = full + STAGES;
     uint64_t* empty = bfull + STAGES;
     uint64_t* rfull = empty + STAGES;
     uint64_t* rempty = rfull + RAW;
     uint64_t* tfull = rempty + RAW;
-    uint64_t* rbar = tfull + 1;  // rows of this CTA's share of the tile received from the cluster
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -139,11 +136,8 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
             mbar_init(&rempty[r], 4);
         }
         mbar_init(tfull, 1);
-        mbar_init(rbar, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        const int own = min((rank + 1) * 128 / nsplit, sa.M) - rank * 128 / nsplit;
-        if (nsplit > 1 && own > 0) mbar_arrive_expect_tx(rbar, uint32_t(nsplit * own * BN * 4));
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
@@ -265,56 +259,29 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
             }
         }
     } else {
-        // warps 2-5: the accumulator is complete once tfull fires (the rows leave TMEM below)
-        mbar_wait(tfull, 0, abort_flag, ep.status, kErrTimeoutEpilogue);
-    }
-
-    // Cluster reduction.  CTA q owns rows [r0, r1) of the tile; every CTA sends each of its accumulator rows
-    // straight from TMEM to the owner's shared memory (slot [sender rank][row - r0], 16-byte chunks
-    // XOR-swizzled by slot row), with asynchronous stores that count their bytes on the owner's mbarrier; the
-    // owner adds the slots in rank order (fixed order: results do not depend on timing).  The slots reuse the
-    // operand ring, so the first cluster barrier waits until every CTA's MMAs have finished reading it.
-    // Every thread of every CTA reaches both cluster barriers, also after a wait gave up (the status word then
-    // reports it and the output is not used).
-    tc_fence_before();
-    __syncthreads();
-    if (nsplit > 1) cluster_sync();
-    tc_fence_after();
-    const int RP = (128 + nsplit - 1) / nsplit;  // slot rows per sender
-    if (warp >= 2 && warp < 6) {
-        const int row = (warp & 3) * 32 + lane;
-        const uint32_t tb = tmem_base + (uint32_t((warp & 3) * 32) << 16);
-        if (row < sa.M) {
-            int q = row * nsplit / 128;
-            while ((q + 1) * 128 / nsplit <= row) ++q;
-            while (q * 128 / nsplit > row) --q;
-            const int srow = rank * RP + (row - q * 128 / nsplit);
-            const uint32_t sw = uint32_t(srow & 7);
-            const uint32_t local = smem_u32(accs) + uint32_t(srow * BN * 4);
-            const uint32_t dst = nsplit > 1 ? map_to_cta(local, uint32_t(q)) : local;
-            const uint32_t bar = map_to_cta(smem_u32(rbar), uint32_t(q));
+        // warps 2-5: TMEM lanes [32 q, 32 q + 32) -> accumulator copy rows (stride LDS floats)
+        const int quarter = warp & 3;
+        if (mbar_wait(tfull, 0, abort_flag, ep.status, kErrTimeoutEpilogue)) {
+            tc_fence_after();
+            const uint32_t tb = tmem_base + (uint32_t(quarter * 32) << 16);
+            float* arow = accs + size_t(quarter * 32 + lane) * S::LDS;
 #pragma unroll 1
             for (int c = 0; c < C; ++c) {
                 float v[32];
                 tmem_ld_32x32b_x32(tb + uint32_t(c * 32), v);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 f = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                    const uint32_t off = ((uint32_t(c * 8 + j) ^ sw) << 4);
-                    if (nsplit > 1)
-                        st_async_f4(dst + off, f, bar);
-                    else
-                        *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(accs) + size_t(srow) * BN * 4 + off) = f;
-                }
+                for (int q = 0; q < 8; ++q)
+                    *reinterpret_cast<float4*>(arow + c * 32 + 4 * q) =
+                        make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
         }
     }
+    // Every thread of every CTA of the cluster reaches both cluster barriers, also after a wait gave up (the
+    // status word then reports it and the output is not used).
     tc_fence_before();
-    if (nsplit > 1)
-        cluster_arrive_relaxed();  // rows sent; the matching wait keeps every CTA resident until all arrived
-    else
-        __syncthreads();
+    __syncthreads();
+    if (nsplit > 1) cluster_sync();
     pdl_wait();  // outputs / residual / gate belong to the previous kernels until they completed
     {
         const int r0 = rank * 128 / nsplit;
@@ -322,9 +289,10 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
         if (r1 > sa.M) r1 = sa.M;
         constexpr int GC = EPI == EPI_SWIGLU ? 128 / 4 : BN / 4;  // 4-column groups per row
         constexpr int U = 4;                                     // groups in flight per thread
-        const int total = r1 > r0 ? (r1 - r0) * GC : 0;
-        bool ready = nsplit == 1;
+        const uint32_t base = smem_u32(accs);
+        const int total = (r1 - r0) * GC;
         for (int e0 = threadIdx.x; e0 < total; e0 += U * int(blockDim.x)) {
+            // issue every load of U groups (peer partials; residual and gate) before using any of them
             float4 v[U], u[U], x[U], g[U];
 #pragma unroll
             for (int k = 0; k < U; ++k) {
@@ -340,25 +308,25 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
                             ep.gate + (ep.gate_rows ? row / ep.gate_rows : row) * ep.ldg + col);
                 }
             }
-            if (!ready) {  // the residual / gate loads above are in flight meanwhile
-                mbar_wait_cluster(rbar, 0, abort_flag, ep.status, kErrTimeoutEpilogue);
-                ready = true;
-            }
-            for (int q = 0; q < nsplit; ++q) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (q >= nsplit) break;
+                float4 p[U], pu[U];
 #pragma unroll
                 for (int k = 0; k < U; ++k) {
                     const int e = e0 + k * int(blockDim.x);
                     if (e < total) {
-                        const int srow = q * RP + e / GC;
-                        const uint32_t sw = uint32_t(srow & 7);
-                        const float* slot = accs + size_t(srow) * BN;
-                        const float4 p = *reinterpret_cast<const float4*>(slot + ((uint32_t(e % GC) ^ sw) << 2));
-                        v[k] = make_float4(v[k].x + p.x, v[k].y + p.y, v[k].z + p.z, v[k].w + p.w);
-                        if (EPI == EPI_SWIGLU) {
-                            const float4 pu = *reinterpret_cast<const float4*>(slot + ((uint32_t(e % GC + 32) ^ sw) << 2));
-                            u[k] = make_float4(u[k].x + pu.x, u[k].y + pu.y, u[k].z + pu.z, u[k].w + pu.w);
-                        }
+                        const uint32_t off = uint32_t(((r0 + e / GC) * S::LDS + (e % GC) * 4) * 4);
+                        const uint32_t a = map_to_cta(base + off, uint32_t(q));
+                        p[k] = ld_dsmem_f4(a);
+                        if (EPI == EPI_SWIGLU) pu[k] = ld_dsmem_f4(a + 128 * 4);
                     }
+                }
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    v[k] = make_float4(v[k].x + p[k].x, v[k].y + p[k].y, v[k].z + p[k].z, v[k].w + p[k].w);
+                    if (EPI == EPI_SWIGLU)
+                        u[k] = make_float4(u[k].x + pu[k].x, u[k].y + pu[k].y, u[k].z + pu[k].z, u[k].w + pu[k].w);
                 }
             }
             if (*abort_flag) continue;
@@ -370,8 +338,7 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
             }
         }
     }
-    if (nsplit > 1) cluster_wait();  // no CTA leaves while a partner may still send to it
-    __syncthreads();
+    if (nsplit > 1) cluster_sync();  // no CTA leaves while a partner still reads its shared memory
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, S::TMEM_COLS);
