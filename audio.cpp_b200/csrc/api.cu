@@ -194,6 +194,12 @@ CUtensorMap make_tmap_f32_box32(const void* base, int64_t rows, int64_t cols, in
     return m;
 }
 
+// The residual (and gate) of EPI_RESID can go through TMA boxes: plain 16-byte aligned fp32 matrices.
+bool resid_tma_ok(const EpiParams& ep, int64_t N) {
+    return !ep.gate_rows && reinterpret_cast<uintptr_t>(ep.resid) % 16 == 0 && ep.ldr % 4 == 0 && ep.ldr >= N &&
+           (!ep.gate || (reinterpret_cast<uintptr_t>(ep.gate) % 16 == 0 && ep.ldg % 4 == 0 && ep.ldg >= N));
+}
+
 template <int BN, int EPI, typename CT>
 void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int64_t N, int64_t K, const EpiParams& ep,
                    int num_sms, cudaStream_t st) {
@@ -214,9 +220,7 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
         e.tma_out = 1;
     }
     // residual (and gate) through TMA boxes when both are plain 16-byte aligned fp32 matrices
-    if (EPI == EPI_RESID && !ep.gate_rows && reinterpret_cast<uintptr_t>(ep.resid) % 16 == 0 && ep.ldr % 4 == 0 &&
-        ep.ldr >= N && (!ep.gate || (reinterpret_cast<uintptr_t>(ep.gate) % 16 == 0 && ep.ldg % 4 == 0 &&
-                                     ep.ldg >= N))) {
+    if (EPI == EPI_RESID && resid_tma_ok(ep, N)) {
         to = make_tmap_f32_box32(ep.resid, M, N, ep.ldr);
         if (ep.gate) tg = make_tmap_f32_box32(ep.gate, M, N, ep.ldg);
         e.tma_resid = 1;
@@ -230,13 +234,20 @@ void launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, int64_t M, int6
 template <int BN, int EPI, typename CT>
 void launch_gemm_pair_t(const CUtensorMap& ta, const CUtensorMap& tb_half, int64_t M, int64_t N, int64_t K,
                         const EpiParams& ep, int num_sms, cudaStream_t st) {
-    using S = GemmPairShape<BN>;
+    using S = GemmPairShape<BN, EPI>;
     set_smem_limit(gemm_tc2_kernel<BN, EPI, CT>, int(S::SMEM_BYTES));
     const int64_t units = ((M + 255) / 256) * (N / BN);
     if (units == 0) return;
     const int64_t pairs = units < num_sms / 2 ? units : num_sms / 2;
+    CUtensorMap to{}, tg{};
+    EpiParams e = ep;
+    if (EPI == EPI_RESID && resid_tma_ok(ep, N)) {
+        to = make_tmap_f32_box32(ep.resid, M, N, ep.ldr);
+        if (ep.gate) tg = make_tmap_f32_box32(ep.gate, M, N, ep.ldg);
+        e.tma_resid = 1;
+    }
     launch_k(gemm_tc2_kernel<BN, EPI, CT>, dim3(unsigned(2 * pairs)), dim3(192), S::SMEM_BYTES, st, 1, ta, tb_half,
-             int(M), int(N), int(K), ep);
+             to, tg, int(M), int(N), int(K), e);
 }
 
 // 2-SM pair tiles of 256 x bn (bn = 256 or 192); tb_half is B's tensor map with a bn / 2-row box.
@@ -404,7 +415,7 @@ struct HeadModel {
     DevBuf w_in, w_cond, w_t1, w_t2, w_ada, w_final, norms;
     std::vector<DevBuf> w_gu, w_down;
     CUtensorMap tm_in, tm_cond, tm_ada, tm_final, tm_t1, tm_t2;
-    std::vector<CUtensorMap> tm_gu, tm_gu128, tm_down256, tm_down192;
+    std::vector<CUtensorMap> tm_gu, tm_gu128, tm_down256, tm_down192, tm_down128;
     // Q8_0 checkpoints: the same projections kept as k-block-major Q8_0 planes for the weight-streaming GEMM
     // (few rows), next to the fp16 copies the tensor-bound GEMMs read.
     bool q8 = false;
@@ -709,11 +720,13 @@ void head_load_t(b2d_ctx* ctx, HeadModel& m, const b2d_tensor_view* ts, int n) {
     m.tm_gu128.clear();
     m.tm_down256.clear();
     m.tm_down192.clear();
+    m.tm_down128.clear();
     for (int64_t l = 0; l < L; ++l) {
         m.tm_gu.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 256));
         m.tm_gu128.push_back(make_tmap(m.w_gu[size_t(l)].p, bf, 2 * F, H, 128));  // 2-SM pair tiles
         m.tm_down256.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 256));
         if (H % 192 == 0) m.tm_down192.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 192));
+        if (H % 256 == 0) m.tm_down128.push_back(make_tmap(m.w_down[size_t(l)].p, bf, H, F, 128));  // pair tiles
     }
 }
 
@@ -857,13 +870,21 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         ep.ldr = H;
         ep.gate = shift + 2 * H;
         ep.ldg = m.NADA;
-        // 192-wide tiles when they fill the SMs better (H = 1536: 8 x 16 = 128 tiles vs 96)
+        // 192-wide tiles when they fill the SMs better (H = 1536: 8 x 16 = 128 tiles vs 96); 2-SM 256 x 256 pair
+        // tiles for wide or many-row projections, which cut the operand stream per SM by a third (measured with
+        // the gate: 7B width 2048 / 8192 / 16384 rows 175 / 580 / 1121 us against 216 / 738 / 1254 us for 1-SM
+        // 256-wide tiles; H = 1536 x 16384 rows 232 against 275 us; at H = 1536 x 2048 rows the 1-SM 192-wide
+        // tiles stay ahead, 34.9 against 36.9 us)
         const int64_t mt = (R + 127) / 128;
+        const int64_t pair_units = ((R + 255) / 256) * (H / 256);
+        const bool use_pair = !m.tm_down128.empty() && F >= 4096 && (pair_units >= sms || H >= 3072);
         const bool use192 = !m.tm_down192.empty() && waves_eff(mt * (H / 192), sms) > waves_eff(mt * (H / 256), sms);
         if (stream)
             launch_stream<CT>(ws.plan_down, EPI_RESID, ws.tm_ffn, q8s ? ws.tm_ada_s : ws.tm_down_s[size_t(l)],
                               q8s ? m.q_down[size_t(l)].as<int8_t>() : nullptr,
                               q8s ? m.d_down[size_t(l)].as<__half>() : nullptr, R, H, F, ep, st);
+        else if (use_pair)
+            launch_gemm_pair<CT>(EPI_RESID, ws.tm_ffn, m.tm_down128[size_t(l)], R, H, F, ep, sms, st, 256);
         else if (use192)
             launch_gemm<CT>(192, EPI_RESID, ws.tm_ffn, m.tm_down192[size_t(l)], R, H, F, ep, sms, st);
         else

@@ -122,21 +122,27 @@ struct GemmShape {
 // residual stream, 32 x 32 boxes through TMA.  The warp keeps up to 4 (2 with a gate) box loads in flight
 // ahead of the chunk it is updating, including the next unit's first chunks, so the residual / gate reads
 // overlap the MMA main loop instead of following it.  Returns false when a wait gave up.
+// Units: u = first, first + stride, ... < num_units; unit u covers rows (t % m_tiles) * m_step + row_off and
+// columns (t / m_tiles) * BN, t = u % num_tiles (1-SM tiles: m_step 128, row_off 0; 2-SM pair tiles: m_step
+// 256, row_off = 128 x the CTA's rank).  The accumulator goes back to the MMA warp on tempty[acc], or on the
+// leader CTA's barrier tempty_remote[acc] (a cluster address) for pair tiles.
 template <int BN>
 __device__ __forceinline__ bool resid_tma_epilogue(uint32_t tmem_base, int quarter, int lane, uint8_t* boxes,
                                                    uint64_t* bars, const CUtensorMap* tmR, const CUtensorMap* tmG,
                                                    const EpiParams& ep, int m_tiles, int num_tiles, int num_units,
-                                                   uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag) {
+                                                   uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag,
+                                                   int first, int stride, int m_step, int row_off,
+                                                   const uint32_t* tempty_remote) {
     constexpr int C = BN / 32;
     const bool has_gate = ep.gate != nullptr;
     const uint32_t nb = has_gate ? 2u : 4u;
     const uint32_t slot_bytes = has_gate ? 2 * kResidBoxBytes : kResidBoxBytes;
-    int lu = blockIdx.x, lc = 0;  // next box load: unit, chunk
+    int lu = first, lc = 0;  // next box load: unit, chunk
     uint32_t ld_seq = 0, cs_seq = 0;
     auto issue_next = [&]() {
         if (lu >= num_units) return;
         const int tile = lu % num_tiles;
-        const int m0 = (tile % m_tiles) * 128, n0 = (tile / m_tiles) * BN;
+        const int m0 = (tile % m_tiles) * m_step + row_off, n0 = (tile / m_tiles) * BN;
         const uint32_t slot = ld_seq % nb;
         uint8_t* box = boxes + slot * slot_bytes;
         mbar_arrive_expect_tx(&bars[slot], slot_bytes);
@@ -145,7 +151,7 @@ __device__ __forceinline__ bool resid_tma_epilogue(uint32_t tmem_base, int quart
         ++ld_seq;
         if (++lc == C) {
             lc = 0;
-            lu += gridDim.x;
+            lu += stride;
         }
     };
     if (lane == 0)
@@ -153,9 +159,9 @@ __device__ __forceinline__ bool resid_tma_epilogue(uint32_t tmem_base, int quart
     const uint32_t sw = uint32_t(lane & 7);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+    for (int u = first; u < num_units; u += stride) {
         const int tile = u % num_tiles;
-        const int m0 = (tile % m_tiles) * 128, n0 = (tile / m_tiles) * BN;
+        const int m0 = (tile % m_tiles) * m_step + row_off, n0 = (tile / m_tiles) * BN;
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, ep.status, kErrTimeoutEpilogue)) return false;
         tc_fence_after();
         const uint32_t tbase = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
@@ -166,7 +172,10 @@ __device__ __forceinline__ bool resid_tma_epilogue(uint32_t tmem_base, int quart
             tmem_ld_wait();
             if (c == C - 1) {  // the accumulator is in registers: hand TMEM back to the MMA warp
                 tc_fence_before();
-                mbar_arrive(&tempty[acc]);
+                if (tempty_remote)
+                    mbar_arrive_cluster(tempty_remote[acc]);
+                else
+                    mbar_arrive(&tempty[acc]);
             }
             if (ep.bias) {
 #pragma unroll
@@ -490,7 +499,8 @@ __global__ void __launch_bounds__(192, 1)
                 uint8_t* epi = smem + size_t(STAGES) * S::STAGE_BYTES;
                 resid_tma_epilogue<BN>(tmem_base, quarter, lane, epi + quarter * kResidWarpBytes,
                                        reinterpret_cast<uint64_t*>(epi + 4 * kResidWarpBytes) + quarter * 4, &tmO,
-                                       &tmG, ep, m_tiles, num_tiles, num_units, tfull, tempty, abort_flag);
+                                       &tmG, ep, m_tiles, num_tiles, num_units, tfull, tempty, abort_flag,
+                                       int(blockIdx.x), int(gridDim.x), BM, 0, nullptr);
                 goto done;
             }
         }
@@ -532,24 +542,30 @@ done:
 // both halves is counted on the leader's full barrier; commits multicast to both CTAs'
 // empty / tmem-full barriers; both epilogues release the accumulator on the leader's
 // tmem-empty barrier.  No TMA multicast is used.
-template <int BN_>
+template <int BN_, int EPI = -1>
 struct GemmPairShape {
     static constexpr int BM = 128;  // rows per CTA (256 per pair)
     static constexpr int BN = BN_;  // columns per pair tile (BN / 2 rows of B per CTA): 192 or 256
     static constexpr int BK = 64;
-    static constexpr int STAGES = BN == 256 ? 6 : 7;
     static constexpr uint32_t A_BYTES = BM * BK * 2;
     static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;
     static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+    // residual epilogue: the TMA box ring (1024-aligned, after the barrier block) next to a shorter operand ring
+    static constexpr bool RESID_TMA = EPI == EPI_RESID;
+    static constexpr int STAGES_FIT = int((232448 - 2048 - kResidStageBytes) / STAGE_BYTES);
+    static constexpr int STAGES = RESID_TMA ? (STAGES_FIT < 6 ? STAGES_FIT : 6) : (BN == 256 ? 6 : 7);
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + 256 + 4 * 32 * 33 * 4;
+    static constexpr size_t EPI_BYTES = RESID_TMA ? 1024 + kResidStageBytes : 256 + 4 * 32 * 33 * 4;
+    static constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 + EPI_BYTES;
+    static_assert(SMEM_BYTES <= 232448, "shared memory");
 };
 
 template <int BN_, int EPI, typename CT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmG, int M, int N,
                     int K, EpiParams ep) {
-    using S = GemmPairShape<BN_>;
+    using S = GemmPairShape<BN_, EPI>;
     constexpr int BM = S::BM, BN = S::BN, BK = S::BK, STAGES = S::STAGES;
 
     extern __shared__ uint8_t smem_raw[];
@@ -578,6 +594,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 256);
+        }
+        if constexpr (S::RESID_TMA) {
+            uint64_t* rb = reinterpret_cast<uint64_t*>(smem + size_t(STAGES) * S::STAGE_BYTES + 1024 +
+                                                       4 * kResidWarpBytes);
+            for (int i = 0; i < 16; ++i) mbar_init(&rb[i], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -654,9 +675,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         }
     } else {
         const int quarter = warp & 3;
-        float* stg = reinterpret_cast<float*>(smem + size_t(STAGES) * S::STAGE_BYTES + 256) + quarter * (32 * 33);
+        uint8_t* epi = smem + size_t(STAGES) * S::STAGE_BYTES + (S::RESID_TMA ? 1024 : 256);
+        float* stg = reinterpret_cast<float*>(epi) + quarter * (S::RESID_TMA ? kResidWarpBytes / 4 : 32 * 33);
         const uint32_t tempty_leader[2] = {map_to_cta(smem_u32(&tempty[0]), 0), map_to_cta(smem_u32(&tempty[1]), 0)};
         pdl_wait();
+        if constexpr (S::RESID_TMA) {
+            if (ep.tma_resid) {
+                resid_tma_epilogue<BN>(tmem_base, quarter, lane, epi + quarter * kResidWarpBytes,
+                                       reinterpret_cast<uint64_t*>(epi + 4 * kResidWarpBytes) + quarter * 4, &tmO,
+                                       &tmG, ep, pm, num_units, num_units, tfull, tempty, abort_flag, cluster,
+                                       nclusters, 2 * BM, int(rank) * BM, tempty_leader);
+                goto done;
+            }
+        }
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int u = cluster; u < num_units; u += nclusters) {

@@ -121,6 +121,12 @@ def test_pair_gemm_all_epilogues(ctx, bf16, m, n, k):
     torch.cuda.synchronize()
     want = x0 + gate * ref
     assert float((x - want).norm() / want.norm()) < 1e-5
+    x = x0.clone()  # no gate: x += acc + bias
+    ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=3, bn=512, bias=bias.data_ptr(),
+             resid=x.data_ptr(), ldr=n)
+    torch.cuda.synchronize()
+    want = x0 + ref
+    assert float((x - want).norm() / want.norm()) < 1e-5
     f = n // 2
     sw = torch.zeros(m, f, device="cuda", dtype=dt)
     ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=2, bn=512, bias=bias.data_ptr(),
@@ -159,4 +165,10 @@ def test_pair192_gemm_epilogues(ctx, bf16, m, n, k):
              resid=x.data_ptr(), ldr=n, gate=gate.data_ptr(), ldg=n)
     torch.cuda.synchronize()
     want = x0 + gate * ref
+    assert float((x - want).norm() / want.norm()) < 1e-5
+    x = x0.clone()  # no gate: x += acc + bias
+    ctx.gemm(a.data_ptr(), b.data_ptr(), m, n, k, bf16=bf16, epilogue=3, bn=384, bias=bias.data_ptr(),
+             resid=x.data_ptr(), ldr=n)
+    torch.cuda.synchronize()
+    want = x0 + ref
     assert float((x - want).norm() / want.norm()) < 1e-5
