@@ -193,10 +193,9 @@ DIT_CONFIGS = {
     "sao_q8_16x1024": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16))),
     # full-size parity cases (BASELINE C3/C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
     "sao_bf16_1x1024_2steps": DitConfig(steps=2),
-    # C3 at 10 and 25 DPM++ 2M steps: the multistep (second-order) update at full size, with the reference's
-    # latents and the fp32-activation restatement
+    # C3 at 10 DPM++ 2M steps: the multistep (second-order) update at full size, with the reference's latents
+    # (BF16 and F32 weights) and the fp32-activation restatement
     "sao_bf16_1x1024_10steps": DitConfig(steps=10),
-    "sao_bf16_1x1024_25steps": DitConfig(steps=25),
     # C3 in full (100 DPM++ 2M steps), with APG (the reference default) and as plain CFG
     "sao_bf16_1x1024_noapg": DitConfig(apg=0.0),
     # C4 at its full latent length: 16 prompts + CFG = 32 sequences x 1025 tokens, Q8_0, 2 steps
