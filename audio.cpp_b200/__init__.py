@@ -524,6 +524,16 @@ class StableAudioConditioner:
                                                 _ptr(cmask), _ptr(glob), C.c_void_p(stream)))
         return cross, cmask, glob
 
+    def encode(self, prompt_ids, prompt_mask, normalized_seconds, negative_ids=None, negative_mask=None,
+               stream: int = 0):
+        """FoundationConditionerRuntime::encode (src/models/stable_audio/foundation/conditioner.cpp:411-420): the
+        prompt batch and, when given, the negative prompt batch, both with the batch's normalized total seconds.
+        Returns {"positive": (cross, cross_mask, global), "negative": (...) or None}."""
+        out = {"positive": self.encode_one(prompt_ids, prompt_mask, normalized_seconds, stream), "negative": None}
+        if negative_ids is not None and len(negative_ids) > 0:
+            out["negative"] = self.encode_one(negative_ids, negative_mask, normalized_seconds, stream)
+        return out
+
 
 class VibeVoiceLanguageModel:
     """VibeVoiceDecoderWeightsRuntime's prefill / cached step (include/engine/models/vibevoice/decoder.h:106-143) on a

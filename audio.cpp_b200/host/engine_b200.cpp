@@ -1,6 +1,7 @@
 // Implementation of the audio.cpp-facing C++ classes (engine_b200.h) over the b200diff C ABI.
 #include "engine_b200.h"
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -450,12 +451,29 @@ FoundationConditionerRuntime::FoundationConditionerRuntime(const T5Config & conf
     device_->check(b2d_saocond_load(device_->ctx(), &c, views.data(), static_cast<int32_t>(views.size())));
 }
 
+// As FoundationConditionerRuntime::encode (src/models/stable_audio/foundation/conditioner.cpp:411-420).
+StableAudioConditioningInputs FoundationConditionerRuntime::encode(const StableAudioConditioningBatch & inputs) const {
+    StableAudioConditioningInputs out;
+    const std::vector<float> start(static_cast<size_t>(std::max<int64_t>(inputs.prompt_tokens.batch, 0)), 0.0F);
+    out.positive = encode_one(inputs.prompt_tokens, start, inputs.normalized_seconds);
+    if (inputs.negative_prompt_tokens.batch > 0) {
+        out.negative = encode_one(inputs.negative_prompt_tokens, start, inputs.normalized_seconds);
+        out.has_negative = true;
+    }
+    return out;
+}
+
 // Validation and messages as encode_one (src/models/stable_audio/foundation/conditioner.cpp:156-163, 422-430).
 StableAudioConditionedInput FoundationConditionerRuntime::encode_one(
-    const StableAudioTokenBatch & tokens, const std::vector<float> & normalized_total_seconds) const {
-    if (tokens.batch <= 0) throw std::runtime_error("Stable Audio Foundation conditioner requires a positive batch");
-    if (static_cast<int64_t>(normalized_total_seconds.size()) != tokens.batch)
-        throw std::runtime_error("Stable Audio Foundation conditioner seconds batch does not match prompt batch");
+    const StableAudioTokenBatch & tokens, const std::vector<float> & normalized_start_seconds,
+    const std::vector<float> & normalized_total_seconds) const {
+    for (const auto * seconds : {&normalized_start_seconds, &normalized_total_seconds}) {
+        if (tokens.batch <= 0) throw std::runtime_error("Stable Audio Foundation conditioner requires a positive batch");
+        if (static_cast<int64_t>(seconds->size()) != tokens.batch)
+            throw std::runtime_error("Stable Audio Foundation conditioner seconds batch does not match prompt batch");
+    }
+    for (const float s : normalized_start_seconds)
+        if (s != 0.0F) throw std::runtime_error("b200: conditioner evaluates seconds_start at 0 only");
     if (tokens.tokens != config_.prompt_max_length)
         throw std::runtime_error("Stable Audio Foundation conditioner token length mismatch");
     const int64_t B = tokens.batch, P = tokens.tokens, d = config_.t5_hidden_size;

@@ -235,6 +235,21 @@ struct StableAudioSamplingState {
     std::vector<float> local_add_conditioning;
 };
 
+// Token batches and the conditioning batch (include/engine/models/stable_audio/conditioner.h:14-26).
+struct StableAudioTokenBatch {
+    int64_t batch = 0;
+    int64_t tokens = 0;
+    std::vector<int32_t> input_ids;
+    std::vector<uint8_t> attention_mask;
+};
+
+struct StableAudioConditioningBatch {
+    StableAudioTokenBatch prompt_tokens;
+    StableAudioTokenBatch negative_prompt_tokens;
+    std::vector<float> normalized_seconds;
+    std::vector<float> seconds_fourier_features;
+};
+
 struct StableAudioConditionedInput {
     int64_t batch = 0;
     int64_t cross_tokens = 0;
@@ -291,22 +306,21 @@ struct T5Config {
     float t5_rms_norm_eps = 1.0e-6F;
 };
 
-struct StableAudioTokenBatch {
-    int64_t batch = 0;
-    int64_t tokens = 0;
-    std::vector<int32_t> input_ids;
-    std::vector<uint8_t> attention_mask;
-};
-
-// FoundationConditionerRuntime::encode_one on the GPU (b2d_saocond_*).
+// FoundationConditionerRuntime on the GPU (b2d_saocond_*): encode runs the prompt batch and, when it has one, the
+// negative prompt batch, with normalized start seconds 0 and the batch's normalized total seconds, as
+// include/engine/models/stable_audio/foundation/conditioner.h:43-72 declares it (encode public, encode_one private).
 class FoundationConditionerRuntime {
 public:
     FoundationConditionerRuntime(const T5Config & config, const std::vector<engine::b200::RawTensor> & tensors,
                                  int device);
-    StableAudioConditionedInput encode_one(const StableAudioTokenBatch & tokens,
-                                           const std::vector<float> & normalized_total_seconds) const;
+    StableAudioConditioningInputs encode(const StableAudioConditioningBatch & inputs) const;
 
 private:
+    // The device path evaluates seconds_start at 0 only (what encode passes); other start values are rejected.
+    StableAudioConditionedInput encode_one(const StableAudioTokenBatch & tokens,
+                                           const std::vector<float> & normalized_start_seconds,
+                                           const std::vector<float> & normalized_total_seconds) const;
+
     T5Config config_;
     std::unique_ptr<engine::b200::Device> device_;
 };

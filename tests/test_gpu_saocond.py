@@ -28,3 +28,7 @@ def test_saocond_encode_matches_reference(b2d, ctx, name):
     if cfg.has_negative:
         neg, _, _ = cond.encode_one(inp["negative_ids"].array(), inp["negative_mask"].array(), secs)
         assert rel_l2(neg, g["cross_negative"].array()) < 1e-2
+        # encode (the reference's public entry) runs both batches and returns the same values
+        both = cond.encode(inp["input_ids"].array(), inp["attention_mask"].array(), secs,
+                           inp["negative_ids"].array(), inp["negative_mask"].array())
+        assert rel_l2(both["positive"][0], cross) < 1e-6 and rel_l2(both["negative"][0], neg) < 1e-6
