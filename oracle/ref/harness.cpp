@@ -11,6 +11,8 @@
 //   vvpredict <weights> <in> <out> <thr>   one VibeVoiceDiffusionHeadWeightsRuntime::predict
 //   vv <weights> <in> <out> <thr> <reps>   sample_vibevoice_speech_latents (whole step loop)
 //   dit <weights> <in> <out> <thr> <reps> FoundationRfDitRuntime::sample
+//   dit_fresh <weights> <in> <out> <thr> <reps>  the same DPM++ 2M trajectory with a fresh FoundationRfDitRuntime
+//                                         for every model evaluation (see cmd_dit)
 //   sa3 <weights> <in> <out> <thr> <reps> StableAudioRfDitRuntime::sample (Stable Audio 3 DiT)
 //
 // Reference entry points exercised (paths inside audio.cpp):
@@ -39,6 +41,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -336,7 +339,8 @@ int cmd_vv(const std::string & w, const std::string & in_path, const std::string
 }
 
 // ---------------------------------------------------------- Stable Audio DiT
-int cmd_dit(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps) {
+int cmd_dit(const std::string & w, const std::string & in_path, const std::string & out_path, int threads, int reps,
+            bool fresh_graph_per_step = false) {
     namespace sa = engine::models::stable_audio;
     const Bundle in = read_bundle(in_path);
     auto assets = std::make_shared<sa::StableAudioAssets>();
@@ -397,8 +401,62 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     std::vector<float> times;
     uint64_t final_offset = 0;
     std::vector<float> result;
-    dit.prepare(sampling, cfg_scale);
-    for (int r = 0; r < std::max(reps, 1); ++r) {
+    if (fresh_graph_per_step) {
+        // FoundationRfDitRuntime computes correctly only on the first compute of its graph: its RoPE positions
+        // input is written once, when the graph is built (src/models/stable_audio/foundation/rf_dit.cpp:928-932),
+        // and ggml's graph allocator hands an input's memory to later nodes once its last consumer has run
+        // (external/ggml/src/ggml-alloc.c:692, 803-815), so every later compute reads stale positions.  Here each
+        // model evaluation runs on a fresh runtime (a one-step sample from sigma_i, which returns the denoised
+        // latent), and the DPM++ 2M update of sample_dpmpp_2m (rf_dit.cpp:814-872) is restated around it.
+        if (sampler != 0) throw std::runtime_error("dit_fresh supports the dpmpp-2m sampler only");
+        const double t0 = now_ms();
+        std::vector<float> sig(static_cast<size_t>(steps + 1), 0.0F);
+        for (int64_t i = 0; i < steps; ++i) {
+            const float ramp = steps == 1 ? 1.0F
+                                          : std::pow(1.0F - static_cast<float>(i) / static_cast<float>(steps - 1), rho);
+            sig[static_cast<size_t>(i)] = std::exp(ramp * (std::log(sigma_max) - std::log(sigma_min)) + std::log(sigma_min));
+        }
+        std::vector<float> x = sampling.noise;
+        for (float & v : x) v *= sig[0];
+        std::vector<float> old;
+        sa::StableAudioSamplingState one = sampling;
+        one.schedule_points = 2;
+        one.schedule.assign(static_cast<size_t>(batch * 2), 0.0F);
+        for (int64_t step = 0; step < steps; ++step) {
+            const float s = sig[static_cast<size_t>(step)], sn = sig[static_cast<size_t>(step + 1)];
+            for (size_t i = 0; i < x.size(); ++i) one.noise[i] = x[i] / s;
+            sa::foundation::FoundationRfDitRuntime fresh(exec, assets, storage);
+            fresh.prepare(one, cfg_scale);
+            uint64_t offset = 0;
+            std::vector<float> den = fresh.sample(one, cond, seed, offset, policy, sampler_name, 0.5F * s, s, rho,
+                                                  cfg_scale, apg_scale);
+            std::fprintf(stderr, "dit_fresh step %lld / %lld sigma %g\n", static_cast<long long>(step + 1),
+                         static_cast<long long>(steps), static_cast<double>(s));
+            if (sn == 0.0F) {
+                x = std::move(den);
+                break;
+            }
+            const float h = -std::log(sn) + std::log(s);
+            const float x_scale = sn / s;
+            const float den_scale = -std::expm1(-h);
+            if (old.empty()) {
+                for (size_t i = 0; i < x.size(); ++i) x[i] = x_scale * x[i] + den_scale * den[i];
+            } else {
+                const float h_last = std::log(sig[static_cast<size_t>(step - 1)]) - std::log(s);
+                const float r = h_last / h;
+                const float dc = 1.0F + 1.0F / (2.0F * r), oc = -1.0F / (2.0F * r);
+                for (size_t i = 0; i < x.size(); ++i) x[i] = x_scale * x[i] + den_scale * (dc * den[i] + oc * old[i]);
+            }
+            old = std::move(den);
+        }
+        result = std::move(x);
+        times.push_back(static_cast<float>(now_ms() - t0));
+        reps = 0;
+    } else {
+        dit.prepare(sampling, cfg_scale);
+        reps = std::max(reps, 1);
+    }
+    for (int r = 0; r < reps; ++r) {
         uint64_t offset = in.count("rng_offset") ? static_cast<uint64_t>(i64_scalar(in, "rng_offset")) : 0;
         const double t0 = now_ms();
         result = dit.sample(sampling, cond, seed, offset, policy, sampler_name, sigma_min, sigma_max, rho, cfg_scale,
@@ -803,6 +861,7 @@ int main(int argc, char ** argv) {
         if (cmd == "vvpredict") return cmd_vvpredict(arg(2), arg(3), arg(4), std::stoi(arg(5)));
         if (cmd == "vv") return cmd_vv(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "dit") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
+        if (cmd == "dit_fresh") return cmd_dit(arg(2), arg(3), arg(4), std::stoi(arg(5)), 1, true);
         if (cmd == "sa3") return cmd_sa3(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "vvlm") return cmd_vvlm(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));
         if (cmd == "saocond") return cmd_saocond(arg(2), arg(3), arg(4), std::stoi(arg(5)), std::stoi(arg(6)));

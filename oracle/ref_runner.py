@@ -73,7 +73,7 @@ def run(cmd: str, inputs: Dict[str, B.Tensor], weights: Optional[Dict[str, B.Ten
         inp, out = os.path.join(tmp, "in.b2db"), os.path.join(tmp, "out.b2db")
         B.write(inp, inputs)
         args = [exe, cmd]
-        if cmd in ("vvpredict", "vv", "dit", "sa3", "oobleck", "vvdec", "saocond", "vvlm"):
+        if cmd in ("vvpredict", "vv", "dit", "dit_fresh", "sa3", "oobleck", "vvdec", "saocond", "vvlm"):
             if weights_path is None:
                 weights_path = os.path.join(tmp, "w.b2db")
                 B.write(weights_path, weights)

@@ -136,6 +136,21 @@ def dit_f32_golden(name: str) -> None:
     print("dit", name, "as f32 ok")
 
 
+def dit_fresh_golden(name: str) -> None:
+    """The reference's DPM++ 2M trajectory with a fresh FoundationRfDitRuntime for every model evaluation (harness
+    command ``dit_fresh``).  The stock runtime computes its first graph call correctly and later calls with stale
+    RoPE positions (written once when the graph is built, rf_dit.cpp:928-932, while ggml's allocator lends an
+    input's memory to later nodes, ggml-alloc.c:692, 803-815), so its multi-step latents drift from its own
+    algorithm; this fixture holds the reference's arithmetic (BF16 weights, bf16-rounded activations) without that
+    drift."""
+    cfg = synth.DIT_CONFIGS[name]
+    w, inp = synth.dit_weights(cfg), synth.dit_inputs(cfg)
+    out = ref_runner.run("dit_fresh", inp, w, timeout=6 * 3600)
+    B.write(os.path.join(HERE, "dit_%s_fresh.b2db" % name),
+            {"latents": out["latents"], "input_sha256": B.Tensor(B.U8, (32,), digest(w, inp))})
+    print("dit", name, "fresh-graph ok")
+
+
 def sa3_golden(name: str) -> None:
     """Stable Audio 3 DiT (StableAudioRfDitRuntime::sample) on a tiny seeded configuration."""
     cfg = synth.SA3_CONFIGS[name]
@@ -204,6 +219,8 @@ def main(argv) -> None:
             head_storage_golden(n[7:], 13, "q8")
         elif n.startswith("head:"):
             head_golden(n[5:])
+        elif n.startswith("ditfresh:"):
+            dit_fresh_golden(n[9:])
         elif n.startswith("ditf32:"):
             dit_f32_golden(n[7:])
         elif n.startswith("dit:"):
