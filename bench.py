@@ -195,6 +195,57 @@ def bench_reference(args):
     print(json.dumps(line))
 
 
+def bench_ggml_cuda(args):
+    """GPU comparison point: the reference's own ggml-cuda backend (oracle/ref/Makefile VARIANT=cuda, compiled for
+    sm_100a from the vendored sources) running the reference's stock sampling entry points on the C2 head workload
+    and the C3 DiT workload, timed by the harness around each whole sampling call (host inputs in, host latents
+    out, the runtime and its device weights built before the first call).  One JSON line, rank 0 only."""
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from oracle import bundle as B
+    from oracle import ref_runner, synth
+    exe = ref_runner.cuda_binary()
+    if exe is None:
+        print(json.dumps({"impl": "reference-ggml-cuda", "unavailable": "oracle/_ref/b2d_ref_cuda not built"}))
+        return
+    env = {"B2D_REF_BACKEND": "cuda"}
+    golden_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden")
+
+    def rel_to_golden(name, lat):
+        path = os.path.join(golden_dir, name + ".b2db")
+        if not os.path.exists(path):
+            return None
+        ref = B.read(path)["latents"].array().astype(np.float64).ravel()
+        return float(np.linalg.norm(lat.astype(np.float64).ravel() - ref) / np.linalg.norm(ref))
+
+    line = {"impl": "reference-ggml-cuda", "n_gpus": 1, "backend": "audio.cpp vendored ggml-cuda, sm_100a"}
+    cfg = synth.HEAD_CONFIGS[WORKLOAD]
+    reps = args.warmup + args.steps
+    try:
+        o = ref_runner.run("vv", synth.head_inputs(cfg), synth.head_weights(cfg), reps=reps, exe=exe,
+                           env=env, timeout=900)
+        ms = float(np.median(np.asarray(o["wall_ms"].data[args.warmup:], np.float64)))
+        line["head"] = {"workload": WORKLOAD, "metric": METRIC, "value": round(cfg.frames / (ms / 1e3), 1),
+                        "unit": UNIT, "ms_per_call": round(ms, 3), "calls_timed": args.steps,
+                        "rel_l2_vs_reference_cpu": rel_to_golden("head_" + WORKLOAD, o["latents"].array())}
+    except Exception as e:  # the reference's failure is reported, not raised
+        line["head"] = {"unavailable": str(e).splitlines()[0][:300]}
+    dcfg = synth.DIT_CONFIGS[DIT_WORKLOAD]
+    try:
+        calls = max(1, args.dit_steps)
+        o = ref_runner.run("dit", synth.dit_inputs(dcfg), synth.dit_weights(dcfg), reps=1 + calls,
+                           exe=exe, env=env, timeout=1800)
+        ms = float(np.median(np.asarray(o["wall_ms"].data[1:], np.float64)))
+        line["dit"] = {"workload": DIT_WORKLOAD, "metric": "sequence-steps/s (SAO DiT, CFG rows counted)",
+                       "value": round(2 * dcfg.batch * dcfg.steps / (ms / 1e3), 3), "unit": "seq-steps/s",
+                       "ms_per_call": round(ms, 2), "calls_timed": calls,
+                       "rel_l2_vs_reference_cpu": rel_to_golden("dit_" + DIT_WORKLOAD, o["latents"].array())}
+    except Exception as e:
+        line["dit"] = {"unavailable": str(e).splitlines()[0][:300]}
+    print(json.dumps(line))
+
+
 def gemm_roofline(b2d, ctx, torch, cfg, peaks):
     """Times the dominant kernel (FFN gate/up GEMM + SwiGLU epilogue, 2048 x 9216 x 1536) with CUDA events."""
     M, K, N = 2 * cfg.frames, cfg.hidden, 2 * cfg.ffn
@@ -851,8 +902,12 @@ def main():
     ap.add_argument("--dit-warmup", type=int, default=1)
     ap.add_argument("--small", action="store_true",
                     help="profiling only: smaller SA3 / Oobleck shapes that an ncu capture can finish")
+    ap.add_argument("--gpu-baseline", action="store_true",
+                    help="time the reference's own ggml-cuda backend (oracle/_ref/b2d_ref_cuda) on C2 and C3 instead")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.gpu_baseline:
+        bench_ggml_cuda(args)
+    elif args.impl == "reference":
         bench_reference(args)
     else:
         bench_ours(args)

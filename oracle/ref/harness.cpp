@@ -44,6 +44,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -53,6 +54,14 @@
 #include <vector>
 
 namespace {
+
+// Backend the reference runtimes are created on: CPU unless B2D_REF_BACKEND=cuda (a build with VARIANT=cuda, which
+// links the vendored ggml-cuda backend; device 0).  The CUDA backend is a timing comparison point only.
+engine::core::BackendType ref_backend() {
+    const char * b = std::getenv("B2D_REF_BACKEND");
+    if (b != nullptr && std::strcmp(b, "cuda") == 0) return engine::core::BackendType::Cuda;
+    return engine::core::BackendType::Cpu;
+}
 
 // ---------------------------------------------------------------- bundle I/O
 // Layout: "B2DB" u32 version u32 count, then per entry
@@ -287,7 +296,7 @@ int cmd_vvpredict(const std::string & w, const std::string & in_path, const std:
     const Bundle in = read_bundle(in_path);
     auto assets = head_assets(w, in);
     engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime head(
-        assets, engine::core::BackendType::Cpu, 0, threads);
+        assets, ref_backend(), 0, threads);
     const auto noisy = f32s(in, "noisy");
     const auto cond = f32s(in, "condition");
     const int64_t latent = assets->config.diffusion_head.latent_size;
@@ -309,7 +318,7 @@ int cmd_vv(const std::string & w, const std::string & in_path, const std::string
                              ? static_cast<engine::assets::TensorStorageType>(i64_scalar(in, "storage_type"))
                              : engine::assets::TensorStorageType::Native;
     engine::models::vibevoice::VibeVoiceDiffusionHeadWeightsRuntime head(
-        assets, engine::core::BackendType::Cpu, 0, threads, 64ull * 1024ull * 1024ull, 64ull * 1024ull * 1024ull,
+        assets, ref_backend(), 0, threads, 64ull * 1024ull * 1024ull, 64ull * 1024ull * 1024ull,
         storage);
     engine::models::vibevoice::VibeVoiceDPMSolverScheduler sched(cfg);
     engine::models::vibevoice::VibeVoiceSpeechDiffusionInput input;
@@ -390,7 +399,7 @@ int cmd_dit(const std::string & w, const std::string & in_path, const std::strin
     const float sigma_max = f32_scalar(in, "sigma_max");
     const float rho = f32_scalar(in, "rho");
 
-    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    engine::core::ExecutionContext exec({ref_backend(), 0, threads});
     const auto storage = in.count("storage_type")
                              ? static_cast<engine::assets::TensorStorageType>(i64_scalar(in, "storage_type"))
                              : engine::assets::TensorStorageType::Native;
@@ -530,7 +539,7 @@ int cmd_sa3(const std::string & w, const std::string & in_path, const std::strin
     const char * sampler_name = i64_scalar(in, "sampler") == 1 ? "euler" : "pingpong";
     const uint64_t seed = static_cast<uint64_t>(i64_scalar(in, "seed"));
 
-    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    engine::core::ExecutionContext exec({ref_backend(), 0, threads});
     sa::StableAudioRfDitRuntime dit(exec, assets, engine::assets::TensorStorageType::Native);
     engine::sampling::TorchCudaSamplingPolicy policy;
     policy.multiprocessor_count = i64_scalar(in, "rng_sms");
@@ -575,7 +584,7 @@ int cmd_oobleck(const std::string & w, const std::string & in_path, const std::s
     const int64_t batch = i64_scalar(in, "batch");
     const int64_t tokens = i64_scalar(in, "latent_tokens");
     const auto latents = f32s(in, "latents");
-    engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+    engine::core::ExecutionContext exec({ref_backend(), 0, threads});
     sf::OobleckAutoencoderRuntime vae(exec, assets, engine::assets::TensorStorageType::Native);
     vae.prepare_decode(batch, tokens);
     std::vector<float> times, audio;
@@ -635,7 +644,7 @@ int cmd_vvdec(const std::string & w, const std::string & in_path, const std::str
     assets->config.acoustic_tokenizer = tok_config(in, "acoustic_");
     assets->config.semantic_tokenizer = tok_config(in, "semantic_");
     assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
-    vv::VibeVoiceTokenizerWeightsRuntime rt(assets, engine::core::BackendType::Cpu, 0, threads);
+    vv::VibeVoiceTokenizerWeightsRuntime rt(assets, ref_backend(), 0, threads);
     vv::VibeVoiceTokenizerLatents lat;
     lat.values = f32s(in, "latents");
     lat.dim = assets->config.acoustic_tokenizer.vae_dim;
@@ -699,7 +708,7 @@ int cmd_saocond(const std::string & w, const std::string & in_path, const std::s
         sa::StableAudioConditioningBatch b;
         b.prompt_tokens = tokens(ids, mask);
         b.normalized_seconds = seconds;
-        engine::core::ExecutionContext exec({engine::core::BackendType::Cpu, 0, threads});
+        engine::core::ExecutionContext exec({ref_backend(), 0, threads});
         sf::FoundationConditionerRuntime rt(exec, assets, engine::assets::TensorStorageType::Native, batch);
         rt.prepare();
         const double t0 = now_ms();
@@ -752,7 +761,7 @@ int cmd_vvlm(const std::string & w, const std::string & in_path, const std::stri
     c.rope_theta = f32_scalar(in, "rope_theta");
     c.tie_word_embeddings = true;
     assets->model_weights = std::make_shared<BundleTensorSource>(read_bundle(w));
-    vv::VibeVoiceDecoderWeightsRuntime lm(assets, engine::core::BackendType::Cpu, 0, threads);
+    vv::VibeVoiceDecoderWeightsRuntime lm(assets, ref_backend(), 0, threads);
     const int64_t prefill = i64_scalar(in, "prefill");
     std::vector<int32_t> ids;
     for (const int64_t v : i64s(in, "prefill_ids")) ids.push_back(static_cast<int32_t>(v));

@@ -62,9 +62,16 @@ def dropin_binary() -> Optional[str]:
     return path if os.path.exists(path) else None
 
 
+def cuda_binary() -> Optional[str]:
+    """The harness built with the vendored ggml-cuda backend for sm_100a (oracle/ref/Makefile VARIANT=cuda): the
+    reference's own GPU code path, run with B2D_REF_BACKEND=cuda as a timing comparison point."""
+    path = os.path.join(REF_DIR, "b2d_ref_cuda")
+    return path if os.path.exists(path) else None
+
+
 def run(cmd: str, inputs: Dict[str, B.Tensor], weights: Optional[Dict[str, B.Tensor]] = None,
         threads: int = 0, reps: int = 1, weights_path: Optional[str] = None, timeout: float = 3600,
-        exe: Optional[str] = None) -> Dict[str, B.Tensor]:
+        exe: Optional[str] = None, env: Optional[Dict[str, str]] = None) -> Dict[str, B.Tensor]:
     exe = exe or binary()
     if exe is None:
         raise RuntimeError("reference CPU build not found under oracle/_ref (run oracle/ref/Makefile)")
@@ -82,7 +89,8 @@ def run(cmd: str, inputs: Dict[str, B.Tensor], weights: Optional[Dict[str, B.Ten
                 args.append(str(reps))
         else:
             args += [inp, out]
-        proc = subprocess.run(args, capture_output=True, text=True, timeout=timeout)
+        proc = subprocess.run(args, capture_output=True, text=True, timeout=timeout,
+                              env=None if env is None else {**os.environ, **env})
         if proc.returncode != 0:
             raise RuntimeError("reference harness failed (%d): %s" % (proc.returncode, proc.stderr[-2000:]))
         return B.read(out)
