@@ -583,7 +583,8 @@ StreamPlan stream_plan(b2d_ctx* ctx, bool q8, int epi, int64_t N, int64_t K) {
 
 template <int BN, int WF, int EPI, typename CT>
 void launch_stream_t(const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* q, const __half* d, int64_t M,
-                     int64_t N, int64_t K, int split, const EpiParams& ep, cudaStream_t st) {
+                     int64_t N, int64_t K, int split, const EpiParams& ep, cudaStream_t st, const DevBuf* pf0,
+                     const DevBuf* pf1) {
     using S = StreamShape<BN, WF>;
     set_smem_limit(gemm_stream_kernel<BN, WF, EPI, CT>, int(S::SMEM_BYTES));
     StreamArgs a;
@@ -593,6 +594,12 @@ void launch_stream_t(const CUtensorMap& ta, const CUtensorMap& tb, const int8_t*
     a.k_blocks = int(K / 64);
     a.q8 = q;
     a.q8d = d;
+    const DevBuf* pf[2] = {pf0, pf1};
+    for (int r = 0; r < 2; ++r)
+        if (pf[r] && pf[r]->p) {
+            a.pf[r] = static_cast<const uint8_t*>(pf[r]->p);  // cudaMalloc base: 256-byte aligned
+            a.pf_bytes[r] = pf[r]->bytes;
+        }
     launch_k(gemm_stream_kernel<BN, WF, EPI, CT>, dim3(unsigned((N / BN) * split)), dim3(S::THREADS), S::SMEM_BYTES, st,
              split, ta, tb, a, ep);
 }
@@ -601,7 +608,8 @@ void launch_stream_t(const CUtensorMap& ta, const CUtensorMap& tb, const int8_t*
 // through `tb` (box rows = plan.bn) or Q8_0 planes (q, d).  Outputs need 16-byte aligned rows.
 template <typename CT>
 void launch_stream(StreamPlan plan, int epi, const CUtensorMap& ta, const CUtensorMap& tb, const int8_t* q,
-                   const __half* d, int64_t M, int64_t N, int64_t K, const EpiParams& ep, cudaStream_t st) {
+                   const __half* d, int64_t M, int64_t N, int64_t K, const EpiParams& ep, cudaStream_t st,
+                   const DevBuf* pf0 = nullptr, const DevBuf* pf1 = nullptr) {
     if (M > 128 || M <= 0) fail(B2D_EINVAL, "weight-streaming GEMM takes 1..128 rows (got %lld)", (long long)M);
     const int bn = plan.bn;
     if (bn == 0 || N % bn || K % 64 || plan.split < 1 || plan.split > K / 64)
@@ -611,8 +619,8 @@ void launch_stream(StreamPlan plan, int epi, const CUtensorMap& ta, const CUtens
     const bool wq = q != nullptr;
 #define B2D_S(BNv, EPIv)                                                                                     \
     if (bn == BNv && epi == EPIv) {                                                                          \
-        if (wq) launch_stream_t<BNv, WF_Q8, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st);            \
-        else launch_stream_t<BNv, WF_16, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st);               \
+        if (wq) launch_stream_t<BNv, WF_Q8, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st, pf0, pf1);  \
+        else launch_stream_t<BNv, WF_16, EPIv, CT>(ta, tb, q, d, M, N, K, plan.split, ep, st, pf0, pf1);     \
         return;                                                                                              \
     }
     B2D_S(256, EPI_F32) B2D_S(256, EPI_SWIGLU) B2D_S(256, EPI_RESID) B2D_S(256, EPI_CT)
@@ -843,9 +851,18 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
     // Up to 128 rows the per-step projections stream their weights (HBM-bound); above, tensor-bound tiles.
     const bool stream = R <= 128 && m.NADA % 256 == 0 && H % 256 == 0 && (2 * F) % 256 == 0 && m.NADA % 4 == 0;
     const bool q8s = stream && m.q8;
+    // Each streamed projection hints the next one's weights into L2 (gate/up of layer l after adaLN or the
+    // down projection of layer l - 1; down of layer l after gate/up of layer l).
+    const auto gu_pf = [&](int64_t l, int r) -> const DevBuf* {
+        if (l >= L) return nullptr;
+        return q8s ? (r == 0 ? &m.q_gu[size_t(l)] : &m.d_gu[size_t(l)]) : (r == 0 ? &m.w_gu[size_t(l)] : nullptr);
+    };
+    const auto down_pf = [&](int64_t l, int r) -> const DevBuf* {
+        return q8s ? (r == 0 ? &m.q_down[size_t(l)] : &m.d_down[size_t(l)]) : (r == 0 ? &m.w_down[size_t(l)] : nullptr);
+    };
     if (stream)
         launch_stream<CT>(ws.plan_ada, EPI_F32, ws.tm_sc, ws.tm_ada_s, q8s ? m.q_ada.as<int8_t>() : nullptr,
-                          q8s ? m.d_ada.as<__half>() : nullptr, R, m.NADA, H, ep, st);
+                          q8s ? m.d_ada.as<__half>() : nullptr, R, m.NADA, H, ep, st, gu_pf(0, 0), gu_pf(0, 1));
     else
         launch_gemm<CT>(256, EPI_F32, ws.tm_sc, m.tm_ada, R, m.NADA, H, ep, sms, st);
     const float* ada = ws.ada.as<float>();
@@ -861,7 +878,8 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         if (stream)
             launch_stream<CT>(ws.plan_gu, EPI_SWIGLU, ws.tm_h, q8s ? ws.tm_ada_s : ws.tm_gu_s[size_t(l)],
                               q8s ? m.q_gu[size_t(l)].as<int8_t>() : nullptr,
-                              q8s ? m.d_gu[size_t(l)].as<__half>() : nullptr, R, 2 * F, H, ep, st);
+                              q8s ? m.d_gu[size_t(l)].as<__half>() : nullptr, R, 2 * F, H, ep, st, down_pf(l, 0),
+                              down_pf(l, 1));
         else
             launch_gemm_pair<CT>(EPI_SWIGLU, ws.tm_h, m.tm_gu128[size_t(l)], R, 2 * F, H, ep, sms, st);
         ep = EpiParams{};
@@ -882,7 +900,8 @@ void head_forward(b2d_ctx* ctx, HeadModel& m, HeadWorkspace& ws, int temb_row, c
         if (stream)
             launch_stream<CT>(ws.plan_down, EPI_RESID, ws.tm_ffn, q8s ? ws.tm_ada_s : ws.tm_down_s[size_t(l)],
                               q8s ? m.q_down[size_t(l)].as<int8_t>() : nullptr,
-                              q8s ? m.d_down[size_t(l)].as<__half>() : nullptr, R, H, F, ep, st);
+                              q8s ? m.d_down[size_t(l)].as<__half>() : nullptr, R, H, F, ep, st, gu_pf(l + 1, 0),
+                              gu_pf(l + 1, 1));
         else if (use_pair)
             launch_gemm_pair<CT>(EPI_RESID, ws.tm_ffn, m.tm_down128[size_t(l)], R, H, F, ep, sms, st, 256);
         else if (use192)

@@ -59,7 +59,27 @@ struct StreamArgs {
     int k_blocks = 0;
     const int8_t* q8 = nullptr;   // WF_Q8: quants [K/64][N][64]
     const __half* q8d = nullptr;  // WF_Q8: scales [K/64][N][2]
+    // Up to two ranges the NEXT projection streams (its weights; Q8_0: quants and scales), hinted into L2 once
+    // this kernel has issued all of its own loads: HBM keeps streaming through this kernel's tail (TMEM drain,
+    // cluster reduction, epilogue) and the next kernel's launch and pipeline fill.  Each CTA takes an equal
+    // 16-byte-aligned share.  Values are unaffected: a prefetch only warms L2.
+    const uint8_t* pf[2] = {nullptr, nullptr};
+    uint64_t pf_bytes[2] = {0, 0};
 };
+
+// This CTA's share of the L2 prefetch ranges, in pieces of at most 64 KB.
+__device__ __forceinline__ void stream_prefetch_next(const StreamArgs& sa) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (sa.pf[r] == nullptr || sa.pf_bytes[r] < 16) continue;
+        const uint64_t units = sa.pf_bytes[r] >> 4;  // whole 16-byte units (a tail below 16 bytes is left out)
+        const uint64_t u0 = units * blockIdx.x / gridDim.x, u1 = units * (blockIdx.x + 1) / gridDim.x;
+        for (uint64_t u = u0; u < u1; u += 4096) {
+            const uint64_t n = u1 - u < 4096 ? u1 - u : 4096;
+            bulk_prefetch_l2(sa.pf[r] + (u << 4), uint32_t(n << 4));
+        }
+    }
+}
 
 // Epilogue of 4 consecutive output columns [col, col + 4) of one row (col within the weight rows, n0 = the
 // tile's first).  EPI_SWIGLU: v = gate sums, u = the matching linear-half sums (128 columns further);
@@ -187,6 +207,7 @@ __global__ void __launch_bounds__(StreamShape<BN, WF>::THREADS, 1)
                     bulk_load(rb + S::Q_BYTES, sa.q8d + blk * 2, S::D_BYTES, &rfull[r]);
                 }
             }
+            stream_prefetch_next(sa);
         }
     } else if (warp == 1) {
         if (lane == 0) {

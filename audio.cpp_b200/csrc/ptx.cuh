@@ -115,6 +115,13 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
         : "memory");
 }
 
+// L2 prefetch of a global range (no shared memory, no completion to wait for): address 16-byte aligned, bytes
+// a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
 // 2-D tiled store from shared memory (bulk group); rows / columns outside the map's extent are not written.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x, int32_t y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
