@@ -33,7 +33,7 @@ EXPORTED = ["b2d_create", "b2d_destroy", "b2d_last_error", "b2d_sync", "b2d_vers
             "b2d_sa3_load", "b2d_sa3_sample", "b2d_sa3_sample_device", "b2d_oobleck_load", "b2d_oobleck_decode",
             "b2d_oobleck_decode_device", "b2d_vvdec_load", "b2d_vvdec_decode", "b2d_vvdec_decode_device",
             "b2d_saocond_load", "b2d_saocond_encode", "b2d_saocond_encode_device",
-            "b2d_vvlm_load", "b2d_vvlm_prefill", "b2d_vvlm_step"]
+            "b2d_vvlm_load", "b2d_vvlm_prefill", "b2d_vvlm_step", "b2d_vvlm_prefill_device", "b2d_vvlm_step_device"]
 
 
 class B2DError(RuntimeError):
@@ -175,6 +175,8 @@ def lib() -> C.CDLL:
         L.b2d_vvlm_load.argtypes = [P, C.POINTER(VvlmConfig), C.POINTER(TensorView), I32]
         L.b2d_vvlm_prefill.argtypes = [P, P, I64, P, P, P]
         L.b2d_vvlm_step.argtypes = [P, P, P, P, P]
+        L.b2d_vvlm_prefill_device.argtypes = [P, P, I64, P, P, P]
+        L.b2d_vvlm_step_device.argtypes = [P, P, P, P, P]
         _lib = L
     return _lib
 
@@ -563,6 +565,17 @@ class VibeVoiceLanguageModel:
         hidden = np.empty(self.cfg.hidden, np.float32)
         self.ctx.check(lib().b2d_vvlm_step(self.ctx.handle, _ptr(e), _ptr(logits), _ptr(hidden), C.c_void_p(stream)))
         return logits, hidden
+
+    def prefill_device(self, embeddings, logits, hidden, stream: int = 0):
+        """Device embeddings [steps, hidden] -> device logits [vocab] and hidden [hidden], asynchronous on `stream`
+        (torch CUDA tensors, fp32, contiguous)."""
+        self.ctx.check(lib().b2d_vvlm_prefill_device(self.ctx.handle, _ptr(embeddings), embeddings.shape[0],
+                                                     _ptr(logits), _ptr(hidden), C.c_void_p(stream)))
+
+    def step_device(self, embedding, logits, hidden, stream: int = 0):
+        """One cached position from a device embedding [hidden]; outputs as prefill_device."""
+        self.ctx.check(lib().b2d_vvlm_step_device(self.ctx.handle, _ptr(embedding), _ptr(logits), _ptr(hidden),
+                                                  C.c_void_p(stream)))
 
 
 class VibeVoiceDiffusionHead:

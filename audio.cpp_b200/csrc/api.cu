@@ -1071,6 +1071,11 @@ void head_predict(b2d_ctx* ctx, const float* noisy, int64_t frames, float timest
 #include "t5_runtime.inc"
 #include "lm_runtime.inc"
 
+// Forgets the decoder's cached positions (after a device-side failure of an asynchronous forward).
+void lm_invalidate(b2d_ctx* ctx) {
+    if (ctx && ctx->lm) ctx->lm->pos = 0;
+}
+
 }  // namespace
 
 // =================================================================== C ABI
@@ -1150,7 +1155,15 @@ b2d_status b2d_selftest_wait_timeout(b2d_ctx* ctx, uint32_t polls, void* stream)
 }
 
 b2d_status b2d_sync(b2d_ctx* ctx, void* stream) {
-    return guarded(ctx, [&] { check_status_word(ctx, static_cast<cudaStream_t>(stream)); });
+    return guarded(ctx, [&] {
+        try {
+            check_status_word(ctx, static_cast<cudaStream_t>(stream));
+        } catch (...) {
+            // an asynchronous decoder forward may have written garbage cache rows: the next call must prefill
+            lm_invalidate(ctx);
+            throw;
+        }
+    });
 }
 
 b2d_status b2d_vv_head_load(b2d_ctx* ctx, const b2d_vv_head_config* config, const b2d_tensor_view* tensors,
@@ -1634,6 +1647,24 @@ b2d_status b2d_vvlm_step(b2d_ctx* ctx, const float* embedding, float* logits, fl
         if (!ctx->lm) fail(B2D_ESTATE, "VibeVoice decoder weights are not loaded");
         if (ctx->lm->pos == 0) fail(B2D_ESTATE, "VibeVoice decoder cached step before prefill");
         lm_forward<__half>(ctx, embedding, 1, logits, last_hidden, static_cast<cudaStream_t>(stream));
+    });
+}
+
+b2d_status b2d_vvlm_prefill_device(b2d_ctx* ctx, const float* embeddings, int64_t steps, float* logits,
+                                   float* last_hidden, void* stream) {
+    return guarded(ctx, [&] {
+        if (!ctx->lm) fail(B2D_ESTATE, "VibeVoice decoder weights are not loaded");
+        ctx->lm->pos = 0;
+        lm_forward<__half>(ctx, embeddings, steps, logits, last_hidden, static_cast<cudaStream_t>(stream), true);
+    });
+}
+
+b2d_status b2d_vvlm_step_device(b2d_ctx* ctx, const float* embedding, float* logits, float* last_hidden,
+                                void* stream) {
+    return guarded(ctx, [&] {
+        if (!ctx->lm) fail(B2D_ESTATE, "VibeVoice decoder weights are not loaded");
+        if (ctx->lm->pos == 0) fail(B2D_ESTATE, "VibeVoice decoder cached step before prefill");
+        lm_forward<__half>(ctx, embedding, 1, logits, last_hidden, static_cast<cudaStream_t>(stream), true);
     });
 }
 

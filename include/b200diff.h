@@ -404,6 +404,15 @@ B2D_API b2d_status b2d_vvlm_prefill(b2d_ctx* ctx, const float* embeddings, int64
 B2D_API b2d_status b2d_vvlm_step(b2d_ctx* ctx, const float* embedding, float* logits, float* last_hidden,
                                  void* stream);
 
+/* b2d_vvlm_prefill / b2d_vvlm_step with device buffers (embeddings in, logits and last_hidden out), asynchronous
+ * on `stream`: the last hidden state can feed b2d_vv_sample_device as a condition without a host round trip (the
+ * generator's per-token hand-off, src/models/vibevoice/generator.cpp:590-608).  Check b2d_sync for device-side
+ * status; a failure reported there also clears the decoder's cache position (prefill again). */
+B2D_API b2d_status b2d_vvlm_prefill_device(b2d_ctx* ctx, const float* embeddings, int64_t steps, float* logits,
+                                           float* last_hidden, void* stream);
+B2D_API b2d_status b2d_vvlm_step_device(b2d_ctx* ctx, const float* embedding, float* logits, float* last_hidden,
+                                        void* stream);
+
 /* ------------------------------------------------------ kernel-level entries */
 /* Q8_0 rows (GGUF bytes, dev) -> fp32 (dev), bit-exact with dequantize_row_q8_0
  * (external/ggml/src/ggml-quants.c:491-505). */

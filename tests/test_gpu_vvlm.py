@@ -34,3 +34,32 @@ def test_vvlm_prefill_and_steps_match_reference(b2d, ctx, name):
     err_h = rel_l2(np.stack(hidden), g["last_hidden"].array())
     print("%s: logits %.3g, hidden %.3g" % (name, err_l, err_h))
     assert err_l < 1e-2 and err_h < 1e-2
+
+
+def test_vvlm_device_buffers_match_host_buffers(b2d, ctx):
+    """prefill_device / step_device (device embeddings in, device logits and hidden out, no host round trip) give
+    the host entry points' values."""
+    import torch
+    cfg = synth.VVLM_CONFIGS["vvlm_tiny"]
+    w, inp = synth.vvlm_weights(cfg), synth.vvlm_inputs(cfg)
+    lm = b2d.VibeVoiceLanguageModel(ctx, cfg.hidden, cfg.intermediate, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                    cfg.layers, cfg.vocab, cfg.max_positions, cfg.eps, cfg.rope_theta,
+                                    weights=weight_specs(w))
+    table = w["model.language_model.embed_tokens.weight"].array()
+    host = [lm.prefill(table[inp["prefill_ids"].array()])]
+    host += [lm.step(table[i]) for i in inp["step_ids"].array()]
+    dev = torch.device("cuda", ctx.device)
+    lg = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+    hd = torch.empty(cfg.hidden, dtype=torch.float32, device=dev)
+    got = []
+    e = torch.from_numpy(np.ascontiguousarray(table[inp["prefill_ids"].array()], np.float32)).to(dev)
+    lm.prefill_device(e, lg, hd)
+    ctx.sync()
+    got.append((lg.cpu().numpy(), hd.cpu().numpy()))
+    for i in inp["step_ids"].array():
+        e = torch.from_numpy(np.ascontiguousarray(table[i], np.float32)).to(dev)
+        lm.step_device(e, lg, hd)
+        ctx.sync()
+        got.append((lg.cpu().numpy(), hd.cpu().numpy()))
+    for (hl, hh), (gl, gh) in zip(host, got):
+        assert rel_l2(gl, hl) < 1e-6 and rel_l2(gh, hh) < 1e-6
