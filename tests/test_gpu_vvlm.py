@@ -63,3 +63,44 @@ def test_vvlm_device_buffers_match_host_buffers(b2d, ctx):
         got.append((lg.cpu().numpy(), hd.cpu().numpy()))
     for (hl, hh), (gl, gh) in zip(host, got):
         assert rel_l2(gl, hl) < 1e-6 and rel_l2(gh, hh) < 1e-6
+
+
+def test_lm_hidden_state_feeds_the_head_on_device(b2d, ctx):
+    """The generator's per-token hand-off with every buffer on the GPU: the LM's cached step writes its last hidden
+    state to device memory and the diffusion head samples that token's latent from it as the positive condition
+    (src/models/vibevoice/generator.cpp:590-608).  Same latents as the host-buffer chain."""
+    import torch
+    lcfg = synth.VVLmConfig(hidden=256, intermediate=512, heads=4, kv_heads=2, head_dim=64, layers=1, prefill=5,
+                            steps=3, wseed=51, seed=52)
+    hcfg = synth.HeadConfig(hidden=256, wtype=synth.F16, frames=1, steps=5)
+    w, inp = synth.vvlm_weights(lcfg), synth.vvlm_inputs(lcfg)
+    lm = b2d.VibeVoiceLanguageModel(ctx, lcfg.hidden, lcfg.intermediate, lcfg.heads, lcfg.kv_heads, lcfg.head_dim,
+                                    lcfg.layers, lcfg.vocab, lcfg.max_positions, lcfg.eps, lcfg.rope_theta,
+                                    weights=weight_specs(w))
+    head = b2d.VibeVoiceDiffusionHead(ctx, hcfg.hidden, hcfg.layers, hcfg.ffn_ratio,
+                                      weights=weight_specs(synth.head_weights(hcfg)))
+    table = w["model.language_model.embed_tokens.weight"].array()
+    ids = inp["step_ids"].array()
+    neg = np.zeros((1, hcfg.hidden), np.float32)
+    x0 = np.random.default_rng(7).standard_normal((len(ids), 2, 64)).astype(np.float32)
+    # host buffers
+    lm.prefill(table[inp["prefill_ids"].array()])
+    host = []
+    for j, i in enumerate(ids):
+        _, hd = lm.step(table[i])
+        host.append(head.sample(hd[None, :].copy(), neg, x0[j], hcfg.steps, hcfg.cfg))
+    # device buffers
+    dev = torch.device("cuda", ctx.device)
+    lg = torch.empty(lcfg.vocab, dtype=torch.float32, device=dev)
+    hd = torch.empty(1, lcfg.hidden, dtype=torch.float32, device=dev)
+    neg_d = torch.zeros(1, hcfg.hidden, dtype=torch.float32, device=dev)
+    x0_d = torch.from_numpy(x0).to(dev)
+    out = torch.empty(len(ids), 1, 64, dtype=torch.float32, device=dev)
+    lm.prefill_device(torch.from_numpy(np.ascontiguousarray(table[inp["prefill_ids"].array()])).to(dev), lg, hd)
+    for j, i in enumerate(ids):
+        lm.step_device(torch.from_numpy(np.ascontiguousarray(table[i])).to(dev), lg, hd)
+        head.sample_device(hd, neg_d, x0_d[j], hcfg.steps, hcfg.cfg, out[j])
+    ctx.sync()
+    got = out.cpu().numpy()
+    for j in range(len(ids)):
+        assert rel_l2(got[j], host[j]) < 1e-6, j
