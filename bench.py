@@ -1,6 +1,6 @@
 """Benchmark of the diffusion denoising hot path on B200.
 
-Workload: VibeVoice-1.5B diffusion head, Q8_0 weights
+Workload (the headline configuration, C2): VibeVoice-1.5B diffusion head, Q8_0 weights
 (random N(0, 0.02), seeded), 1024 frames per call with CFG pairs (2048 head
 rows), conditions N(0,1) [1024, 1536], null condition zeros, x_T N(0,1),
 10-step DPM-Solver++(2M), CFG 1.3.  One "step" = one whole sampling call

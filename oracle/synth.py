@@ -94,7 +94,7 @@ class HeadConfig:
 
 
 HEAD_CONFIGS = {
-    # BASELINE configs (C1, C2, C5)
+    # the benchmarked head configurations (C1, C2, C5)
     "vv15_f16_64": HeadConfig(wtype=F16, frames=64),
     "vv15_q8_1024": HeadConfig(wtype=Q8_0, frames=1024),
     "vv7_q8_8192": HeadConfig(hidden=3584, wtype=Q8_0, frames=8192),
@@ -191,7 +191,7 @@ class DitConfig:
 DIT_CONFIGS = {
     "sao_bf16_1x1024": DitConfig(),
     "sao_q8_16x1024": DitConfig(wtype=Q8_0, batch=16, prompt_seeds=tuple(range(16))),
-    # full-size parity cases (BASELINE C3/C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
+    # full-size parity cases (the C3 / C4 shapes, 2 DPM++ steps so the CPU reference finishes in about a minute)
     "sao_bf16_1x1024_2steps": DitConfig(steps=2),
     # C3 at 10 DPM++ 2M steps: the multistep (second-order) update at full size, with the reference's latents
     # (BF16 and F32 weights) and the fp32-activation restatement
