@@ -30,6 +30,7 @@ METRIC = "latent frames/sec (VibeVoice diffusion head)"
 UNIT = "frames/s"
 T_START = time.time()
 WORKLOAD = "vv15_q8_1024"
+C1_WORKLOAD = "vv15_f16_64"
 
 
 def load_package():
@@ -197,7 +198,7 @@ def bench_reference(args):
 
 def bench_ggml_cuda(args):
     """GPU comparison point: the reference's own ggml-cuda backend (oracle/ref/Makefile VARIANT=cuda, compiled for
-    sm_100a from the vendored sources) running the reference's stock sampling entry points on the C2 head workload
+    sm_100a from the vendored sources) running the reference's stock sampling entry points on the C2 and C1 head workloads
     and the C3 DiT workload, timed by the harness around each whole sampling call (host inputs in, host latents
     out, the runtime and its device weights built before the first call).  One JSON line, rank 0 only."""
     world, rank, _ = dist_setup()
@@ -220,17 +221,18 @@ def bench_ggml_cuda(args):
         return float(np.linalg.norm(lat.astype(np.float64).ravel() - ref) / np.linalg.norm(ref))
 
     line = {"impl": "reference-ggml-cuda", "n_gpus": 1, "backend": "audio.cpp vendored ggml-cuda, sm_100a"}
-    cfg = synth.HEAD_CONFIGS[WORKLOAD]
     reps = args.warmup + args.steps
-    try:
-        o = ref_runner.run("vv", synth.head_inputs(cfg), synth.head_weights(cfg), reps=reps, exe=exe,
-                           env=env, timeout=900)
-        ms = float(np.median(np.asarray(o["wall_ms"].data[args.warmup:], np.float64)))
-        line["head"] = {"workload": WORKLOAD, "metric": METRIC, "value": round(cfg.frames / (ms / 1e3), 1),
-                        "unit": UNIT, "ms_per_call": round(ms, 3), "calls_timed": args.steps,
-                        "rel_l2_vs_reference_cpu": rel_to_golden("head_" + WORKLOAD, o["latents"].array())}
-    except Exception as e:  # the reference's failure is reported, not raised
-        line["head"] = {"unavailable": str(e).splitlines()[0][:300]}
+    for key, workload in (("head", WORKLOAD), ("c1", C1_WORKLOAD)):
+        cfg = synth.HEAD_CONFIGS[workload]
+        try:
+            o = ref_runner.run("vv", synth.head_inputs(cfg), synth.head_weights(cfg), reps=reps, exe=exe,
+                               env=env, timeout=900)
+            ms = float(np.median(np.asarray(o["wall_ms"].data[args.warmup:], np.float64)))
+            line[key] = {"workload": workload, "metric": METRIC, "value": round(cfg.frames / (ms / 1e3), 1),
+                         "unit": UNIT, "ms_per_call": round(ms, 3), "calls_timed": args.steps,
+                         "rel_l2_vs_reference_cpu": rel_to_golden("head_" + workload, o["latents"].array())}
+        except Exception as e:  # the reference's failure is reported, not raised
+            line[key] = {"unavailable": str(e).splitlines()[0][:300]}
     dcfg = synth.DIT_CONFIGS[DIT_WORKLOAD]
     try:
         calls = max(1, args.dit_steps)
@@ -541,7 +543,7 @@ def bench_c1(args, torch, b2d, ctx, world, rank, timed, peaks):
     """C1: VibeVoice-1.5B head, F16 weights, 64 frames (128 head rows), 10 steps, CFG 1.3.  Weight streaming:
     judged on weight bytes per call against the measured HBM copy bandwidth.  Per rank its own 64 frames."""
     from oracle import synth
-    cfg = synth.HEAD_CONFIGS["vv15_f16_64"]
+    cfg = synth.HEAD_CONFIGS[C1_WORKLOAD]
     w = node_shared(synth.head_weights, cfg)
     inp = synth.head_inputs(synth.HeadConfig(**{**cfg.__dict__, "cseed": 1 + 100 * rank, "xseed": 2 + 100 * rank}))
     head = b2d.VibeVoiceDiffusionHead(ctx, cfg.hidden, cfg.layers, cfg.ffn_ratio,
@@ -565,7 +567,7 @@ def bench_c1(args, torch, b2d, ctx, world, rank, timed, peaks):
     res = {"metric": "latent frames/sec (VibeVoice diffusion head, C1 weight streaming)",
            "value": round(frames / (ms / 1e3), 1), "unit": "frames/s", "ms_per_call": round(ms, 4),
            "timed_calls": 20, "warmup_calls": 5,
-           "config": {"workload": "vv15_f16_64", "model": "VibeVoice-1.5B diffusion head (random-init)",
+           "config": {"workload": C1_WORKLOAD, "model": "VibeVoice-1.5B diffusion head (random-init)",
                       "weights": "f16", "frames_per_rank": cfg.frames, "head_rows_per_rank": 2 * cfg.frames,
                       "dpm_steps": cfg.steps, "cfg_scale": cfg.cfg, "n_gpus": world},
            "dtype": "f16 tensor-core operands, fp32 accumulate",
