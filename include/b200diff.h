@@ -92,7 +92,8 @@ B2D_API b2d_status b2d_create(int device, b2d_ctx** out);
 B2D_API void b2d_destroy(b2d_ctx* ctx);
 B2D_API const char* b2d_last_error(const b2d_ctx* ctx);
 /* Waits for the context's outstanding work and reports any device-side status
- * (non-finite latent, expired wait) raised since the last check. */
+ * (non-finite latent, expired wait) raised since the last check.  When it reports one, the context's VibeVoice
+ * decoder cache position is also cleared (its next call must be a prefill). */
 B2D_API b2d_status b2d_sync(b2d_ctx* ctx, void* stream);
 /* Version string of the library build. */
 B2D_API const char* b2d_version(void);
