@@ -81,7 +81,7 @@ def head_storage_golden(name: str, storage: int, tag: str) -> None:
 
 def sched_golden() -> None:
     rng = np.random.default_rng(7)
-    for steps in (1, 2, 10, 20):
+    for steps in (1, 2, 10, 20, 3, 5, 50, 100):
         n = 96
         sample = rng.standard_normal(n).astype(np.float32)
         outs = rng.standard_normal((steps, n)).astype(np.float32)

@@ -35,7 +35,7 @@ def test_create_without_gpu_fails_cleanly(b2d):
         b2d.Context(0)
 
 
-@pytest.mark.parametrize("steps", [1, 2, 10, 20])
+@pytest.mark.parametrize("steps", [1, 2, 3, 5, 10, 20, 50, 100])
 def test_schedule_matches_reference(b2d, steps):
     g = golden("sched_%d" % steps)
     sched = b2d.vv_schedule(1000, steps)
